@@ -1,0 +1,379 @@
+#!/usr/bin/env python
+"""Decode throughput of the 7B-shaped 4-bit Llama decoder on B200.
+
+Workload (one "step" = one decode step of every sequence in the batch):
+32 layers, d_model 4096, 32 heads x 128, SwiGLU 11008, RMSNorm, RoPE,
+vocab 32000, every linear Q4_0 (block 32, f16 scales) from N(0, 0.02)
+synthetic weights, a 2048-token random-id prompt per sequence, then decode
+steps at batch 32 (headline) and batch 1. KV cache bf16, paged.
+
+Prints one JSON line (rank 0). With torchrun (N > 1) every rank runs an
+independent replica on its own GPU; value is the sum over ranks, timed as the
+max over ranks. --impl reference times the CPU oracle port of the reference
+path (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tokens/s (7B-shape 4-bit) at 1/2/4/8 B200; dequant-GEMV HBM GB/s vs peak"
+FALLBACK_HBM_GBS = 6650.0
+CFG_7B = dict(vocab_size=32000, dim=4096, n_layers=32, n_heads=32, n_kv_heads=32, ffn_dim=11008)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="vortex", choices=["vortex", "reference"])
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--prompt-len", type=int, default=2048)
+    ap.add_argument("--e2e-steps", type=int, default=16)
+    ap.add_argument("--no-batch1", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-layers", type=int, default=1)
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------- helpers
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(gpus):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        rank = int(os.environ["RANK"])
+        local = int(os.environ.get("LOCAL_RANK", rank))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        return rank, ws, local
+    return 0, 1, 0
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, ws):
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- CPU baseline (oracle port)
+
+def cpu_layer_sample(n_threads: int, seed: int = 7):
+    """Time one Llama-style layer decode step for one token at context 2048 on
+    the CPU oracle (f64, dequantize-then-matvec per reference order) plus the
+    LM head, split across n_threads by output rows. Returns (seconds for one
+    token of the full 32-layer model, description)."""
+    import concurrent.futures as cf
+
+    import numpy as np
+
+    from oracle import oracle as O
+    rng = np.random.default_rng(seed)
+    d, f, V = CFG_7B["dim"], CFG_7B["ffn_dim"], CFG_7B["vocab_size"]
+    shapes = [(3 * d, d), (d, d), (2 * f, d), (d, f)]
+    mats = [(O.quantize_blocks(O.GGML_Q4_0, rng.normal(0, 0.02, n * k).astype(np.float32)), n, k) for n, k in shapes]
+    lm = (O.quantize_blocks(O.GGML_Q4_0, rng.normal(0, 0.02, V * d).astype(np.float32)), V, d)
+    bpr = lambda k: k // 32 * 18
+
+    def gemv_rows(args):
+        blocks, n, k, x, r0, r1 = args
+        O.gemv_blocks(O.GGML_Q4_0, blocks[r0 * bpr(k):r1 * bpr(k)], r1 - r0, k, x)
+
+    def gemv(pool, blocks, n, k):
+        x = rng.standard_normal((1, k))
+        step = (n + n_threads - 1) // n_threads
+        list(pool.map(gemv_rows, [(blocks, n, k, x, r, min(n, r + step)) for r in range(0, n, step)]))
+
+    ctx, hd, H = 2048, 128, 32
+    K = rng.standard_normal((ctx, hd))
+    Vv = rng.standard_normal((ctx, hd))
+    q = rng.standard_normal(hd)
+    with cf.ThreadPoolExecutor(max_workers=n_threads) as pool:
+        t0 = time.perf_counter()
+        for blocks, n, k in mats:
+            gemv(pool, blocks, n, k)
+        list(pool.map(lambda h: O.paged_attention(q, K, Vv, hd), range(H)))
+        t_layer = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        gemv(pool, *lm)
+        t_lm = time.perf_counter() - t0
+    per_token = CFG_7B["n_layers"] * t_layer + t_lm
+    return per_token, f"one layer (4 fused Q4_0 GEMVs + 32-head attention at ctx 2048) + LM head, batch 1, " \
+                      f"{n_threads} thread(s), extrapolated x32 layers"
+
+
+def run_reference(args, rank, ws):
+    if rank != 0:
+        return
+    n_threads = os.cpu_count() or 1
+    # warmup samples
+    for _ in range(max(0, min(args.warmup, 1))):
+        cpu_layer_sample(n_threads)
+    times = []
+    t_all = time.perf_counter()
+    steps = max(1, min(args.steps, 4))
+    for _ in range(steps):
+        per_token, desc = cpu_layer_sample(n_threads)
+        times.append(per_token)
+    per_token = statistics.median(times)
+    value = 1.0 / per_token
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": per_token * 1e3 * args.batch,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": "7B-shape Llama decoder decode, Q4_0 linears, CPU oracle port of the reference "
+                                   "path (sampled layer, extrapolated)", "global_batch": args.batch,
+                       "seq_len": args.prompt_len, "parallelism": "cpu threads"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": n_threads, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "wall_s": time.perf_counter() - t_all}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU arm
+
+def time_attention(dec, seq_ids, hd_heads, reps=20):
+    """Average duration of the decode attention kernel (layer 0) on the
+    decoder's cache at its current lengths, CUDA events on the launch stream."""
+    import ctypes
+
+    import numpy as np
+    import torch
+
+    from vortex_b200 import _native as N
+    kv = ctypes.c_void_p()
+    N.check(N.lib().vxb_decoder_kv(dec.ptr, ctypes.byref(kv)))
+    H, hd = hd_heads
+    n = len(seq_ids)
+    q = torch.randn(n, H, hd, device="cuda").bfloat16()
+    out = torch.empty_like(q)
+    ids = np.ascontiguousarray(seq_ids, dtype=np.int64)
+    s = torch.cuda.Stream()
+    L = N.lib()
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            N.check(L.vxb_decode_attention(kv, 0, n, ids.ctypes.data_as(ctypes.c_void_p), ctypes.c_void_p(q.data_ptr()),
+                                           H, ctypes.c_float(1.0 / hd ** 0.5), ctypes.c_void_p(out.data_ptr()), None,
+                                           ctypes.c_void_p(s.cuda_stream)))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(reps):
+            L.vxb_decode_attention(kv, 0, n, ids.ctypes.data_as(ctypes.c_void_p), ctypes.c_void_p(q.data_ptr()), H,
+                                   ctypes.c_float(1.0 / hd ** 0.5), ctypes.c_void_p(out.data_ptr()), None,
+                                   ctypes.c_void_p(s.cuda_stream))
+        e1.record(s)
+    torch.cuda.synchronize()
+    lens = []
+    for sid in seq_ids:
+        ln = ctypes.c_int64()
+        N.check(L.vxb_kv_seq_len(kv, 0, int(sid), ctypes.byref(ln)))
+        lens.append(ln.value)
+    return e0.elapsed_time(e1) / reps * 1e-3, lens
+
+
+def run_decode(dec, seq_ids, prompt, steps, warmup, ws, torch):
+    """Prefill token by token (untimed), warm up, then time `steps` decode
+    steps with CUDA events on the decoder's stream."""
+    import numpy as np
+    B = len(seq_ids)
+    tok = torch.from_numpy(prompt[:, 0].astype(np.int32)).cuda()
+    nxt = torch.empty(B, dtype=torch.int32, device="cuda")
+    for t in range(prompt.shape[1]):
+        tok.copy_(torch.from_numpy(prompt[:, t].astype(np.int32)))
+        dec.step_device(seq_ids, tok, nxt)
+    for _ in range(warmup):
+        tok.copy_(nxt)
+        dec.step_device(seq_ids, tok, nxt)
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        tok.copy_(nxt)
+        dec.step_device(seq_ids, tok, nxt)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(ws)
+    return e0.elapsed_time(e1) * 1e-3, nxt
+
+
+def main():
+    args = parse()
+    rank, ws, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        run_reference(args, rank, ws)
+        return
+    import numpy as np
+    import torch
+
+    from vortex_b200 import decoder as D
+
+    torch.cuda.set_device(local)
+    B = args.batch
+    max_seq = args.prompt_len + args.warmup + args.steps + args.e2e_steps + 8
+    t_setup = time.perf_counter()
+    dec = D.Decoder(max_batch=B, max_seq=max_seq, **CFG_7B)
+    dec.init_random(seed=1234, sigma=0.02)
+    rng = np.random.default_rng(2024 + rank)
+    prompt = rng.integers(0, CFG_7B["vocab_size"], size=(B, args.prompt_len))
+    seq_ids = list(range(B))
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    t_dev, nxt = run_decode(dec, seq_ids, prompt, args.steps, args.warmup, ws, torch)
+    clocks = sampler.stop()
+    t_max = max_over_ranks(t_dev, ws)
+    value = ws * B * args.steps / t_max
+
+    # end to end through the host-buffer C ABI call (tokens H2D, next tokens D2H)
+    host_tok = nxt.cpu().numpy().astype(np.int32)
+    barrier(ws)
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        host_tok = dec.step(seq_ids, host_tok)
+    t_e2e = max_over_ranks(time.perf_counter() - t0, ws)
+    e2e = ws * B * args.e2e_steps / t_e2e
+    h2d = B * 4 + CFG_7B["n_layers"] * B * 16 + B * 4
+    d2h = B * 4
+
+    # dominant kernel at this workload: decode attention (KV bytes >> weights)
+    hbm, peak_src = measured_peaks()
+    t_attn, lens = time_attention(dec, seq_ids, (CFG_7B["n_heads"], CFG_7B["dim"] // CFG_7B["n_heads"]))
+    hd = CFG_7B["dim"] // CFG_7B["n_heads"]
+    attn_bytes = sum(lens) * CFG_7B["n_kv_heads"] * hd * 2 * 2 + 2 * B * CFG_7B["dim"] * 2
+    achieved = attn_bytes / t_attn / 1e9
+
+    # batch 1 on a freed slot
+    b1 = None
+    if not args.no_batch1:
+        dec.free_seq(seq_ids[-1])
+        sid = [10_000]
+        t1, _ = run_decode(dec, sid, prompt[:1], args.steps, args.warmup, ws, torch)
+        b1 = max_over_ranks(t1, ws)
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        per_token, desc = cpu_layer_sample(1)
+        cpu = {"value": 1.0 / per_token, "unit": "tokens/s", "cores": 1, "kind": "port", "sample": desc}
+
+    launches_per_step = 1 + CFG_7B["n_layers"] * 10 + 3
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_max / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "7B-shape Llama decoder decode (32 layers, d4096, 32x128 heads, SwiGLU 11008, "
+                                   "vocab 32000, Q4_0 linears, bf16 paged KV), random weights N(0,0.02)",
+                       "global_batch": ws * B, "batch_per_gpu": B, "seq_len": args.prompt_len,
+                       "prompt_len": args.prompt_len, "decode_steps": args.steps,
+                       "parallelism": "replicas" if ws > 1 else "single",
+                       "l2": "inputs larger than L2 (3.7 GB weights + KV per step)"},
+            "batch1_tokens_per_s": (ws * args.steps / b1) if b1 else None,
+            "batch1_ms_per_step": (b1 / args.steps * 1e3) if b1 else None,
+            "roofline": {"kernel": "decode_attn_kernel (layer 0, batch %d)" % B, "bound": "hbm",
+                         "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "peak_source": peak_src, "traffic": None,
+                         "algorithmic_bytes": attn_bytes, "launch_us": t_attn * 1e6},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches_per_step * args.steps,
+            "setup_s": time.perf_counter() - t_setup,
+        }
+        print(json.dumps(line), flush=True)
+    dec.close()
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,221 @@
+/*
+ * vxb.h -- C ABI of vortex_b200, the B200 (sm_100a) implementation of the
+ * Vortex quantized-inference hot path.
+ *
+ * Conventions
+ *  - Every entry point returns an int status: VXB_OK (0) or a negative VXB_E*
+ *    code; none aborts or throws. vxb_last_error() gives the message, which
+ *    maps onto the reference's `Err(String)` results.
+ *  - Buffers are caller-owned. Pointers named d_* are device pointers (from
+ *    vxb_alloc, cudaMalloc or any allocator of the same device); h_* are host
+ *    pointers. `stream` is a cudaStream_t passed as void* (NULL = default).
+ *  - One context per device. A context is not shared between host threads
+ *    without external locking (the reference serialises its handle tables
+ *    with a Mutex; callers keep that discipline).
+ *  - bf16 / f16 values are passed as uint16_t bit patterns.
+ *
+ * Each declaration names the reference interface it replaces
+ * (MangoByteLabs/vortex, paths relative to that project).
+ */
+#ifndef VXB_H
+#define VXB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VXB_ABI_VERSION 1
+
+/* status codes */
+#define VXB_OK 0
+#define VXB_EINVAL (-1)      /* bad argument (shape, pointer, enum) */
+#define VXB_ECUDA (-2)       /* CUDA runtime error */
+#define VXB_ENOMEM (-3)      /* device or host allocation failed */
+#define VXB_ETIMEOUT (-4)    /* a bounded device-side wait ran out */
+#define VXB_EFORMAT (-5)     /* malformed GGUF data */
+#define VXB_ENOBLOCKS (-6)   /* KV cache out of blocks */
+#define VXB_EUNSUPPORTED (-7)/* valid request this build does not handle */
+#define VXB_ENCCL (-8)       /* NCCL error */
+
+/* weight block formats: the GGML type ids of gguf_loader.rs GGMLQuantType
+ * (src/gguf_loader.rs:61-75) */
+#define VXB_Q4_0 2
+#define VXB_Q8_0 8
+
+/* element types */
+#define VXB_F32 0
+#define VXB_BF16 1
+#define VXB_F16 2
+#define VXB_I8 3
+
+typedef struct vxb_ctx vxb_ctx;
+
+/* ------------------------------------------------------------------------ */
+/* Context and memory.                                                       */
+/* Replaces gpu_runtime::CpuRuntime alloc/free/copy                          */
+/* (src/gpu_runtime.rs:297-348) and cuda_available (src/gpu_runtime.rs:654). */
+/* ------------------------------------------------------------------------ */
+int vxb_abi_version(void);
+int vxb_device_count(int *count);
+int vxb_init(int device, vxb_ctx **out);
+int vxb_destroy(vxb_ctx *ctx);
+const char *vxb_last_error(const vxb_ctx *ctx); /* ctx may be NULL: last global error */
+int vxb_alloc(vxb_ctx *ctx, size_t bytes, void **d_out);
+int vxb_free(vxb_ctx *ctx, void *d_ptr);
+int vxb_memcpy_h2d(vxb_ctx *ctx, void *d_dst, const void *h_src, size_t bytes, void *stream);
+int vxb_memcpy_d2h(vxb_ctx *ctx, void *h_dst, const void *d_src, size_t bytes, void *stream);
+int vxb_memset(vxb_ctx *ctx, void *d_dst, int value, size_t bytes, void *stream);
+int vxb_sync(vxb_ctx *ctx, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Weight blocks (host codec).                                               */
+/* The storage format is the GGUF block layout of gguf_loader.rs             */
+/* (Q8_0: f16 d + 32 x i8; Q4_0: f16 d + 16 bytes, byte j = elements 2j (low  */
+/* nibble) and 2j+1 (high), value = nibble - 8; src/gguf_loader.rs:413-498). */
+/* Codes follow QuantTensor::quantize PerGroup rules with group 32 over the  */
+/* flat buffer (src/quantize.rs:96-163, calibration 585-600); the f64 scale  */
+/* is narrowed to f32 and then to f16 by tensor_engine::f32_to_f16           */
+/* (truncating, src/tensor_engine.rs:42-64).                                 */
+/* ------------------------------------------------------------------------ */
+size_t vxb_block_bytes(int fmt, size_t n_elements);
+/* Replaces QuantTensor::quantize (src/quantize.rs:81-163) + pack_int4 (664). */
+int vxb_pack_blocks_f64(int fmt, const double *h_w, size_t n, uint8_t *h_blocks);
+int vxb_pack_blocks_f32(int fmt, const float *h_w, size_t n, uint8_t *h_blocks);
+/* Replaces dequantize_q4_0 / dequantize_q8_0 (src/gguf_loader.rs:413-498). */
+int vxb_unpack_blocks(int fmt, const uint8_t *h_blocks, size_t n, float *h_out);
+
+/* Device quantizer: f32 weights on the device -> GGUF blocks on the device,
+ * bit-identical to vxb_pack_blocks_f32. Replaces QuantTensor::quantize for
+ * weights that already live in HBM. */
+int vxb_quantize_blocks(vxb_ctx *ctx, int fmt, const float *d_w, size_t n, uint8_t *d_blocks,
+                        void *stream);
+/* Device dequantizer (gguf_loader.rs dequantize_q*_0 on the device). */
+int vxb_dequantize_blocks(vxb_ctx *ctx, int fmt, const uint8_t *d_blocks, size_t n, float *d_out,
+                          void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Tiled weights: the kernels' HBM layout of a weight matrix W [N, K]         */
+/* (row-major, K % 32 == 0). The same codes and f16 scales as the GGUF       */
+/* blocks, regrouped so that each warp reads 512 contiguous bytes per load    */
+/* and each lane's 16 bytes are its tensor-core operand fragments. The        */
+/* conversion is lossless: vxb_untile_weights restores the exact blocks.     */
+/* ------------------------------------------------------------------------ */
+size_t vxb_tiled_bytes(int fmt, int N, int K);
+int vxb_tile_weights(vxb_ctx *ctx, int fmt, const uint8_t *d_blocks, int N, int K, void *d_tiled,
+                     void *stream);
+int vxb_untile_weights(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K,
+                       uint8_t *d_blocks, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* K1: decode dequant-GEMV / skinny GEMM, y[b, n] = sum_k W[n, k] x[b, k].   */
+/* Replaces weight_only_matmul (src/quantize.rs:845-852) and the matmul in   */
+/* Linear::forward (src/transformer.rs:332-352) for batch <= 32 rows.        */
+/* x: bf16 [batch, K]; y: [batch, N] of y_dtype (VXB_F32 or VXB_BF16).        */
+/* Accumulates in f32; uses the context workspace for split-K partials.      */
+/* ------------------------------------------------------------------------ */
+int vxb_gemv_q(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const uint16_t *d_x,
+               int batch, int y_dtype, void *d_y, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Paged KV cache. Replaces PagedKVCache (src/kv_cache.rs:29-93) and the     */
+/* kv_cache_* builtins (src/kv_cache.rs:183-290). Blocks of block_size       */
+/* tokens come from a free stack initialised to (0..max_blocks).rev();       */
+/* each (layer, seq_id) has its own block table; a block is popped when the  */
+/* last block is full. A token holds [num_kv_heads, head_dim] keys and       */
+/* values, stored as bf16 (VXB_BF16) or int8 with one f32 scale per (token,  */
+/* head) (VXB_I8: calibrate_minmax absmax/127, src/quantize.rs:585-591).     */
+/* Calls on one cache are stream-ordered by the caller.                      */
+/* ------------------------------------------------------------------------ */
+typedef struct vxb_kv vxb_kv;
+/* PagedKVCache::new (src/kv_cache.rs:41-45) / kv_cache_new (183-193) */
+int vxb_kv_create(vxb_ctx *ctx, int num_layers, int num_kv_heads, int head_dim, int block_size,
+                  int max_blocks, int max_seqs, int max_blocks_per_seq, int kv_dtype, vxb_kv **out);
+int vxb_kv_destroy(vxb_kv *kv);
+/* PagedKVCache::append_kv (src/kv_cache.rs:54-67) for one token of each of n
+ * sequences; d_k / d_v are bf16 [n, num_kv_heads, head_dim]. */
+int vxb_kv_append(vxb_kv *kv, int layer, int n, const int64_t *h_seq_ids, const uint16_t *d_k,
+                  const uint16_t *d_v, void *stream);
+/* n_tokens consecutive tokens of one sequence (prefill), [n_tokens, H, D]. */
+int vxb_kv_append_seq(vxb_kv *kv, int layer, int64_t seq_id, int n_tokens, const uint16_t *d_k,
+                      const uint16_t *d_v, void *stream);
+/* PagedKVCache::free_seq (src/kv_cache.rs:82-89): all layers of seq_id. */
+int vxb_kv_free_seq(vxb_kv *kv, int64_t seq_id);
+/* kv_cache_stats (src/kv_cache.rs:220-230): out6 = {used_blocks, free_blocks,
+ * block_size, num_seqs (tables), device bytes in use, distinct sequences}. */
+int vxb_kv_stats(const vxb_kv *kv, int64_t *out6);
+int vxb_kv_seq_len(const vxb_kv *kv, int layer, int64_t seq_id, int64_t *len);
+int vxb_kv_block_table(const vxb_kv *kv, int layer, int64_t seq_id, int32_t *h_out, int cap, int *n);
+/* PagedKVCache::get_kv (src/kv_cache.rs:69-80): f32 [len, H, D] (dequantized). */
+int vxb_kv_gather(vxb_kv *kv, int layer, int64_t seq_id, float *d_k_out, float *d_v_out, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* K4: decode attention. Replaces paged_attention / kv_cache_attention       */
+/* (src/kv_cache.rs:95-112, 207-218): for query row i (sequence h_seq_ids[i])*/
+/* and q head j, out = softmax(q . K^T * softmax_scale) V over every cached   */
+/* token of that sequence (no mask), with kv head j / (Hq / Hkv). An empty    */
+/* sequence gives zeros, as the reference. q / out are bf16 [n, Hq, D];      */
+/* d_lse (optional) receives the natural-log sum of exponentials [n, Hq].    */
+/* ------------------------------------------------------------------------ */
+int vxb_decode_attention(vxb_kv *kv, int layer, int n, const int64_t *h_seq_ids, const uint16_t *d_q,
+                         int num_q_heads, float softmax_scale, uint16_t *d_out, float *d_lse,
+                         void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* K5: single ops of the Llama-style block (stdlib/ai/transformer.vx).       */
+/* ------------------------------------------------------------------------ */
+/* layer_norm (RMS form with bias), stdlib/ai/transformer.vx:413-439:
+ * out = bf16(x * w / sqrt(mean(x^2) + eps) + b), x f32 [rows, n]. */
+int vxb_rmsnorm(vxb_ctx *ctx, const float *d_x, const float *d_w, const float *d_b, int rows, int n,
+                float eps, uint16_t *d_out, void *stream);
+/* feed_forward gate, stdlib/ai/transformer.vx:591-603: act = bf16(silu(g) * u)
+ * with gu = [g | u] f32 [rows, 2*ffn]. */
+int vxb_swiglu(vxb_ctx *ctx, const float *d_gu, int rows, int ffn, uint16_t *d_act, void *stream);
+/* argmax, stdlib/ai/transformer.vx:1163-1177 (first index of the maximum). */
+int vxb_argmax(vxb_ctx *ctx, const float *d_logits, int rows, int vocab, int32_t *d_out, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Decoder: Llama-style block stack (stdlib/ai/transformer.vx:958-1156) with  */
+/* a paged KV cache, one token per sequence per step (greedy next token).    */
+/* Stands behind the transformer_* builtins / TransformerModel::forward call */
+/* signatures (src/transformer.rs:773-814) for this architecture.            */
+/* ------------------------------------------------------------------------ */
+typedef struct vxb_decoder_config {
+    int vocab_size, dim, n_layers, n_heads, n_kv_heads, ffn_dim;
+    int max_batch;    /* sequences per step, <= 32 */
+    int max_seq;      /* tokens per sequence (prompt + generated) */
+    float norm_eps;   /* 1e-5 when <= 0 */
+    int weight_fmt;   /* VXB_Q4_0 or VXB_Q8_0 */
+    int kv_dtype;     /* VXB_BF16 (0 selects it) or VXB_I8 */
+    int kv_block_size;/* 16 when <= 0 */
+} vxb_decoder_config;
+typedef struct vxb_decoder vxb_decoder;
+int vxb_decoder_create(vxb_ctx *ctx, const vxb_decoder_config *cfg, vxb_decoder **out);
+int vxb_decoder_destroy(vxb_decoder *d);
+/* init_random_weights (stdlib/ai/transformer.vx:661-725): linears and
+ * embedding ~N(0, sigma) from a counter-based generator, norms w=1, b=0. */
+int vxb_decoder_init_random(vxb_decoder *d, uint64_t seed, float sigma);
+/* Load one weight from host memory: layer >= 0: which 0..6 = wq, wk, wv, wo,
+ * w1, w2, w3 as GGUF blocks [out, in]; 7..10 = attention-norm w, b, ffn-norm
+ * w, b (f32). layer == -1: 0 embedding (bf16 [vocab, dim]), 1/2 final norm
+ * w/b (f32), 3 output projection (blocks [vocab, dim]). */
+int vxb_decoder_set_weight(vxb_decoder *d, int layer, int which, const void *h_data, size_t bytes);
+/* One step through host buffers (synchronous): token h_tokens[i] of sequence
+ * h_seq_ids[i] is appended; h_next gets the greedy next token, h_logits
+ * (optional) the logits [batch, vocab]. */
+int vxb_decoder_step(vxb_decoder *d, int batch, const int64_t *h_seq_ids, const int32_t *h_tokens,
+                     int32_t *h_next, float *h_logits);
+/* The same with device token buffers, ordered on `stream`. */
+int vxb_decoder_step_device(vxb_decoder *d, int batch, const int64_t *h_seq_ids,
+                            const int32_t *d_tokens, int32_t *d_next, void *stream);
+int vxb_decoder_logits(vxb_decoder *d, int batch, float *d_out, void *stream);
+int vxb_decoder_free_seq(vxb_decoder *d, int64_t seq_id);
+int vxb_decoder_kv(vxb_decoder *d, vxb_kv **out);
+int vxb_decoder_stream(vxb_decoder *d, void **out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VXB_H */

@@ -1,0 +1,516 @@
+// K4: split-K decode attention over the paged KV cache.
+//
+// Replaces paged_attention / kv_cache_attention (src/kv_cache.rs:95-112,
+// 207-218): for one new query per sequence,
+//   out[h] = softmax(q_h . K^T * scale) V      (all cached tokens, no mask)
+// generalised to [num_q_heads, head_dim] queries with grouped-query sharing
+// (q head j reads kv head j / (Hq/Hkv)); Hq == Hkv == 1 is the reference case.
+//
+// One CTA = (sequence, kv head, token split); its four warps stream 16-token
+// pages of K and V from the pool into XOR-swizzled shared memory with
+// double-buffered cp.async, and compute on tensor cores:
+//   S = Q K^T   : mma.m16n8k16 bf16, A = the G query heads of the group
+//                 (rows padded to 16), B = K rows via ldmatrix
+//   online softmax on the S fragments (exp2, per-row max/sum kept in f32,
+//                 quad shuffles for the row reductions)
+//   O += P V    : A = P re-packed from the S fragments, B = V via ldmatrix.trans
+// Warps merge through shared memory; splits merge deterministically in the
+// last-arriving CTA of each (sequence, kv head) (counter in global memory).
+// int8 caches stage int8 pages and one f32 scale per (token, head); the K
+// scale multiplies the scores and the V scale is folded into P.
+#include <cuda_bf16.h>
+
+#include "decode_attn.h"
+#include "kv_cache.h"
+
+using namespace vxb;
+
+namespace {
+
+constexpr int WARPS = 4;
+constexpr int THREADS = WARPS * 32;
+constexpr int PAGE = 16;
+constexpr int kMaxInlineRows = 256;
+
+struct DecodeArgs {
+  const uint16_t *q;  // [n, Hq, D] bf16
+  uint16_t *out;      // [n, Hq, D] bf16
+  float *lse;         // optional [n, Hq] natural-log sum-exp
+  const void *pool_k, *pool_v;
+  const float *sk, *sv;
+  const int32_t *tables;  // this layer: [max_seqs][mbps]
+  const int32_t *lens;    // this layer: [max_seqs]
+  const int32_t *slots;   // [n] in device memory, or null: use slots_inline
+  float *ws_o, *ws_ml;
+  unsigned *counters;
+  int n, Hq, Hkv, G, bs, mbps, splits, tps;
+  float scale_log2;
+  // slot ids passed by value (kernel parameters are captured with a graph
+  // node, so a standalone call stays valid under stream capture)
+  int32_t slots_inline[kMaxInlineRows];
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, int bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes));
+}
+
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, int bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(bytes));
+}
+
+__device__ __forceinline__ void mma_bf16(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+// (a, b) -> hi = bf16x2(a, b) and lo = bf16x2(a - hi.a, b - hi.b)
+__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t &hi, uint32_t &lo) {
+  hi = pack_bf16x2(a, b);
+  const float ha = __uint_as_float(hi << 16), hb = __uint_as_float(hi & 0xFFFF0000u);
+  lo = pack_bf16x2(a - ha, b - hb);
+}
+
+// byte offset of 16-byte chunk c of token row r in a swizzled page tile
+template <int D>
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+  return (uint32_t)(r * D * 2 + ((c ^ (r & 7)) << 4));
+}
+
+template <int D, bool INT8>
+struct Smem {
+  // per warp, per stage: bf16 tiles (converted for int8) and raw int8 pages
+  static constexpr int TILE = PAGE * D * 2;                  // one bf16 page tile
+  static constexpr int RAW = INT8 ? PAGE * D : 0;            // one int8 page
+  static constexpr int SC = INT8 ? PAGE * 4 : 0;             // per-token scales
+  static constexpr int STAGE = INT8 ? 2 * RAW + 2 * SC : 2 * TILE;
+  static constexpr int WARP = 2 * STAGE + (INT8 ? 2 * TILE : 0);
+  static constexpr int TOTAL = WARPS * WARP;
+};
+
+template <int D, bool INT8>
+__global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a) {
+  using SM = Smem<D, INT8>;
+  constexpr int CHUNKS = D / 8;  // 16-byte chunks per bf16 row
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int s_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q4 = lane & 3;
+  const int i = blockIdx.x / a.Hkv, h = blockIdx.x % a.Hkv, split = blockIdx.y;
+  const int slot = a.slots ? a.slots[i] : a.slots_inline[i];
+  const int len = slot >= 0 ? a.lens[slot] : 0;
+  const int t0 = split * a.tps;
+  const int t1 = min(len, t0 + a.tps);
+  const int32_t *table = a.tables + (size_t)(slot >= 0 ? slot : 0) * a.mbps;
+  uint8_t *wsm = smem + (size_t)warp * SM::WARP;
+  const uint32_t wsm_s = (uint32_t)__cvta_generic_to_shared(wsm);
+
+  // Q fragments (rows = the G query heads of this group, padded to 16)
+  uint32_t qa[D / 16][4];
+  {
+    const uint32_t *qrow0 = reinterpret_cast<const uint32_t *>(a.q + ((size_t)i * a.Hq + (size_t)h * a.G + g) * D);
+    const uint32_t *qrow1 = reinterpret_cast<const uint32_t *>(a.q + ((size_t)i * a.Hq + (size_t)h * a.G + g + 8) * D);
+    const bool v0 = g < a.G, v1 = g + 8 < a.G;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ks++) {
+      qa[ks][0] = v0 ? qrow0[ks * 8 + q4] : 0u;
+      qa[ks][1] = v1 ? qrow1[ks * 8 + q4] : 0u;
+      qa[ks][2] = v0 ? qrow0[ks * 8 + 4 + q4] : 0u;
+      qa[ks][3] = v1 ? qrow1[ks * 8 + 4 + q4] : 0u;
+    }
+  }
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int dt = 0; dt < D / 8; dt++) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+  const int pg0 = t0 / PAGE, pg1 = t1 > t0 ? (t1 + PAGE - 1) / PAGE : pg0;
+  const int npages = pg1 - pg0;
+  const int my = npages > warp ? (npages - warp + WARPS - 1) / WARPS : 0;
+
+  auto prefetch = [&](int j, int stage) {
+    const int p = pg0 + warp + j * WARPS;
+    const int tok0 = p * PAGE;
+    const int block = table[tok0 / a.bs];
+    const int off = tok0 % a.bs;
+    const size_t base = ((size_t)block * a.Hkv + h) * a.bs + off;  // token row index in pool
+    uint8_t *st = wsm + stage * SM::STAGE;
+    const uint32_t st_s = wsm_s + stage * SM::STAGE;
+    if (!INT8) {
+      const uint16_t *kp = reinterpret_cast<const uint16_t *>(a.pool_k) + base * D;
+      const uint16_t *vp = reinterpret_cast<const uint16_t *>(a.pool_v) + base * D;
+#pragma unroll
+      for (int c = lane; c < PAGE * CHUNKS; c += 32) {
+        const int r = c / CHUNKS, cc = c % CHUNKS;
+        const int bytes = tok0 + r < len ? 16 : 0;
+        cp_async16(st_s + swz<D>(r, cc), kp + (size_t)r * D + cc * 8, bytes);
+        cp_async16(st_s + SM::TILE + swz<D>(r, cc), vp + (size_t)r * D + cc * 8, bytes);
+      }
+    } else {
+      const int8_t *kp = reinterpret_cast<const int8_t *>(a.pool_k) + base * D;
+      const int8_t *vp = reinterpret_cast<const int8_t *>(a.pool_v) + base * D;
+      constexpr int RCH = D / 16;  // 16-byte chunks per int8 row
+#pragma unroll
+      for (int c = lane; c < PAGE * RCH; c += 32) {
+        const int r = c / RCH, cc = c % RCH;
+        const int bytes = tok0 + r < len ? 16 : 0;
+        cp_async16(st_s + r * D + cc * 16, kp + (size_t)r * D + cc * 16, bytes);
+        cp_async16(st_s + SM::RAW + r * D + cc * 16, vp + (size_t)r * D + cc * 16, bytes);
+      }
+      {
+        // per-token scales: lanes 0-15 the K scales, lanes 16-31 the V scales
+        const bool isv = lane >= 16;
+        const int r = lane & 15;
+        cp_async4(st_s + 2 * SM::RAW + (isv ? SM::SC : 0) + r * 4, (isv ? a.sv : a.sk) + base + r,
+                  tok0 + r < len ? 4 : 0);
+      }
+      (void)st;
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
+  if (my > 0) prefetch(0, 0);
+  for (int j = 0; j < my; j++) {
+    const int stage = j & 1;
+    if (j + 1 < my) {
+      prefetch(j + 1, stage ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncwarp();
+    const int p = pg0 + warp + j * WARPS;
+    const int tok0 = p * PAGE;
+    uint32_t kt = wsm_s + stage * SM::STAGE, vt = kt + SM::TILE;
+    float ksc[2][2], vsc[2][2];
+    if (INT8) {
+      // scales of this lane's token columns (tok 2q, 2q+1 of each n-tile)
+      const float *scs = reinterpret_cast<const float *>(wsm + stage * SM::STAGE + 2 * SM::RAW);
+#pragma unroll
+      for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          const int r = nt * 8 + q4 * 2 + e;
+          const bool ok = tok0 + r < len;
+          ksc[nt][e] = ok ? scs[r] : 0.f;
+          vsc[nt][e] = ok ? scs[PAGE + r] : 0.f;
+        }
+      // int8 -> bf16 (exact) into the swizzled tiles
+      const int8_t *rk = reinterpret_cast<const int8_t *>(wsm + stage * SM::STAGE);
+      uint8_t *tk = wsm + 2 * SM::STAGE;
+      for (int c = lane; c < 2 * PAGE * CHUNKS; c += 32) {
+        const bool isv = c >= PAGE * CHUNKS;
+        const int cc_ = isv ? c - PAGE * CHUNKS : c;
+        const int r = cc_ / CHUNKS, cc = cc_ % CHUNKS;
+        const int8_t *src = rk + (isv ? SM::RAW : 0) + r * D + cc * 8;
+        const uint2 raw = *reinterpret_cast<const uint2 *>(src);
+        const int8_t *b8 = reinterpret_cast<const int8_t *>(&raw);
+        uint4 outv;
+        outv.x = pack_bf16x2((float)b8[0], (float)b8[1]);
+        outv.y = pack_bf16x2((float)b8[2], (float)b8[3]);
+        outv.z = pack_bf16x2((float)b8[4], (float)b8[5]);
+        outv.w = pack_bf16x2((float)b8[6], (float)b8[7]);
+        *reinterpret_cast<uint4 *>(tk + (isv ? SM::TILE : 0) + swz<D>(r, cc)) = outv;
+      }
+      __syncwarp();
+      kt = wsm_s + 2 * SM::STAGE;
+      vt = kt + SM::TILE;
+    }
+
+    // S = Q K^T for the page's 16 tokens (two n-tiles of 8)
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ks++) {
+      const int r = (lane >> 4) * 8 + (lane & 7);
+      const int c = ks * 2 + ((lane >> 3) & 1);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(kt + swz<D>(r, c), b0, b1, b2, b3);
+      mma_bf16(s[0], qa[ks], b0, b1);
+      mma_bf16(s[1], qa[ks], b2, b3);
+    }
+    // scale, mask, online softmax
+#pragma unroll
+    for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int tok = tok0 + nt * 8 + q4 * 2 + (e & 1);
+        float v = s[nt][e] * a.scale_log2;
+        if (INT8) v *= ksc[nt][e & 1];
+        s[nt][e] = tok < len ? v : -INFINITY;
+      }
+    float mx0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
+    float mx1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float c0 = mn0 == -INFINITY ? 1.f : exp2f(m0 - mn0);
+    const float c1 = mn1 == -INFINITY ? 1.f : exp2f(m1 - mn1);
+    m0 = mn0;
+    m1 = mn1;
+    float pp[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; nt++) {
+      pp[nt][0] = mn0 == -INFINITY ? 0.f : exp2f(s[nt][0] - mn0);
+      pp[nt][1] = mn0 == -INFINITY ? 0.f : exp2f(s[nt][1] - mn0);
+      pp[nt][2] = mn1 == -INFINITY ? 0.f : exp2f(s[nt][2] - mn1);
+      pp[nt][3] = mn1 == -INFINITY ? 0.f : exp2f(s[nt][3] - mn1);
+    }
+    l0 = l0 * c0 + (pp[0][0] + pp[0][1] + pp[1][0] + pp[1][1]);
+    l1 = l1 * c1 + (pp[0][2] + pp[0][3] + pp[1][2] + pp[1][3]);
+#pragma unroll
+    for (int dt = 0; dt < D / 8; dt++) {
+      o[dt][0] *= c0;
+      o[dt][1] *= c0;
+      o[dt][2] *= c1;
+      o[dt][3] *= c1;
+    }
+    if (INT8) {
+#pragma unroll
+      for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) pp[nt][e] *= vsc[nt][e & 1];
+    }
+    // P = P_hi + P_lo, both bf16 (P_lo = the rounding residue of P_hi), so
+    // the two PV products carry P to ~2^-17 relative.
+    uint32_t pa[4], pl[4];
+    split_bf16x2(pp[0][0], pp[0][1], pa[0], pl[0]);
+    split_bf16x2(pp[0][2], pp[0][3], pa[1], pl[1]);
+    split_bf16x2(pp[1][0], pp[1][1], pa[2], pl[2]);
+    split_bf16x2(pp[1][2], pp[1][3], pa[3], pl[3]);
+#pragma unroll
+    for (int dt2 = 0; dt2 < D / 16; dt2++) {
+      const int r = ((lane >> 3) & 1) * 8 + (lane & 7);
+      const int c = dt2 * 2 + (lane >> 4);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(vt + swz<D>(r, c), b0, b1, b2, b3);
+      mma_bf16(o[2 * dt2], pa, b0, b1);
+      mma_bf16(o[2 * dt2 + 1], pa, b2, b3);
+      mma_bf16(o[2 * dt2], pl, b0, b1);
+      mma_bf16(o[2 * dt2 + 1], pl, b2, b3);
+    }
+    __syncwarp();
+  }
+  // row sums across the quad
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+  // ---- merge the four warps through shared memory
+  __syncthreads();
+  float *mo = reinterpret_cast<float *>(smem);   // [WARPS][16][D]
+  float *mm = mo + WARPS * 16 * D;               // [WARPS][16]
+  float *ml = mm + WARPS * 16;                   // [WARPS][16]
+#pragma unroll
+  for (int dt = 0; dt < D / 8; dt++) {
+    const int d = dt * 8 + q4 * 2;
+    mo[((size_t)warp * 16 + g) * D + d] = o[dt][0];
+    mo[((size_t)warp * 16 + g) * D + d + 1] = o[dt][1];
+    mo[((size_t)warp * 16 + g + 8) * D + d] = o[dt][2];
+    mo[((size_t)warp * 16 + g + 8) * D + d + 1] = o[dt][3];
+  }
+  if (q4 == 0) {
+    mm[warp * 16 + g] = m0;
+    mm[warp * 16 + g + 8] = m1;
+    ml[warp * 16 + g] = l0;
+    ml[warp * 16 + g + 8] = l1;
+  }
+  __syncthreads();
+  const int G = a.G;
+  const size_t grp = (size_t)i * a.Hkv + h;
+  const float LN2 = 0.69314718055994530942f;
+  for (int e = threadIdx.x; e < G * D; e += THREADS) {
+    const int r = e / D, d = e % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < WARPS; w++) M = fmaxf(M, mm[w * 16 + r]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < WARPS; w++) {
+        const float f = exp2f(mm[w * 16 + r] - M);
+        L += ml[w * 16 + r] * f;
+        O += mo[((size_t)w * 16 + r) * D + d] * f;
+      }
+    }
+    if (a.splits == 1) {
+      const size_t orow = (size_t)i * a.Hq + (size_t)h * G + r;
+      a.out[orow * D + d] = f32_to_bf16_bits(L > 0.f ? O / L : 0.f);
+      if (a.lse && d == 0) a.lse[orow] = L > 0.f ? (M + log2f(L)) * LN2 : -INFINITY;
+    } else {
+      const size_t pr = (grp * a.splits + split) * G + r;
+      __stcg(a.ws_o + pr * D + d, O);
+      if (d == 0) {
+        __stcg(a.ws_ml + pr * 2, M);
+        __stcg(a.ws_ml + pr * 2 + 1, L);
+      }
+    }
+  }
+  if (a.splits == 1) return;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(a.counters + grp, 1u) == (unsigned)(a.splits - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int e = threadIdx.x; e < G * D; e += THREADS) {
+    const int r = e / D, d = e % D;
+    float M = -INFINITY;
+    for (int sp = 0; sp < a.splits; sp++) M = fmaxf(M, __ldcg(a.ws_ml + ((grp * a.splits + sp) * G + r) * 2));
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+      for (int sp = 0; sp < a.splits; sp++) {
+        const size_t pr = (grp * a.splits + sp) * G + r;
+        const float f = exp2f(__ldcg(a.ws_ml + pr * 2) - M);
+        L += __ldcg(a.ws_ml + pr * 2 + 1) * f;
+        O += __ldcg(a.ws_o + pr * D + d) * f;
+      }
+    }
+    const size_t orow = (size_t)i * a.Hq + (size_t)h * G + r;
+    a.out[orow * D + d] = f32_to_bf16_bits(L > 0.f ? O / L : 0.f);
+    if (a.lse && d == 0) a.lse[orow] = L > 0.f ? (M + log2f(L)) * LN2 : -INFINITY;
+  }
+  if (threadIdx.x == 0) a.counters[grp] = 0u;
+}
+
+template <int D, bool INT8>
+int launch_t(vxb_ctx *ctx, const DecodeArgs &a, cudaStream_t st) {
+  auto kfn = decode_attn_kernel<D, INT8>;
+  using SM = Smem<D, INT8>;
+  const size_t merge = (size_t)WARPS * 16 * D * 4 + 2 * WARPS * 16 * 4;
+  const size_t smem = SM::TOTAL > merge ? SM::TOTAL : merge;
+  static bool configured[64] = {false};
+  if (!configured[ctx->device & 63]) {
+    VXB_CUDA_TRY(ctx, cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    configured[ctx->device & 63] = true;
+  }
+  dim3 grid(a.n * a.Hkv, a.splits);
+  kfn<<<grid, THREADS, smem, st>>>(a);
+  return launch_check(ctx, "decode_attn_kernel");
+}
+
+}  // namespace
+
+namespace vxb {
+
+DecodePlan decode_plan(const vxb_ctx *ctx, int n, int Hkv, int max_len) {
+  DecodePlan p;
+  const int sms = ctx->num_sms > 0 ? ctx->num_sms : 148;
+  const int pairs = n * Hkv;
+  int splits = (3 * sms + pairs - 1) / pairs;
+  const int max_split = max(1, (max_len + 63) / 64);
+  splits = max(1, min(splits, max_split));
+  int tps = (max_len + splits - 1) / splits;
+  tps = max(64, (tps + 63) / 64 * 64);
+  splits = max(1, (max_len + tps - 1) / tps);
+  p.splits = splits;
+  p.tps = tps;
+  return p;
+}
+
+size_t decode_ws_bytes(int n, int Hkv, int G, int D, int splits) {
+  const size_t pr = (size_t)n * Hkv * splits * G;
+  return 256 + pr * D * 4 + pr * 2 * 4 + 256;
+}
+
+int decode_attn_launch(vxb_kv *kv, int layer, int n, const int32_t *d_slots, const int32_t *h_slots,
+                       const uint16_t *d_q, int Hq, float softmax_scale, uint16_t *d_out, float *d_lse,
+                       const DecodePlan &p, float *ws, cudaStream_t st) {
+  vxb_ctx *ctx = kv->ctx;
+  const int Hkv = kv->num_kv_heads, D = kv->head_dim;
+  const int G = Hq / Hkv;
+  DecodeArgs a;
+  a.q = d_q;
+  a.out = d_out;
+  a.lse = d_lse;
+  a.pool_k = kv->pool_k;
+  a.pool_v = kv->pool_v;
+  a.sk = kv->scale_k;
+  a.sv = kv->scale_v;
+  a.tables = kv->d_tables + (size_t)layer * kv->max_seqs * kv->max_blocks_per_seq;
+  a.lens = kv->d_lens + (size_t)layer * kv->max_seqs;
+  a.slots = d_slots;
+  if (!d_slots) {
+    if (!h_slots || n > kMaxInlineRows) return set_error(ctx, VXB_EINVAL, "decode attention: %d rows without device slots", n);
+    for (int i = 0; i < n; i++) a.slots_inline[i] = h_slots[i];
+  }
+  const size_t pr = (size_t)n * Hkv * p.splits * G;
+  a.ws_ml = ws;
+  a.ws_o = ws + ((pr * 2 + 63) / 64 * 64);
+  a.counters = ctx->counters;
+  a.n = n;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.G = G;
+  a.bs = kv->block_size;
+  a.mbps = kv->max_blocks_per_seq;
+  a.splits = p.splits;
+  a.tps = p.tps;
+  a.scale_log2 = softmax_scale * 1.44269504088896340736f;
+  const bool i8 = kv->dtype == VXB_I8;
+  if (D == 128) return i8 ? launch_t<128, true>(ctx, a, st) : launch_t<128, false>(ctx, a, st);
+  return i8 ? launch_t<64, true>(ctx, a, st) : launch_t<64, false>(ctx, a, st);
+}
+
+}  // namespace vxb
+
+VXB_API int vxb_decode_attention(vxb_kv *kv, int layer, int n, const int64_t *h_seq_ids, const uint16_t *d_q,
+                                 int num_q_heads, float softmax_scale, uint16_t *d_out, float *d_lse, void *stream) {
+  if (!kv || !kv->ctx) return set_error(nullptr, VXB_EINVAL, "vxb_decode_attention: null cache");
+  vxb_ctx *ctx = kv->ctx;
+  if (layer < 0 || layer >= kv->num_layers) return set_error(ctx, VXB_EINVAL, "vxb_decode_attention: layer out of range");
+  if (n < 0 || (n > 0 && (!h_seq_ids || !d_q || !d_out))) return set_error(ctx, VXB_EINVAL, "vxb_decode_attention: bad arguments");
+  if (num_q_heads <= 0 || num_q_heads % kv->num_kv_heads || num_q_heads / kv->num_kv_heads > 16)
+    return set_error(ctx, VXB_EINVAL, "vxb_decode_attention: num_q_heads %d must be a multiple (<= 16x) of the %d kv heads",
+                     num_q_heads, kv->num_kv_heads);
+  if (((uintptr_t)d_q) % 16) return set_error(ctx, VXB_EINVAL, "vxb_decode_attention: q must be 16-byte aligned");
+  if (n == 0) return VXB_OK;
+  if (int rc = use_device(ctx)) return rc;
+  std::vector<int32_t> slots(n);
+  int max_len = 0;
+  for (int i = 0; i < n; i++) {
+    auto si = kv->slot_of.find(h_seq_ids[i]);
+    slots[i] = si == kv->slot_of.end() ? -1 : si->second;
+    auto it = kv->tables.find(std::make_pair(layer, h_seq_ids[i]));
+    if (it != kv->tables.end()) max_len = std::max<int>(max_len, (int)it->second.len);
+  }
+  const int G = num_q_heads / kv->num_kv_heads;
+  const int rows = std::min(n, kMaxInlineRows);
+  const DecodePlan p = decode_plan(ctx, rows, kv->num_kv_heads, std::max(max_len, 1));
+  const size_t wsb = decode_ws_bytes(rows, kv->num_kv_heads, G, kv->head_dim, p.splits);
+  if (int rc = ws_reserve(ctx, wsb, (size_t)rows * kv->num_kv_heads)) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  // rows go in chunks whose slot ids travel as kernel parameters
+  for (int r0 = 0; r0 < n; r0 += kMaxInlineRows) {
+    const int nr = std::min(kMaxInlineRows, n - r0);
+    const size_t off = (size_t)r0 * num_q_heads * kv->head_dim;
+    if (int rc = decode_attn_launch(kv, layer, nr, nullptr, slots.data() + r0, d_q + off, num_q_heads, softmax_scale,
+                                    d_out + off, d_lse ? d_lse + (size_t)r0 * num_q_heads : nullptr, p,
+                                    (float *)ctx->ws, st))
+      return rc;
+  }
+  return VXB_OK;
+}

@@ -1,0 +1,20 @@
+// Internal interface of the K1 GEMV (shared with the decoder).
+#pragma once
+
+#include "vxb_internal.h"
+
+namespace vxb {
+
+struct GemvPlan {
+  int S;     // k-splits (CTAs per row group)
+  bool pdl;  // launch with programmatic stream serialization
+};
+
+GemvPlan gemv_plan(const vxb_ctx *ctx, int fmt, int N, int K, int batch);
+size_t gemv_smem_bytes(int fmt, int N, int K, int batch, int S);
+
+// y = W x (+ resid). d_resid (optional) is f32 [batch, N] added in the epilogue.
+int gemv_launch(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const uint16_t *d_x, int batch,
+                int y_dtype, void *d_y, const float *d_resid, void *stream, const GemvPlan *plan_override);
+
+}  // namespace vxb
