@@ -69,6 +69,11 @@ int vxb_memcpy_h2d(vxb_ctx *ctx, void *d_dst, const void *h_src, size_t bytes, v
 int vxb_memcpy_d2h(vxb_ctx *ctx, void *h_dst, const void *d_src, size_t bytes, void *stream);
 int vxb_memset(vxb_ctx *ctx, void *d_dst, int value, size_t bytes, void *stream);
 int vxb_sync(vxb_ctx *ctx, void *stream);
+/* Synchronize the device, read and clear the context's device error word.
+ * Kernels bound every wait (clock64 budget); a wait that runs out sets the
+ * word and the kernel finishes instead of hanging. Returns VXB_ETIMEOUT
+ * (and *out != 0) when that happened since the last call. */
+int vxb_device_error(vxb_ctx *ctx, int *out);
 
 /* ------------------------------------------------------------------------ */
 /* Weight blocks (host codec).                                               */

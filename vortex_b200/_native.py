@@ -55,6 +55,7 @@ SIGNATURES = {
     "vxb_memcpy_d2h": (_I, [_P, _P, _P, _SZ, _P]),
     "vxb_memset": (_I, [_P, _P, _I, _SZ, _P]),
     "vxb_sync": (_I, [_P, _P]),
+    "vxb_device_error": (_I, [_P, ctypes.POINTER(_I)]),
     "vxb_block_bytes": (_SZ, [_I, _SZ]),
     "vxb_pack_blocks_f64": (_I, [_I, _P, _SZ, _P]),
     "vxb_pack_blocks_f32": (_I, [_I, _P, _SZ, _P]),

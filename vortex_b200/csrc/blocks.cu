@@ -195,34 +195,41 @@ __global__ void tile_codes_kernel(const uint8_t *__restrict__ blocks, int fmt, i
   const size_t tc = idx / 128;  // (tile, chunk) of the part
   const int c = (int)(tc % g.n_chunks);
   const int t = (int)(tc / g.n_chunks);
-  const int r0 = t * 16 + l / 4, r1 = r0 + 8, cc = (l % 4) * 2;
+  // k-permuted fragments: lane q of a k16 step holds columns 4q..4q+3, so the
+  // activation operand of the lane is 8 contiguous bytes
+  const int r0 = t * 16 + l / 4, r1 = r0 + 8, k4 = (l % 4) * 4;
   codes += (size_t)tile0 * g.n_chunks * 128;
   uint32_t w = 0;
   if (fmt == VXB_Q4_0) {
-    const int kb = (4 * c + j) * 16;
-    w = q4_nibble(blocks, N, K, r0, kb + cc) | (q4_nibble(blocks, N, K, r1, kb + cc) << 4) |
-        (q4_nibble(blocks, N, K, r0, kb + cc + 8) << 8) | (q4_nibble(blocks, N, K, r1, kb + cc + 8) << 12) |
-        (q4_nibble(blocks, N, K, r0, kb + cc + 1) << 16) | (q4_nibble(blocks, N, K, r1, kb + cc + 1) << 20) |
-        (q4_nibble(blocks, N, K, r0, kb + cc + 9) << 24) | (q4_nibble(blocks, N, K, r1, kb + cc + 9) << 28);
+    const int kb = (4 * c + j) * 16 + k4;
+    w = q4_nibble(blocks, N, K, r0, kb) | (q4_nibble(blocks, N, K, r1, kb) << 4) |
+        (q4_nibble(blocks, N, K, r0, kb + 2) << 8) | (q4_nibble(blocks, N, K, r1, kb + 2) << 12) |
+        (q4_nibble(blocks, N, K, r0, kb + 1) << 16) | (q4_nibble(blocks, N, K, r1, kb + 1) << 20) |
+        (q4_nibble(blocks, N, K, r0, kb + 3) << 24) | (q4_nibble(blocks, N, K, r1, kb + 3) << 28);
   } else {
-    const int kb = (2 * c + j / 2) * 16 + ((j & 1) ? 8 : 0);
-    w = q8_byte(blocks, N, K, r0, kb + cc) | (q8_byte(blocks, N, K, r0, kb + cc + 1) << 8) |
-        (q8_byte(blocks, N, K, r1, kb + cc) << 16) | (q8_byte(blocks, N, K, r1, kb + cc + 1) << 24);
+    const int kb = (2 * c + j / 2) * 16 + k4 + ((j & 1) ? 2 : 0);
+    w = q8_byte(blocks, N, K, r0, kb) | (q8_byte(blocks, N, K, r0, kb + 1) << 8) |
+        (q8_byte(blocks, N, K, r1, kb) << 16) | (q8_byte(blocks, N, K, r1, kb + 1) << 24);
   }
   codes[idx] = w;
 }
 
-// One thread per u32 of the part's scales: (tile, block, i) -> rows 16t+i, 16t+i+8.
+// One thread per u32 of the part's scales, ordered (tile, chunk, i, block of
+// the chunk): entry = f16 scale of row 16t+i (low half) | row 16t+i+8 (high).
 __global__ void tile_scales_kernel(const uint8_t *__restrict__ blocks, int fmt, int N, int K, TiledGeom g, int tile0,
                                    uint32_t *__restrict__ scales, uint32_t *__restrict__ hdr) {
   const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   const size_t total = (size_t)((N + 15) / 16) * g.n_blocks * 8;
   if (idx >= total) return;
-  const int i = idx % 8;
-  const int b = (int)((idx / 8) % g.n_blocks);
-  const int t = (int)(idx / (8 * (size_t)g.n_blocks));
+  const int bpc = g.chunk / 32;
+  const int bb = idx % bpc;
+  const int i = (idx / bpc) % 8;
+  const size_t tc = idx / (8 * bpc);
+  const int c = (int)(tc % g.n_chunks);
+  const int t = (int)(tc / g.n_chunks);
+  const int b = c * bpc + bb;
   scales += (size_t)tile0 * g.n_blocks * 8;
-  const size_t bb = fmt == VXB_Q4_0 ? 18 : 34;
+  const size_t blk_bytes = fmt == VXB_Q4_0 ? 18 : 34;
   uint32_t out = 0;
   bool sub = false;
 #pragma unroll
@@ -230,7 +237,7 @@ __global__ void tile_scales_kernel(const uint8_t *__restrict__ blocks, int fmt, 
     const int r = t * 16 + i + 8 * h;
     uint32_t s = 0;
     if (r < N && b < K / 32) {
-      const uint8_t *blk = blocks + ((size_t)r * (K / 32) + b) * bb;
+      const uint8_t *blk = blocks + ((size_t)r * (K / 32) + b) * blk_bytes;
       s = (uint32_t)blk[0] | ((uint32_t)blk[1] << 8);
       if ((s & 0x7C00u) == 0 && (s & 0x3FFu) != 0) sub = true;
     }
@@ -249,7 +256,8 @@ __global__ void untile_kernel(const uint8_t *__restrict__ tiled, int fmt, int N,
   const int r = (int)(idx / nbk), b = (int)(idx % nbk);
   const int t = r / 16, ri = r % 16;
   const uint32_t *sc = (const uint32_t *)(tiled + g.codes_off + g.codes_bytes);
-  const uint32_t s = sc[((size_t)t * g.n_blocks + b) * 8 + (ri & 7)] >> (ri >= 8 ? 16 : 0);
+  const int bpc = g.chunk / 32;
+  const uint32_t s = sc[(((size_t)t * g.n_chunks + b / bpc) * 8 + (ri & 7)) * bpc + b % bpc] >> (ri >= 8 ? 16 : 0);
   const uint8_t *codes = tiled + g.codes_off;
   if (fmt == VXB_Q4_0) {
     uint8_t *o = blocks + idx * 18;
@@ -261,8 +269,8 @@ __global__ void untile_kernel(const uint8_t *__restrict__ tiled, int fmt, int N,
         const int k = b * 32 + 2 * jb + e;
         const int step = k / 16, kk = k % 16;
         const int c = step / 4, j = step % 4;
-        const int kc = kk & 7, lane = (ri & 7) * 4 + kc / 2;
-        const int pos = (ri >= 8 ? 4 : 0) + (kk >= 8 ? 8 : 0) + ((kc & 1) ? 16 : 0);
+        const int jj = kk & 3, lane = (ri & 7) * 4 + kk / 4;
+        const int pos = (ri >= 8 ? 4 : 0) + (jj >= 2 ? 8 : 0) + ((jj & 1) ? 16 : 0);
         const uint32_t w = ((const uint32_t *)codes)[(((size_t)t * g.n_chunks + c) * 32 + lane) * 4 + j];
         nib[e] = (w >> pos) & 0xF;
       }
@@ -276,9 +284,9 @@ __global__ void untile_kernel(const uint8_t *__restrict__ tiled, int fmt, int N,
       const int k = b * 32 + e;
       const int step = k / 16, kk = k % 16;
       const int c = step / 2;
-      const int kc = kk & 7, lane = (ri & 7) * 4 + kc / 2;
-      const int j = (step % 2) * 2 + (kk >= 8 ? 1 : 0);
-      const int byte = (ri >= 8 ? 2 : 0) + (kc & 1);
+      const int jj = kk & 3, lane = (ri & 7) * 4 + kk / 4;
+      const int j = (step % 2) * 2 + (jj >= 2 ? 1 : 0);
+      const int byte = (ri >= 8 ? 2 : 0) + (jj & 1);
       o[2 + e] = codes[((((size_t)t * g.n_chunks + c) * 32 + lane) * 4 + j) * 4 + byte];
     }
   }

@@ -34,6 +34,15 @@ int use_device(vxb_ctx *ctx) {
 }
 
 int ws_reserve(vxb_ctx *ctx, size_t bytes, size_t counters) {
+  if (!ctx->d_err) {
+    int *p = nullptr;
+    if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) {
+      cudaGetLastError();
+      return set_error(ctx, VXB_ENOMEM, "device error word allocation failed");
+    }
+    VXB_CUDA_TRY(ctx, cudaMemset(p, 0, sizeof(int)));
+    ctx->d_err = p;
+  }
   if (bytes > ctx->ws_bytes) {
     size_t nb = round_up(bytes > (size_t)16 << 20 ? bytes : (size_t)16 << 20, 1 << 20);
     void *p = nullptr;
@@ -120,6 +129,7 @@ VXB_API int vxb_destroy(vxb_ctx *ctx) {
   cudaSetDevice(ctx->device);
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->counters) cudaFree(ctx->counters);
+  if (ctx->d_err) cudaFree(ctx->d_err);
   if (cur >= 0) cudaSetDevice(cur);
   delete ctx;
   return VXB_OK;
@@ -176,6 +186,18 @@ VXB_API int vxb_memset(vxb_ctx *ctx, void *d_dst, int value, size_t bytes, void 
   int rc = use_device(ctx);
   if (rc) return rc;
   VXB_CUDA_TRY(ctx, cudaMemsetAsync(d_dst, value, bytes, (cudaStream_t)stream));
+  return VXB_OK;
+}
+
+VXB_API int vxb_device_error(vxb_ctx *ctx, int *out) {
+  if (!ctx || !out) return set_error(ctx, VXB_EINVAL, "vxb_device_error: null argument");
+  *out = 0;
+  if (!ctx->d_err) return VXB_OK;
+  if (int rc = use_device(ctx)) return rc;
+  VXB_CUDA_TRY(ctx, cudaDeviceSynchronize());
+  VXB_CUDA_TRY(ctx, cudaMemcpy(out, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  VXB_CUDA_TRY(ctx, cudaMemset(ctx->d_err, 0, sizeof(int)));
+  if (*out) return set_error(ctx, VXB_ETIMEOUT, "a bounded device wait timed out (error word %d)", *out);
   return VXB_OK;
 }
 

@@ -7,26 +7,34 @@
 // (src/transformer.rs:332-352) at decode batch sizes.
 //
 // Design (HBM-bound streaming):
-//  * Each warp owns one 16-row tile and streams its 512-byte (tile, k-chunk)
-//    slices with 128-bit non-allocating loads; every lane's 16 bytes are its
-//    tensor-core A fragments, so codes are unpacked in registers and never
-//    touch shared memory. Codes (-8..7 or -128..127) are exact in bf16:
-//    Q4_0 uses the bf16 magic 128+n (1 LOP3 + 1 SUB.BF16X2 per two codes),
-//    Q8_0 goes through the f32 magic 2^23+u and one CVT per two codes.
-//  * The activations x (bf16) of the CTA's k-range are copied into shared
-//    memory unchanged with cp.async by all threads and used directly as the
-//    bf16 B operand.
-//  * mma.m16n8k16 (bf16 x bf16 -> f32) forms the per-block dot products of
-//    two k16 steps; the per-(row, block) f16 scale is applied in f32 to that
-//    block partial, so scales never round into the operands.
-//  * Split-K across CTAs with deterministic reduction: each CTA writes its
-//    f32 partial to the workspace and the last CTA of a row group (counter in
-//    global memory) sums the partials in split order and applies the
-//    epilogue. Counters are returned to zero by that CTA.
-//  * All weight loads of a warp are issued before griddepcontrol.wait, so
-//    under programmatic dependent launch the weight stream of this GEMV
-//    overlaps the tail of the kernel that produces x.
+//  * A CTA owns 8 sixteen-row tiles (one per consumer warp) and a k-range. A
+//    producer warp streams the CTA's 512-byte (tile, chunk) code slices and
+//    their scales into a ring of shared-memory stages with cp.async.bulk
+//    (TMA bulk copies, one mbarrier per stage with transaction counts), so the
+//    bytes in flight live in shared memory, not registers.
+//  * Consumer warps read their tile's slices with one 16-byte LDS per lane per
+//    chunk — the slice is the lane's tensor-core A fragments — and unpack the
+//    codes in registers to exact bf16 integers (Q4_0: bf16 magic 128+n, one
+//    LOP3 + one SUB.BF16X2 per two codes; Q8_0: f32 magic 2^23+u and one CVT per
+//    two codes).
+//  * The activations x (bf16) of the CTA's k-range are copied unchanged into
+//    shared memory; the k order of each fragment is permuted in the tiled
+//    layout so a lane's x operand is one 8-byte LDS.
+//  * mma.m16n8k16 (bf16 x bf16 -> f32) forms the per-block dot products of two
+//    k16 steps; the per-(row, block) f16 scale multiplies that f32 block
+//    partial, so scales never round into the operands.
+//  * Split-K across CTAs with a deterministic reduction: each CTA writes its
+//    f32 partial and the last CTA of a row group (counter in global memory)
+//    sums the partials in split order and applies the epilogue; the counter is
+//    returned to zero.
+//  * The producer issues weight copies before any dependency on the kernel
+//    that produces x, so under programmatic dependent launch the weight stream
+//    overlaps the producer kernel's tail. Every mbarrier wait is bounded
+//    (clock64); a timeout sets the context's device error word and the kernel
+//    runs to completion.
 #include <algorithm>
+#include <map>
+#include <mutex>
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -39,28 +47,70 @@ using namespace vxb;
 
 namespace {
 
-constexpr int WARPS = 8;
-constexpr int THREADS = WARPS * 32;
-constexpr int ROWS_PER_CTA = WARPS * 16;
+constexpr int CWARPS = 8;                   // consumer warps (one 16-row tile each)
+constexpr int THREADS = (CWARPS + 1) * 32;  // + one producer warp
+constexpr int ROWS_PER_CTA = CWARPS * 16;
+constexpr int STAGES = 3;
+constexpr int CS = 4;  // chunks per stage
+
+template <int FMT>
+struct Geo {
+  static constexpr int CH = FMT == 0 ? 64 : 32;     // k per chunk
+  static constexpr int BPC = CH / 32;               // 32-element blocks per chunk
+  static constexpr int SC_PER_CHUNK = 8 * BPC * 4;  // scale bytes per (tile, chunk)
+  static constexpr int CODE_BYTES = CWARPS * CS * 512;
+  static constexpr int STAGE = CODE_BYTES + CWARPS * CS * SC_PER_CHUNK;
+};
 
 struct GemvArgs {
   const uint8_t *codes;
-  const uint32_t *scales;
+  const uint8_t *scales;
   const uint32_t *hdr;
   const uint16_t *x;
   void *y;
   const float *resid;  // optional residual added in the epilogue (f32 [B, N])
   float *ws;
   unsigned *counters;
-  int N, K, B, n_tiles, n_chunks, n_blocks, S, y_dtype, xs_stride;
+  int *err;
+  int N, K, B, n_tiles, n_chunks, S, y_dtype, xs_stride;
 };
 
-__device__ __forceinline__ uint4 ldg_stream(const void *p) {
-  uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-  return r;
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Bounded wait for the phase of the given parity; false after ~2^31 cycles.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (clock64() - t0 > (1ll << 31)) return false;
+    __nanosleep(32);  // let ready warps issue
+  }
+}
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t m, uint32_t o) {
@@ -105,20 +155,17 @@ __device__ __forceinline__ void q8_word(uint32_t w, uint32_t &lo, uint32_t &hi) 
   hi = pack_bf16x2(c2, c3);
 }
 
-// Q8_0 tiled words (a0..a3 | a4..a7) -> A fragment of exact codes.
 __device__ __forceinline__ void decode_q8(uint32_t w0, uint32_t w1, uint32_t A[4]) {
   q8_word(w0, A[0], A[1]);
   q8_word(w1, A[2], A[3]);
 }
 
-__device__ __forceinline__ void mma_bf16(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1,
-                                         const float c[4]) {
+__device__ __forceinline__ void mma_bf16(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%10,%11,%12,%13};"
-      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
-        "f"(c[3]));
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ float2 decode_scales(uint32_t s, bool subnormal) {
@@ -130,9 +177,10 @@ __device__ __forceinline__ float2 decode_scales(uint32_t s, bool subnormal) {
 }
 
 __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc, int src_bytes) {
-  const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem_dst);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(gsrc), "r"(src_bytes));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc), "r"(src_bytes));
 }
+
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(CWARPS * 32) : "memory"); }
 
 __device__ __forceinline__ void epilogue_store(const GemvArgs &a, int b, int row, float v) {
   const size_t o = (size_t)b * a.N + row;
@@ -144,14 +192,14 @@ __device__ __forceinline__ void epilogue_store(const GemvArgs &a, int b, int row
 }
 
 template <int FMT, int NT>
-__global__ void __launch_bounds__(THREADS, 2) gemv_q_kernel(const GemvArgs a) {
-  constexpr int CH = FMT == 0 ? 64 : 32;  // k per chunk
-  constexpr int BPC = CH / 32;            // blocks per chunk
-  constexpr int BR = 8 * NT;              // padded batch rows
-  constexpr int UNROLL = NT <= 2 ? 12 : 8;  // 512-byte loads in flight per warp
-  extern __shared__ __align__(16) uint8_t smem[];
-  uint16_t *xs = reinterpret_cast<uint16_t *>(smem);
-  float *red = reinterpret_cast<float *>(smem + (size_t)BR * a.xs_stride * 2);  // [BR][ROWS_PER_CTA]
+__global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const GemvArgs a) {
+  using G = Geo<FMT>;
+  constexpr int BR = 8 * NT;  // padded batch rows
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t *stages = smem;
+  uint16_t *xs = reinterpret_cast<uint16_t *>(smem + STAGES * G::STAGE);
+  float *red = reinterpret_cast<float *>(smem);  // reuses the stages after the main loop
+  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES];
   __shared__ int s_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -159,106 +207,148 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_q_kernel(const GemvArgs a) {
   const int c0 = (int)((long long)s * a.n_chunks / a.S);
   const int c1 = (int)((long long)(s + 1) * a.n_chunks / a.S);
   const int nck = c1 - c0;
-  const int k0 = c0 * CH, kc = nck * CH;
-  const int tile = g * WARPS + warp;
-  const bool active = tile < a.n_tiles;
+  const int n_iter = (nck + CS - 1) / CS;
+  const int tiles_here = min(CWARPS, a.n_tiles - g * CWARPS);
 
-  const uint4 *wp = reinterpret_cast<const uint4 *>(a.codes + ((size_t)(active ? tile : 0) * a.n_chunks + c0) * 512) + lane;
-  const uint32_t *sp = a.scales + ((size_t)(active ? tile : 0) * a.n_blocks + (size_t)c0 * BPC) * 8 + (lane >> 2);
-
-  // Issue the first batch of weight loads before waiting on the producer of x.
-  uint4 wv[UNROLL];
-  uint32_t sv[UNROLL][BPC];
-#pragma unroll
-  for (int u = 0; u < UNROLL; u++) {
-    if (active && u < nck) {
-      wv[u] = ldg_stream(wp + (size_t)u * 32);
-#pragma unroll
-      for (int bb = 0; bb < BPC; bb++) sv[u][bb] = __ldg(sp + ((size_t)u * BPC + bb) * 8);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], CWARPS);
     }
-  }
-  const bool subnormal = (__ldg(a.hdr + 1) & TILED_FLAG_SUBNORMAL_SCALES) != 0;
-
-  asm volatile("griddepcontrol.launch_dependents;");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-
-  // Stage x[:, k0:k0+kc] (bf16, unchanged) with 16-byte async copies; rows
-  // past the batch and columns past K are zero-filled.
-  {
-    const int per_row = kc / 8;  // 16-byte pieces per row
-    const int total = BR * per_row;
-    for (int i = threadIdx.x; i < total; i += THREADS) {
-      const int b = i / per_row, p = i % per_row;
-      const int kk = k0 + p * 8;
-      const bool ok = b < a.B && kk < a.K;
-      const uint16_t *src = ok ? a.x + (size_t)b * a.K + kk : a.x;
-      cp_async16(xs + (size_t)b * a.xs_stride + p * 8, src, ok ? 16 : 0);
-    }
-    asm volatile("cp.async.wait_all;" ::: "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
+  if (warp == CWARPS) {
+    // ---------------- producer: weight slices -> shared-memory stages
+    if (lane == 0) {
+      for (int it = 0; it < n_iter; it++) {
+        const int slot = it % STAGES;
+        if (it >= STAGES && !mbar_wait(&empty[slot], ((it / STAGES) & 1) ^ 1)) atomicExch(a.err, 1);
+        const int cb = c0 + it * CS;
+        const int nc = min(CS, c1 - cb);
+        uint8_t *st = stages + slot * G::STAGE;
+        mbar_expect_tx(&full[slot], (uint32_t)(tiles_here * nc * (512 + G::SC_PER_CHUNK)));
+        for (int t = 0; t < tiles_here; t++) {
+          const size_t tc = (size_t)(g * CWARPS + t) * a.n_chunks + cb;
+          bulk_g2s(st + t * CS * 512, a.codes + tc * 512, (uint32_t)nc * 512, &full[slot]);
+          bulk_g2s(st + G::CODE_BYTES + t * CS * G::SC_PER_CHUNK, a.scales + tc * G::SC_PER_CHUNK,
+                   (uint32_t)(nc * G::SC_PER_CHUNK), &full[slot]);
+        }
+      }
+    }
+    asm volatile("griddepcontrol.launch_dependents;");
+    return;
+  }
+
+  // ---------------- consumers
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const bool subnormal = (__ldg(a.hdr + 1) & TILED_FLAG_SUBNORMAL_SCALES) != 0;
+  const int k0 = c0 * G::CH, kc = nck * G::CH;
+  {
+    // x[:, k0:k0+kc] (bf16, unchanged), 16-byte async copies of the live
+    // batch rows only; columns past K are zero-filled
+    const int per_row = kc / 8;
+    const int total = min(a.B, BR) * per_row;
+    for (int i = threadIdx.x; i < total; i += CWARPS * 32) {
+      const int b = i / per_row, p = i % per_row;
+      const int kk = k0 + p * 8;
+      const bool ok = b < a.B && kk < a.K;
+      cp_async16(xs + (size_t)b * a.xs_stride + p * 8, ok ? a.x + (size_t)b * a.K + kk : a.x, ok ? 16 : 0);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  }
+  consumer_sync();
+
   float acc[NT][4];
 #pragma unroll
-  for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-    for (int i = 0; i < 4; i++) acc[nt][i] = 0.f;
+  for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+  const bool active = warp < tiles_here;
+  const uint16_t *xl = xs + (size_t)(lane >> 2) * a.xs_stride + (lane & 3) * 4;
 
-  if (active) {
-    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-    const int q2 = (lane & 3) * 2;
-    const uint16_t *xrow = xs + (size_t)(lane >> 2) * a.xs_stride + q2;
-    // Rolling pipeline: slot u holds chunk ci+u; after taking it, the slot is
-    // refilled with chunk ci+u+UNROLL so UNROLL loads stay in flight.
-    for (int ci = 0; ci < nck; ci += UNROLL) {
+  // Blocks of a stage are processed in groups of GB with independent
+  // accumulators: the first k16 step of every block of the group is issued,
+  // then the second, then the scale FMAs, so consecutive MMAs never depend on
+  // each other and the tensor-core latency overlaps across blocks.
+  constexpr int BLK = CS * G::BPC;                           // blocks per stage
+  constexpr int GB = NT == 1 ? BLK : 2;                      // blocks per group
+  for (int it = 0; it < n_iter; it++) {
+    const int slot = it % STAGES;
+    if (!mbar_wait(&full[slot], (it / STAGES) & 1)) atomicExch(a.err, 1);
+    if (active) {
+      const uint8_t *st = stages + slot * G::STAGE;
+      const uint8_t *cw = st + warp * CS * 512 + lane * 16;
+      const uint8_t *sw = st + G::CODE_BYTES + warp * CS * G::SC_PER_CHUNK + (lane >> 2) * G::BPC * 4;
+      const int nc = min(CS, nck - it * CS);
+      uint4 wv[CS];
+      uint32_t sv[CS][G::BPC];
 #pragma unroll
-      for (int u = 0; u < UNROLL; u++) {
-        if (ci + u < nck) {
-          const uint4 cur = wv[u];
-          uint32_t cs[BPC];
-#pragma unroll
-          for (int bb = 0; bb < BPC; bb++) cs[bb] = sv[u][bb];
-          const int nxt = ci + u + UNROLL;
-          if (nxt < nck) {
-            wv[u] = ldg_stream(wp + (size_t)nxt * 32);
-#pragma unroll
-            for (int bb = 0; bb < BPC; bb++) sv[u][bb] = __ldg(sp + ((size_t)nxt * BPC + bb) * 8);
+      for (int j = 0; j < CS; j++) {
+        if (j < nc) {
+          wv[j] = *reinterpret_cast<const uint4 *>(cw + j * 512);
+          if (G::BPC == 2) {
+            const uint2 t2 = *reinterpret_cast<const uint2 *>(sw + j * G::SC_PER_CHUNK);
+            sv[j][0] = t2.x;
+            sv[j][G::BPC - 1] = t2.y;
+          } else {
+            sv[j][0] = *reinterpret_cast<const uint32_t *>(sw + j * G::SC_PER_CHUNK);
           }
-          const uint32_t *wu = reinterpret_cast<const uint32_t *>(&cur);
+        }
+      }
+      const int kstage = it * CS * G::CH;
 #pragma unroll
-          for (int bb = 0; bb < BPC; bb++) {
-            float t[NT][4];
+      for (int b0 = 0; b0 < BLK; b0 += GB) {
+        float t[GB][NT][4];
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
+        for (int gb = 0; gb < GB; gb++)
+#pragma unroll
+          for (int nt = 0; nt < NT; nt++) t[gb][nt][0] = t[gb][nt][1] = t[gb][nt][2] = t[gb][nt][3] = 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+#pragma unroll
+          for (int gb = 0; gb < GB; gb++) {
+            const int blk = b0 + gb, j = blk / G::BPC, bb = blk % G::BPC;
+            if (j < nc) {
+              const uint32_t *wu = reinterpret_cast<const uint32_t *>(&wv[j]);
               uint32_t A[4];
               if (FMT == 0)
                 decode_q4(wu[bb * 2 + h], A);
               else
                 decode_q8(wu[h * 2], wu[h * 2 + 1], A);
-              const int kk = (ci + u) * CH + (bb * 2 + h) * 16;
+              const int kk = kstage + blk * 32 + h * 16;
 #pragma unroll
               for (int nt = 0; nt < NT; nt++) {
-                const uint16_t *xp = xrow + (size_t)nt * 8 * a.xs_stride + kk;
-                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xp);
-                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(xp + 8);
-                mma_bf16(t[nt], A, b0, b1, h == 0 ? zero : t[nt]);
+                // batch rows past B are not staged: their operand is zero
+                uint2 bx = make_uint2(0u, 0u);
+                if (nt * 8 + (lane >> 2) < a.B) bx = *reinterpret_cast<const uint2 *>(xl + (size_t)nt * 8 * a.xs_stride + kk);
+                mma_bf16(t[gb][nt], A, bx.x, bx.y);
               }
             }
-            const float2 d = decode_scales(cs[bb], subnormal);
+          }
+        }
+#pragma unroll
+        for (int gb = 0; gb < GB; gb++) {
+          const int blk = b0 + gb, j = blk / G::BPC, bb = blk % G::BPC;
+          if (j < nc) {
+            const float2 d = decode_scales(sv[j][bb], subnormal);
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
-              acc[nt][0] = fmaf(d.x, t[nt][0], acc[nt][0]);
-              acc[nt][1] = fmaf(d.x, t[nt][1], acc[nt][1]);
-              acc[nt][2] = fmaf(d.y, t[nt][2], acc[nt][2]);
-              acc[nt][3] = fmaf(d.y, t[nt][3], acc[nt][3]);
+              acc[nt][0] = fmaf(d.x, t[gb][nt][0], acc[nt][0]);
+              acc[nt][1] = fmaf(d.x, t[gb][nt][1], acc[nt][1]);
+              acc[nt][2] = fmaf(d.y, t[gb][nt][2], acc[nt][2]);
+              acc[nt][3] = fmaf(d.y, t[gb][nt][3], acc[nt][3]);
             }
           }
         }
       }
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
   }
 
-  // Fragments -> red[b][row].
+  // every stage has been consumed and no copy is in flight: reuse the ring
+  consumer_sync();
   {
     const int rl = warp * 16 + (lane >> 2);
 #pragma unroll
@@ -270,33 +360,30 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_q_kernel(const GemvArgs a) {
       red[(size_t)(b + 1) * ROWS_PER_CTA + rl + 8] = acc[nt][3];
     }
   }
-  __syncthreads();
+  consumer_sync();
 
   const int row0 = g * ROWS_PER_CTA;
   const int nrows = min(ROWS_PER_CTA, a.N - row0);
   const int nel = a.B * ROWS_PER_CTA;
   if (a.S == 1) {
-    for (int i = threadIdx.x; i < nel; i += THREADS) {
+    for (int i = threadIdx.x; i < nel; i += CWARPS * 32) {
       const int b = i / ROWS_PER_CTA, r = i % ROWS_PER_CTA;
       if (r < nrows) epilogue_store(a, b, row0 + r, red[i]);
     }
     return;
   }
   const size_t NP = (size_t)a.n_tiles * 16;
-  for (int i = threadIdx.x; i < nel; i += THREADS) {
+  for (int i = threadIdx.x; i < nel; i += CWARPS * 32) {
     const int b = i / ROWS_PER_CTA, r = i % ROWS_PER_CTA;
     if (r < nrows) __stcg(a.ws + ((size_t)s * a.B + b) * NP + row0 + r, red[i]);
   }
   __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(a.counters + g, 1u);
-    s_last = prev == (unsigned)(a.S - 1);
-  }
-  __syncthreads();
+  consumer_sync();
+  if (threadIdx.x == 0) s_last = atomicAdd(a.counters + g, 1u) == (unsigned)(a.S - 1);
+  consumer_sync();
   if (!s_last) return;
   __threadfence();
-  for (int i = threadIdx.x; i < nel; i += THREADS) {
+  for (int i = threadIdx.x; i < nel; i += CWARPS * 32) {
     const int b = i / ROWS_PER_CTA, r = i % ROWS_PER_CTA;
     if (r >= nrows) continue;
     float v = 0.f;
@@ -304,6 +391,50 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_q_kernel(const GemvArgs a) {
     epilogue_store(a, b, row0 + r, v);
   }
   if (threadIdx.x == 0) a.counters[g] = 0u;
+}
+
+size_t smem_bytes_t(int fmt, int NT, int batch, int xs_stride) {
+  const size_t st = (size_t)STAGES * (fmt == VXB_Q4_0 ? Geo<0>::STAGE : Geo<1>::STAGE);
+  const size_t red = (size_t)8 * NT * ROWS_PER_CTA * 4;
+  return std::max(st, red) + (size_t)std::min(batch, 8 * NT) * xs_stride * 2;
+}
+
+int xs_stride_for(int kc_max) { return kc_max + 16; }  // stride/2 = 8 (mod 32): conflict-free 8-byte loads
+
+// Resident CTAs per SM for an instantiation at a shared-memory size (cached).
+template <int FMT, int NT>
+int occupancy_t(size_t smem) {
+  static std::mutex mu;
+  static std::map<size_t, int> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(smem);
+  if (it != cache.end()) return it->second;
+  auto kfn = gemv_q_kernel<FMT, NT>;
+  int n = 1;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kfn, THREADS, smem) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    n = 1;
+  }
+  cache[smem] = n;
+  return n;
+}
+
+int occupancy(int fmt, int NT, size_t smem) {
+  if (fmt == VXB_Q4_0) {
+    switch (NT) {
+      case 1: return occupancy_t<0, 1>(smem);
+      case 2: return occupancy_t<0, 2>(smem);
+      case 3: return occupancy_t<0, 3>(smem);
+      default: return occupancy_t<0, 4>(smem);
+    }
+  }
+  switch (NT) {
+    case 1: return occupancy_t<1, 1>(smem);
+    case 2: return occupancy_t<1, 2>(smem);
+    case 3: return occupancy_t<1, 3>(smem);
+    default: return occupancy_t<1, 4>(smem);
+  }
 }
 
 template <int FMT, int NT>
@@ -337,22 +468,25 @@ size_t gemv_smem_bytes(int fmt, int N, int K, int batch, int S) {
   const TiledGeom g = tiled_geom(fmt, N, K);
   const int NT = (batch + 7) / 8;
   const int kc_max = (g.n_chunks + S - 1) / S * g.chunk;
-  return (size_t)8 * NT * (kc_max + 8) * 2 + (size_t)8 * NT * ROWS_PER_CTA * 4;
+  return smem_bytes_t(fmt, NT, batch, xs_stride_for(kc_max));
 }
 
 GemvPlan gemv_plan(const vxb_ctx *ctx, int fmt, int N, int K, int batch) {
   const TiledGeom g = tiled_geom(fmt, N, K);
-  const int row_groups = (g.n_tiles + WARPS - 1) / WARPS;
+  const int row_groups = (g.n_tiles + CWARPS - 1) / CWARPS;
   const int sms = ctx->num_sms > 0 ? ctx->num_sms : 148;
-  const int slots = 2 * sms;  // resident CTAs (register-limited to two per SM)
-  // Each CTA streams at a latency-bound rate, so the run time is the number of
-  // CTA waves times the duration of one CTA (proportional to 1/S): pick the
-  // split count that minimises waves/S, with a small cost per extra wave.
+  // Each CTA streams at a rate set by its stage ring, so the run time is the
+  // number of CTA waves times the duration of one CTA (proportional to 1/S):
+  // pick the split count that minimises waves/S, with a small cost per wave.
+  // Resident CTAs per SM come from the occupancy calculator.
   int best = 1;
   double best_cost = 1e30;
-  const int smax = std::min(16, std::max(1, g.n_chunks / 2));
+  const int smax = std::min(32, std::max(1, g.n_chunks / 2));
   for (int S = 1; S <= smax; S++) {
-    if (gemv_smem_bytes(fmt, N, K, batch, S) > 96 * 1024) continue;
+    const size_t sm = gemv_smem_bytes(fmt, N, K, batch, S);
+    if (sm > 200 * 1024) continue;
+    const int per_sm = occupancy(fmt, (batch + 7) / 8, sm);
+    const int slots = per_sm * sms;
     const int waves = (row_groups * S + slots - 1) / slots;
     const double cost = (double)waves / S + 0.03 * waves;
     if (cost < best_cost - 1e-9) {
@@ -360,10 +494,8 @@ GemvPlan gemv_plan(const vxb_ctx *ctx, int fmt, int N, int K, int batch) {
       best = S;
     }
   }
-  int S = best;
-  while (S < g.n_chunks && gemv_smem_bytes(fmt, N, K, batch, S) > 96 * 1024) S++;
   GemvPlan p;
-  p.S = S;
+  p.S = best;
   p.pdl = true;
   return p;
 }
@@ -381,31 +513,30 @@ int gemv_launch(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const 
   const TiledGeom g = tiled_geom(fmt, N, K);
   GemvPlan p = plan_override ? *plan_override : gemv_plan(ctx, fmt, N, K, batch);
   const int NT = (batch + 7) / 8;
-  const int row_groups = (g.n_tiles + WARPS - 1) / WARPS;
-  if (p.S > 1) {
-    if (int rc = ws_reserve(ctx, (size_t)p.S * batch * g.N_pad * sizeof(float), (size_t)row_groups)) return rc;
-  }
+  const int row_groups = (g.n_tiles + CWARPS - 1) / CWARPS;
+  const size_t ws_bytes = p.S > 1 ? (size_t)p.S * batch * g.N_pad * sizeof(float) : 0;
+  if (int rc = ws_reserve(ctx, ws_bytes, (size_t)row_groups)) return rc;
   GemvArgs a;
   const uint8_t *base = (const uint8_t *)d_tiled;
   a.codes = base + g.codes_off;
-  a.scales = (const uint32_t *)(base + g.codes_off + g.codes_bytes);
+  a.scales = base + g.codes_off + g.codes_bytes;
   a.hdr = (const uint32_t *)base;
   a.x = d_x;
   a.y = d_y;
   a.resid = d_resid;
   a.ws = (float *)ctx->ws;
   a.counters = ctx->counters;
+  a.err = ctx->d_err;
   a.N = N;
   a.K = K;
   a.B = batch;
   a.n_tiles = g.n_tiles;
   a.n_chunks = g.n_chunks;
-  a.n_blocks = g.n_blocks;
   a.S = p.S;
   a.y_dtype = y_dtype;
   const int kc_max = (g.n_chunks + p.S - 1) / p.S * g.chunk;
-  a.xs_stride = kc_max + 8;
-  const size_t smem = gemv_smem_bytes(fmt, N, K, batch, p.S);
+  a.xs_stride = xs_stride_for(kc_max);
+  const size_t smem = smem_bytes_t(fmt, NT, batch, a.xs_stride);
   if (smem > 200 * 1024) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q: split plan needs %zu bytes of shared memory", smem);
   dim3 grid(row_groups, p.S);
   cudaStream_t st = (cudaStream_t)stream;

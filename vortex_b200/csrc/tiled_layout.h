@@ -8,11 +8,15 @@
 //                       k16 step, nibbles (value = code + 8) at bit positions
 //                       a0@0 a2@4 a4@8 a6@12 a1@16 a3@20 a5@24 a7@28;
 //                       Q8_0 -> 2 u32 per k16 step, int8 codes a0..a3 | a4..a7.
-//                       (a_i as in the PTX fragment layout: a0/a1 row g, cols
-//                       2q,2q+1; a2/a3 row g+8; a4..a7 the same at cols +8, with
-//                       g = lane/4, q = lane%4.)
-//   scales              per tile t, per 32-element block b: 8 u32, entry i =
-//                       f16 scale of row 16t+i (low half) | row 16t+i+8 (high).
+//                       (a_i as in the PTX fragment layout: a0/a1 row g, a2/a3
+//                       row g+8, a4..a7 the same rows, with g = lane/4.) The
+//                       k order inside a step is permuted: the fragment columns
+//                       {2q, 2q+1, 2q+8, 2q+9} of lane q (q = lane%4) hold the
+//                       matrix columns {4q, 4q+1, 4q+2, 4q+3}, so the lane's
+//                       activation operand is 8 contiguous bytes of x.
+//   scales              per tile t, per chunk c, per row pair i (0..7), per
+//                       block of the chunk: u32 = f16 scale of row 16t+i (low
+//                       half) | row 16t+i+8 (high half).
 // Rows beyond N and columns beyond K are padding with code 0 and scale 0.
 #pragma once
 

@@ -23,6 +23,8 @@ struct vxb_ctx {
   size_t ws_bytes = 0;
   unsigned *counters = nullptr;  // zero-initialised; kernels restore zero after use
   size_t n_counters = 0;
+  // device error word: kernels whose bounded waits time out set it to nonzero
+  int *d_err = nullptr;
 };
 
 namespace vxb {
