@@ -123,6 +123,16 @@ int vxb_untile_weights(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K,
 /* ------------------------------------------------------------------------ */
 int vxb_gemv_q(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const uint16_t *d_x,
                int batch, int y_dtype, void *d_y, void *stream);
+/* The same GEMV for callers that cannot allocate device memory (no
+ * counterpart in the reference: it exists for embedders whose runtime owns
+ * all device memory, or that must not add allocations mid-run). Scratch lives
+ * in a fixed 8 MiB + 64 KiB array in the library, held on every GPU that
+ * loads it; limit: batch * round_up(N, 16) <= 1048576, else VXB_EINVAL. Calls
+ * share that array: calls that overlap on the GPU race. The first call on a
+ * device resolves the array's address (make it before any stream capture).
+ * Allocates nothing: no cudaMalloc / cudaFree. */
+int vxb_gemv_q_static(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const uint16_t *d_x,
+                      int batch, int y_dtype, void *d_y, void *stream);
 
 /* ------------------------------------------------------------------------ */
 /* Paged KV cache. Replaces PagedKVCache (src/kv_cache.rs:29-93) and the     */

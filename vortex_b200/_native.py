@@ -66,6 +66,7 @@ SIGNATURES = {
     "vxb_tile_weights": (_I, [_P, _I, _P, _I, _I, _P, _P]),
     "vxb_untile_weights": (_I, [_P, _I, _P, _I, _I, _P, _P]),
     "vxb_gemv_q": (_I, [_P, _I, _P, _I, _I, _P, _I, _I, _P, _P]),
+    "vxb_gemv_q_static": (_I, [_P, _I, _P, _I, _I, _P, _I, _I, _P, _P]),
     "vxb_kv_create": (_I, [_P, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_P)]),
     "vxb_kv_destroy": (_I, [_P]),
     "vxb_kv_append": (_I, [_P, _I, _I, _P, _P, _P, _P]),

@@ -566,3 +566,116 @@ VXB_API int vxb_gemv_q(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K,
   if (!ctx) return set_error(nullptr, VXB_EINVAL, "vxb_gemv_q: null context");
   return gemv_launch(ctx, fmt, d_tiled, N, K, d_x, batch, y_dtype, d_y, nullptr, stream, nullptr);
 }
+
+// ---------------------------------------------------------------------------
+// GEMV without device allocation.
+//
+// vxb_gemv_q keeps its split-K partial sums, reduction counters and error word
+// in the context workspace, which it grows with cudaMalloc on first use. Some
+// callers cannot allow that: an embedding runtime that owns all device memory
+// through its own arena, a caller that must not add allocations while other
+// work holds a fixed memory budget, or code paths where a cudaMalloc would
+// synchronize the device. vxb_gemv_q_static computes the same product with
+// that scratch in the fixed array below instead. The caller still provides
+// the weights, activations and output. Every GPU that loads the library holds
+// the array (8 MiB of partials + 64 KiB of counters + the error word) until
+// the process exits. All calls on a device share it, and it keeps the last
+// call's contents: the counters are cleared before each launch, and calls that
+// overlap on the GPU (different streams without ordering) race on it.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kStaticPartialBytes = (size_t)8 << 20;  // f32 split-K partials
+constexpr int kStaticCounters = 16384;                   // one per 128-row group
+constexpr size_t kStaticBytes = kStaticPartialBytes + (size_t)kStaticCounters * 4 + 256;
+
+__device__ __align__(256) uint8_t g_static_scratch[kStaticBytes];
+
+std::mutex g_static_mu;
+uint8_t *g_static_addr[64] = {nullptr};
+
+// Device address of g_static_scratch on the context's device (resolved once
+// per device with that device current; the symbol's name in host code is a
+// host-side stand-in, not a device address).
+int static_scratch(vxb_ctx *ctx, uint8_t **out) {
+  if (ctx->device < 0 || ctx->device >= 64) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q_static: device %d", ctx->device);
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (!g_static_addr[ctx->device]) {
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaGetSymbolAddress(g_static_scratch)");
+    g_static_addr[ctx->device] = (uint8_t *)p;
+  }
+  *out = g_static_addr[ctx->device];
+  return VXB_OK;
+}
+
+}  // namespace
+
+VXB_API int vxb_gemv_q_static(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const uint16_t *d_x,
+                              int batch, int y_dtype, void *d_y, void *stream) {
+  if (!ctx) return set_error(nullptr, VXB_EINVAL, "vxb_gemv_q_static: null context");
+  if (fmt != VXB_Q4_0 && fmt != VXB_Q8_0) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q_static: unknown format %d", fmt);
+  if (N <= 0 || K <= 0 || K % 32) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q_static: bad shape N=%d K=%d", N, K);
+  if (batch < 1 || batch > 32) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q_static: batch %d outside 1..32", batch);
+  if (y_dtype != VXB_F32 && y_dtype != VXB_BF16)
+    return set_error(ctx, VXB_EINVAL, "vxb_gemv_q_static: y_dtype must be F32 or BF16");
+  if (!d_tiled || !d_x || !d_y) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q_static: null pointer");
+  if (((uintptr_t)d_tiled) % 256 || ((uintptr_t)d_x) % 16)
+    return set_error(ctx, VXB_EINVAL, "vxb_gemv_q_static: weights must be 256-byte and activations 16-byte aligned");
+  const TiledGeom g = tiled_geom(fmt, N, K);
+  const size_t per_split = (size_t)batch * g.N_pad * sizeof(float);
+  const int row_groups = (g.n_tiles + CWARPS - 1) / CWARPS;
+  // the fixed array must hold the partials of at least two k-splits
+  if (per_split * 2 > kStaticPartialBytes || row_groups > kStaticCounters)
+    return set_error(ctx, VXB_EINVAL,
+                     "vxb_gemv_q_static: batch * N = %d * %d exceeds the static scratch limit "
+                     "(batch * round_up(N, 16) <= %zu)",
+                     batch, N, kStaticPartialBytes / (2 * sizeof(float)));
+  if (int rc = use_device(ctx)) return rc;
+  uint8_t *base = nullptr;
+  if (int rc = static_scratch(ctx, &base)) return rc;
+  GemvPlan p = gemv_plan(ctx, fmt, N, K, batch);
+  p.S = std::max(1, std::min<int>(p.S, (int)(kStaticPartialBytes / per_split)));
+  GemvArgs a;
+  const uint8_t *wb = (const uint8_t *)d_tiled;
+  a.codes = wb + g.codes_off;
+  a.scales = wb + g.codes_off + g.codes_bytes;
+  a.hdr = (const uint32_t *)wb;
+  a.x = d_x;
+  a.y = d_y;
+  a.resid = nullptr;
+  a.ws = (float *)base;
+  a.counters = (unsigned *)(base + kStaticPartialBytes);
+  a.err = (int *)(base + kStaticPartialBytes + (size_t)kStaticCounters * 4);
+  a.N = N;
+  a.K = K;
+  a.B = batch;
+  a.n_tiles = g.n_tiles;
+  a.n_chunks = g.n_chunks;
+  a.S = p.S;
+  a.y_dtype = y_dtype;
+  const int kc_max = (g.n_chunks + p.S - 1) / p.S * g.chunk;
+  a.xs_stride = xs_stride_for(kc_max);
+  const int NT = (batch + 7) / 8;
+  const size_t smem = smem_bytes_t(fmt, NT, batch, a.xs_stride);
+  if (smem > 200 * 1024) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q_static: plan needs %zu bytes of shared memory", smem);
+  cudaStream_t st = (cudaStream_t)stream;
+  // counters must start at zero (a previous call that stopped early could have left them set)
+  VXB_CUDA_TRY(ctx, cudaMemsetAsync(a.counters, 0, (size_t)row_groups * 4, st));
+  dim3 grid(row_groups, p.S);
+  if (fmt == VXB_Q4_0) {
+    switch (NT) {
+      case 1: return launch_t<0, 1>(ctx, a, grid, smem, st, false);
+      case 2: return launch_t<0, 2>(ctx, a, grid, smem, st, false);
+      case 3: return launch_t<0, 3>(ctx, a, grid, smem, st, false);
+      default: return launch_t<0, 4>(ctx, a, grid, smem, st, false);
+    }
+  }
+  switch (NT) {
+    case 1: return launch_t<1, 1>(ctx, a, grid, smem, st, false);
+    case 2: return launch_t<1, 2>(ctx, a, grid, smem, st, false);
+    case 3: return launch_t<1, 3>(ctx, a, grid, smem, st, false);
+    default: return launch_t<1, 4>(ctx, a, grid, smem, st, false);
+  }
+}
