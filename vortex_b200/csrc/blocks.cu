@@ -186,7 +186,7 @@ __device__ __forceinline__ uint32_t q8_byte(const uint8_t *blocks, int N, int K,
 // source rows of the part, which land at tiles [tile0, tile0 + ceil(N/16)) of
 // a layout of geometry g (the whole, possibly fused, matrix).
 __global__ void tile_codes_kernel(const uint8_t *__restrict__ blocks, int fmt, int N, int K, TiledGeom g, int tile0,
-                                  uint32_t *__restrict__ codes) {
+                                  uint8_t *__restrict__ tiled) {
   const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   const size_t total = (size_t)((N + 15) / 16) * g.n_chunks * 128;
   if (idx >= total) return;
@@ -198,7 +198,6 @@ __global__ void tile_codes_kernel(const uint8_t *__restrict__ blocks, int fmt, i
   // k-permuted fragments: lane q of a k16 step holds columns 4q..4q+3, so the
   // activation operand of the lane is 8 contiguous bytes
   const int r0 = t * 16 + l / 4, r1 = r0 + 8, k4 = (l % 4) * 4;
-  codes += (size_t)tile0 * g.n_chunks * 128;
   uint32_t w = 0;
   if (fmt == VXB_Q4_0) {
     const int kb = (4 * c + j) * 16 + k4;
@@ -207,17 +206,19 @@ __global__ void tile_codes_kernel(const uint8_t *__restrict__ blocks, int fmt, i
         (q4_nibble(blocks, N, K, r0, kb + 1) << 16) | (q4_nibble(blocks, N, K, r1, kb + 1) << 20) |
         (q4_nibble(blocks, N, K, r0, kb + 3) << 24) | (q4_nibble(blocks, N, K, r1, kb + 3) << 28);
   } else {
+    // int8 codes are stored offset by 128 (q ^ 0x80)
     const int kb = (2 * c + j / 2) * 16 + k4 + ((j & 1) ? 2 : 0);
     w = q8_byte(blocks, N, K, r0, kb) | (q8_byte(blocks, N, K, r0, kb + 1) << 8) |
         (q8_byte(blocks, N, K, r1, kb) << 16) | (q8_byte(blocks, N, K, r1, kb + 1) << 24);
+    w ^= 0x80808080u;
   }
-  codes[idx] = w;
+  *reinterpret_cast<uint32_t *>(tiled + tiled_codes_at(g, tile0 + t, c) + l * 16 + j * 4) = w;
 }
 
 // One thread per u32 of the part's scales, ordered (tile, chunk, i, block of
 // the chunk): entry = f16 scale of row 16t+i (low half) | row 16t+i+8 (high).
 __global__ void tile_scales_kernel(const uint8_t *__restrict__ blocks, int fmt, int N, int K, TiledGeom g, int tile0,
-                                   uint32_t *__restrict__ scales, uint32_t *__restrict__ hdr) {
+                                   uint8_t *__restrict__ tiled) {
   const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   const size_t total = (size_t)((N + 15) / 16) * g.n_blocks * 8;
   if (idx >= total) return;
@@ -228,7 +229,6 @@ __global__ void tile_scales_kernel(const uint8_t *__restrict__ blocks, int fmt, 
   const int c = (int)(tc % g.n_chunks);
   const int t = (int)(tc / g.n_chunks);
   const int b = c * bpc + bb;
-  scales += (size_t)tile0 * g.n_blocks * 8;
   const size_t blk_bytes = fmt == VXB_Q4_0 ? 18 : 34;
   uint32_t out = 0;
   bool sub = false;
@@ -243,8 +243,8 @@ __global__ void tile_scales_kernel(const uint8_t *__restrict__ blocks, int fmt, 
     }
     out |= s << (16 * h);
   }
-  scales[idx] = out;
-  if (sub) atomicOr(hdr + 1, TILED_FLAG_SUBNORMAL_SCALES);
+  *reinterpret_cast<uint32_t *>(tiled + tiled_scales_at(g, tile0 + t, c) + (i * bpc + bb) * 4) = out;
+  if (sub) atomicOr(reinterpret_cast<uint32_t *>(tiled) + 1, TILED_FLAG_SUBNORMAL_SCALES);
 }
 
 // One thread per (row, block): rebuild the GGUF block from the tiled layout.
@@ -255,10 +255,10 @@ __global__ void untile_kernel(const uint8_t *__restrict__ tiled, int fmt, int N,
   if (idx >= (size_t)N * nbk) return;
   const int r = (int)(idx / nbk), b = (int)(idx % nbk);
   const int t = r / 16, ri = r % 16;
-  const uint32_t *sc = (const uint32_t *)(tiled + g.codes_off + g.codes_bytes);
   const int bpc = g.chunk / 32;
-  const uint32_t s = sc[(((size_t)t * g.n_chunks + b / bpc) * 8 + (ri & 7)) * bpc + b % bpc] >> (ri >= 8 ? 16 : 0);
-  const uint8_t *codes = tiled + g.codes_off;
+  const uint32_t s =
+      *reinterpret_cast<const uint32_t *>(tiled + tiled_scales_at(g, t, b / bpc) + ((ri & 7) * bpc + b % bpc) * 4) >>
+      (ri >= 8 ? 16 : 0);
   if (fmt == VXB_Q4_0) {
     uint8_t *o = blocks + idx * 18;
     o[0] = (uint8_t)(s & 0xFF);
@@ -271,7 +271,7 @@ __global__ void untile_kernel(const uint8_t *__restrict__ tiled, int fmt, int N,
         const int c = step / 4, j = step % 4;
         const int jj = kk & 3, lane = (ri & 7) * 4 + kk / 4;
         const int pos = (ri >= 8 ? 4 : 0) + (jj >= 2 ? 8 : 0) + ((jj & 1) ? 16 : 0);
-        const uint32_t w = ((const uint32_t *)codes)[(((size_t)t * g.n_chunks + c) * 32 + lane) * 4 + j];
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(tiled + tiled_codes_at(g, t, c) + lane * 16 + j * 4);
         nib[e] = (w >> pos) & 0xF;
       }
       o[2 + jb] = (uint8_t)(nib[0] | (nib[1] << 4));
@@ -287,7 +287,7 @@ __global__ void untile_kernel(const uint8_t *__restrict__ tiled, int fmt, int N,
       const int jj = kk & 3, lane = (ri & 7) * 4 + kk / 4;
       const int j = (step % 2) * 2 + (jj >= 2 ? 1 : 0);
       const int byte = (ri >= 8 ? 2 : 0) + (jj & 1);
-      o[2 + e] = codes[((((size_t)t * g.n_chunks + c) * 32 + lane) * 4 + j) * 4 + byte];
+      o[2 + e] = tiled[tiled_codes_at(g, t, c) + lane * 16 + j * 4 + byte] ^ 0x80;
     }
   }
 }
@@ -386,7 +386,8 @@ namespace vxb {
 int tile_header(vxb_ctx *ctx, int fmt, int N, int K, void *d_tiled, cudaStream_t st) {
   const TiledGeom g = tiled_geom(fmt, N, K);
   uint32_t *hdr = (uint32_t *)d_tiled;
-  VXB_CUDA_TRY(ctx, cudaMemsetAsync(hdr, 0, g.codes_off, st));
+  // padding rows of the last 128-row group stay zero (code 0, scale 0)
+  VXB_CUDA_TRY(ctx, cudaMemsetAsync(hdr, 0, g.total_bytes, st));
   tile_header_kernel<<<1, 1, 0, st>>>(hdr, fmt, N, K);
   return launch_check(ctx, "tile_header_kernel");
 }
@@ -399,11 +400,9 @@ int tile_part(vxb_ctx *ctx, int fmt, const uint8_t *d_blocks, int nrows, int K, 
   uint8_t *base = (uint8_t *)d_tiled;
   const int ntiles = (nrows + 15) / 16;
   const size_t nc = (size_t)ntiles * g.n_chunks * 128, ns = (size_t)ntiles * g.n_blocks * 8;
-  tile_codes_kernel<<<(unsigned)((nc + 255) / 256), 256, 0, st>>>(d_blocks, fmt, nrows, K, g, row0 / 16,
-                                                                    (uint32_t *)(base + g.codes_off));
+  tile_codes_kernel<<<(unsigned)((nc + 255) / 256), 256, 0, st>>>(d_blocks, fmt, nrows, K, g, row0 / 16, base);
   if (int rc = launch_check(ctx, "tile_codes_kernel")) return rc;
-  tile_scales_kernel<<<(unsigned)((ns + 255) / 256), 256, 0, st>>>(
-      d_blocks, fmt, nrows, K, g, row0 / 16, (uint32_t *)(base + g.codes_off + g.codes_bytes), (uint32_t *)base);
+  tile_scales_kernel<<<(unsigned)((ns + 255) / 256), 256, 0, st>>>(d_blocks, fmt, nrows, K, g, row0 / 16, base);
   return launch_check(ctx, "tile_scales_kernel");
 }
 

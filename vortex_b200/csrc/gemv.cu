@@ -7,22 +7,26 @@
 // (src/transformer.rs:332-352) at decode batch sizes.
 //
 // Design (HBM-bound streaming):
-//  * A CTA owns 8 sixteen-row tiles (one per consumer warp) and a k-range. A
-//    producer warp streams the CTA's 512-byte (tile, chunk) code slices and
-//    their scales into a ring of shared-memory stages with cp.async.bulk
-//    (TMA bulk copies, one mbarrier per stage with transaction counts), so the
-//    bytes in flight live in shared memory, not registers.
-//  * Consumer warps read their tile's slices with one 16-byte LDS per lane per
-//    chunk — the slice is the lane's tensor-core A fragments — and unpack the
-//    codes in registers to exact bf16 integers (Q4_0: bf16 magic 128+n, one
-//    LOP3 + one SUB.BF16X2 per two codes; Q8_0: f32 magic 2^23+u and one CVT per
-//    two codes).
-//  * The activations x (bf16) of the CTA's k-range are copied unchanged into
-//    shared memory; the k order of each fragment is permuted in the tiled
-//    layout so a lane's x operand is one 8-byte LDS.
-//  * mma.m16n8k16 (bf16 x bf16 -> f32) forms the per-block dot products of two
-//    k16 steps; the per-(row, block) f16 scale multiplies that f32 block
-//    partial, so scales never round into the operands.
+//  * A CTA owns one 128-row group (8 sixteen-row tiles, one per consumer warp)
+//    and a k-range. The tiled layout stores every (row group, k-chunk) as one
+//    contiguous record of codes and scales, so a producer warp moves a whole
+//    stage (CS records) with a single cp.async.bulk copy into a ring of
+//    shared-memory stages (one mbarrier per stage with a transaction count).
+//  * Consumer warps read their tile's codes with one 16-byte LDS per lane per
+//    chunk (the slice is the lane's m16n8k16 A fragments) and turn them into
+//    exact f16 integers: Q4_0 nibbles by LOP3 with the f16 magic 1024 (a nibble
+//    at bits 0-3 gives 1024+n, at bits 4-7 1024+16n) and one HSUB2 per two
+//    codes; Q8_0 bytes (stored as q+128) by one PRMT with the magic byte and one
+//    HSUB2 per two codes.
+//  * The activations of the CTA's k-range are staged in shared memory as f16,
+//    each batch column multiplied by a power of two 2^-e chosen from its largest
+//    magnitude (max |x| * 2^-e in [2^14, 2^15)), so the bf16 -> f16 conversion is
+//    exact for every element within 2^-28 of the column maximum and nothing
+//    overflows; the f32 result is multiplied back by 2^e.
+//  * mma.m16n8k16 (f16 x f16 -> f32) forms the per-block dot products; the
+//    per-(row, block) f16 scale multiplies that f32 block partial with packed
+//    f32x2 FMAs, so scales never round into the operands (Q4_0 rows decoded as
+//    16q carry 1/16 in their scale, an exact factor).
 //  * Split-K across CTAs with a deterministic reduction: each CTA writes its
 //    f32 partial and the last CTA of a row group (counter in global memory)
 //    sums the partials in split order and applies the epilogue; the counter is
@@ -36,6 +40,7 @@
 #include <map>
 #include <mutex>
 
+#include <cooperative_groups.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -44,6 +49,7 @@
 #include "vxb_internal.h"
 
 using namespace vxb;
+namespace cg = cooperative_groups;
 
 namespace {
 
@@ -51,20 +57,21 @@ constexpr int CWARPS = 8;                   // consumer warps (one 16-row tile e
 constexpr int THREADS = (CWARPS + 1) * 32;  // + one producer warp
 constexpr int ROWS_PER_CTA = CWARPS * 16;
 constexpr int STAGES = 3;
-constexpr int CS = 4;  // chunks per stage
+constexpr int CS = 4;  // chunks (records) per stage
+constexpr int kMaxClusterSplits = 8;  // portable cluster size
 
 template <int FMT>
 struct Geo {
   static constexpr int CH = FMT == 0 ? 64 : 32;     // k per chunk
   static constexpr int BPC = CH / 32;               // 32-element blocks per chunk
-  static constexpr int SC_PER_CHUNK = 8 * BPC * 4;  // scale bytes per (tile, chunk)
-  static constexpr int CODE_BYTES = CWARPS * CS * 512;
-  static constexpr int STAGE = CODE_BYTES + CWARPS * CS * SC_PER_CHUNK;
+  static constexpr int SCT = 8 * BPC * 4;           // scale bytes of one tile in a record
+  static constexpr int REC = CWARPS * (512 + SCT);  // bytes of one (row group, chunk) record
+  static constexpr int STAGE = CS * REC;
 };
+static_assert(Geo<0>::REC == 8 * (512 + 64) && Geo<1>::REC == 8 * (512 + 32), "record size");
 
 struct GemvArgs {
-  const uint8_t *codes;
-  const uint8_t *scales;
+  const uint8_t *records;
   const uint32_t *hdr;
   const uint16_t *x;
   void *y;
@@ -72,7 +79,8 @@ struct GemvArgs {
   float *ws;
   unsigned *counters;
   int *err;
-  int N, K, B, n_tiles, n_chunks, S, y_dtype, xs_stride;
+  int N, K, B, NP, n_chunks, S, y_dtype, xs_stride;
+  int cluster;  // 1: the S splits of a row group are one thread-block cluster
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -102,7 +110,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     if (done) return true;
     if (clock64() - t0 > (1ll << 31)) return false;
-    __nanosleep(32);  // let ready warps issue
   }
 }
 
@@ -119,53 +126,47 @@ __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t m, uint32_t 
   return d;
 }
 
-__device__ __forceinline__ uint32_t bsub2(uint32_t a, uint32_t b) {
+__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
   uint32_t d;
-  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
 
-// Q4_0 tiled word -> A fragment {a0a1, a2a3, a4a5, a6a7} of exact codes.
-// Nibble n at bits 0-3 / 16-19 of (w >> 4i): bf16 0x4300|n = 128+n, minus 136.
+// Q4_0 tiled word -> A fragment {a0a1, a2a3, a4a5, a6a7}. Rows g (a0a1, a4a5)
+// come out as the exact codes q, rows g+8 (a2a3, a6a7) as 16q.
 __device__ __forceinline__ void decode_q4(uint32_t w, uint32_t A[4]) {
-  const uint32_t M = 0x43004300u;    // bf16 128.0 x2
-  const uint32_t SUB = 0x43084308u;  // bf16 136.0 x2
-  A[0] = bsub2(lop_and_or(w, 0x000F000Fu, M), SUB);
-  A[1] = bsub2(lop_and_or(w >> 4, 0x000F000Fu, M), SUB);
-  A[2] = bsub2(lop_and_or(w >> 8, 0x000F000Fu, M), SUB);
-  A[3] = bsub2(lop_and_or(w >> 12, 0x000F000Fu, M), SUB);
+  const uint32_t M = 0x64006400u;       // f16 1024.0 x2
+  const uint32_t SUB_LO = 0x64086408u;  // 1024 + 8
+  const uint32_t SUB_HI = 0x64806480u;  // 1024 + 16 * 8
+  const uint32_t w8 = w >> 8;
+  A[0] = hsub2(lop_and_or(w, 0x000F000Fu, M), SUB_LO);
+  A[1] = hsub2(lop_and_or(w, 0x00F000F0u, M), SUB_HI);
+  A[2] = hsub2(lop_and_or(w8, 0x000F000Fu, M), SUB_LO);
+  A[3] = hsub2(lop_and_or(w8, 0x00F000F0u, M), SUB_HI);
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  uint32_t d;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-  return d;
-}
-
-// Four int8 codes of one word -> two bf16x2 (exact): byte b -> f32 2^23 + (b^0x80)
-// via PRMT, minus 2^23 + 128.
-__device__ __forceinline__ void q8_word(uint32_t w, uint32_t &lo, uint32_t &hi) {
-  const uint32_t u = w ^ 0x80808080u;
-  const float B = 8388736.0f;  // 2^23 + 128
-  const float c0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)) - B;
-  const float c1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441)) - B;
-  const float c2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)) - B;
-  const float c3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443)) - B;
-  lo = pack_bf16x2(c0, c1);
-  hi = pack_bf16x2(c2, c3);
-}
-
+// Q8_0 tiled words (bytes q+128) -> A fragment of exact codes: f16 0x64uu is
+// 1024 + u, minus 1152.
 __device__ __forceinline__ void decode_q8(uint32_t w0, uint32_t w1, uint32_t A[4]) {
-  q8_word(w0, A[0], A[1]);
-  q8_word(w1, A[2], A[3]);
+  const uint32_t M = 0x64646464u;
+  const uint32_t SUB = 0x64806480u;  // 1024 + 128
+  A[0] = hsub2(__byte_perm(w0, M, 0x4140), SUB);
+  A[1] = hsub2(__byte_perm(w0, M, 0x4342), SUB);
+  A[2] = hsub2(__byte_perm(w1, M, 0x4140), SUB);
+  A[3] = hsub2(__byte_perm(w1, M, 0x4342), SUB);
 }
 
-__device__ __forceinline__ void mma_bf16(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
+__device__ __forceinline__ void mma_f16(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// the same with a zero accumulator input
+__device__ __forceinline__ void mma_f16_z(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
 }
 
 __device__ __forceinline__ float2 decode_scales(uint32_t s, bool subnormal) {
@@ -176,8 +177,26 @@ __device__ __forceinline__ float2 decode_scales(uint32_t s, bool subnormal) {
   return make_float2(ref_f16_to_f32(s & 0xFFFFu), ref_f16_to_f32(s >> 16));
 }
 
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+// v * 2^e for |e| <= 252: two exact power-of-two factors (exact unless the
+// result leaves the f32 range)
+__device__ __forceinline__ float mul_pow2(float v, int e) {
+  const int e1 = e / 2, e2 = e - e1;
+  return v * __int_as_float((127 + e1) << 23) * __int_as_float((127 + e2) << 23);
+}
+
 __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc, int src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc), "r"(src_bytes));
+}
+
+// all threads of every CTA of the cluster (release / acquire)
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(CWARPS * 32) : "memory"); }
@@ -191,6 +210,90 @@ __device__ __forceinline__ void epilogue_store(const GemvArgs &a, int b, int row
     ((float *)a.y)[o] = v;
 }
 
+// Consumer main loop over n_iter full stages: acc[nt][0] = rows g, acc[nt][1]
+// = rows g+8 of the warp's tile, batch columns (2q, 2q+1) of n-tile nt.
+template <int FMT, int NT, bool SUBN>
+__device__ __forceinline__ void consume_stages(const GemvArgs &a, const uint8_t *stages, uint64_t *full,
+                                               uint64_t *empty, const uint16_t *xs, int n_iter, float2 (&acc)[NT][2]) {
+  using G = Geo<FMT>;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = make_float2(0.f, 0.f);
+  const uint16_t *xl = xs + (size_t)(lane >> 2) * a.xs_stride + (lane & 3) * 4;
+  // batch rows past B are not staged: their operand is zero
+  bool live[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) live[nt] = nt * 8 + (lane >> 2) < a.B;
+
+  // Blocks of a stage are processed in groups of GB with independent
+  // accumulators: the first k16 step of every block of the group is issued,
+  // then the second, then the scale FMAs, so consecutive MMAs never depend on
+  // each other and the tensor-core latency overlaps across blocks.
+  constexpr int BLK = CS * G::BPC;     // blocks per stage
+  constexpr int GB = NT == 1 ? 4 : (NT == 2 ? 2 : 1);  // blocks per group
+  for (int it = 0; it < n_iter; it++) {
+    const int slot = it % STAGES;
+    if (!mbar_wait(&full[slot], (it / STAGES) & 1)) atomicExch(a.err, 1);
+    const uint8_t *st = stages + slot * G::STAGE;
+    const uint8_t *cw = st + warp * 512 + lane * 16;
+    const uint8_t *sw = st + CWARPS * 512 + warp * G::SCT + (lane >> 2) * G::BPC * 4;
+    uint4 wv[CS];
+    uint32_t sv[CS][G::BPC];
+#pragma unroll
+    for (int j = 0; j < CS; j++) {
+      wv[j] = *reinterpret_cast<const uint4 *>(cw + j * G::REC);
+      if (G::BPC == 2) {
+        const uint2 t2 = *reinterpret_cast<const uint2 *>(sw + j * G::REC);
+        sv[j][0] = t2.x;
+        sv[j][G::BPC - 1] = t2.y;
+      } else {
+        sv[j][0] = *reinterpret_cast<const uint32_t *>(sw + j * G::REC);
+      }
+    }
+    const uint16_t *xk = xl + it * CS * G::CH;
+#pragma unroll
+    for (int b0 = 0; b0 < BLK; b0 += GB) {
+      float t[GB][NT][4];
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+#pragma unroll
+        for (int gb = 0; gb < GB; gb++) {
+          const int blk = b0 + gb, j = blk / G::BPC, bb = blk % G::BPC;
+          const uint32_t *wu = reinterpret_cast<const uint32_t *>(&wv[j]);
+          uint32_t A[4];
+          if (FMT == 0)
+            decode_q4(wu[bb * 2 + h], A);
+          else
+            decode_q8(wu[h * 2], wu[h * 2 + 1], A);
+#pragma unroll
+          for (int nt = 0; nt < NT; nt++) {
+            uint2 bx = make_uint2(0u, 0u);
+            if (live[nt]) bx = *reinterpret_cast<const uint2 *>(xk + (size_t)nt * 8 * a.xs_stride + blk * 32 + h * 16);
+            if (h == 0)
+              mma_f16_z(t[gb][nt], A, bx.x, bx.y);
+            else
+              mma_f16(t[gb][nt], A, bx.x, bx.y);
+          }
+        }
+      }
+#pragma unroll
+      for (int gb = 0; gb < GB; gb++) {
+        const int blk = b0 + gb, j = blk / G::BPC, bb = blk % G::BPC;
+        float2 d = decode_scales(sv[j][bb], SUBN);
+        if (FMT == 0) d.y *= 0.0625f;
+        const float2 dg = make_float2(d.x, d.x), dh = make_float2(d.y, d.y);
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+          acc[nt][0] = __ffma2_rn(make_float2(t[gb][nt][0], t[gb][nt][1]), dg, acc[nt][0]);
+          acc[nt][1] = __ffma2_rn(make_float2(t[gb][nt][2], t[gb][nt][3]), dh, acc[nt][1]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+}
+
 template <int FMT, int NT>
 __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const GemvArgs a) {
   using G = Geo<FMT>;
@@ -200,15 +303,16 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const 
   uint16_t *xs = reinterpret_cast<uint16_t *>(smem + STAGES * G::STAGE);
   float *red = reinterpret_cast<float *>(smem);  // reuses the stages after the main loop
   __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES];
+  __shared__ int s_exp[BR];
   __shared__ int s_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = blockIdx.x, s = blockIdx.y;
-  const int c0 = (int)((long long)s * a.n_chunks / a.S);
-  const int c1 = (int)((long long)(s + 1) * a.n_chunks / a.S);
-  const int nck = c1 - c0;
-  const int n_iter = (nck + CS - 1) / CS;
-  const int tiles_here = min(CWARPS, a.n_tiles - g * CWARPS);
+  // k-splits own whole stages (the chunk count is a multiple of CS)
+  const int n_stages = a.n_chunks / CS;
+  const int st0 = (int)((long long)s * n_stages / a.S);
+  const int n_iter = (int)((long long)(s + 1) * n_stages / a.S) - st0;
+  const int c0 = st0 * CS, nck = n_iter * CS;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; i++) {
@@ -220,24 +324,23 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const 
   __syncthreads();
 
   if (warp == CWARPS) {
-    // ---------------- producer: weight slices -> shared-memory stages
+    // ---------------- producer: one bulk copy of CS records per stage
     if (lane == 0) {
+      const uint8_t *src = a.records + ((size_t)g * a.n_chunks + c0) * G::REC;
       for (int it = 0; it < n_iter; it++) {
         const int slot = it % STAGES;
         if (it >= STAGES && !mbar_wait(&empty[slot], ((it / STAGES) & 1) ^ 1)) atomicExch(a.err, 1);
-        const int cb = c0 + it * CS;
-        const int nc = min(CS, c1 - cb);
-        uint8_t *st = stages + slot * G::STAGE;
-        mbar_expect_tx(&full[slot], (uint32_t)(tiles_here * nc * (512 + G::SC_PER_CHUNK)));
-        for (int t = 0; t < tiles_here; t++) {
-          const size_t tc = (size_t)(g * CWARPS + t) * a.n_chunks + cb;
-          bulk_g2s(st + t * CS * 512, a.codes + tc * 512, (uint32_t)nc * 512, &full[slot]);
-          bulk_g2s(st + G::CODE_BYTES + t * CS * G::SC_PER_CHUNK, a.scales + tc * G::SC_PER_CHUNK,
-                   (uint32_t)(nc * G::SC_PER_CHUNK), &full[slot]);
-        }
+        mbar_expect_tx(&full[slot], (uint32_t)G::STAGE);
+        bulk_g2s(stages + slot * G::STAGE, src + (size_t)it * G::STAGE, (uint32_t)G::STAGE, &full[slot]);
       }
     }
     asm volatile("griddepcontrol.launch_dependents;");
+    __syncwarp();
+    if (a.cluster) {
+      // take part in the two cluster barriers of the reduction
+      cluster_sync_all();
+      cluster_sync_all();
+    }
     return;
   }
 
@@ -246,106 +349,55 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const 
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const bool subnormal = (__ldg(a.hdr + 1) & TILED_FLAG_SUBNORMAL_SCALES) != 0;
   const int k0 = c0 * G::CH, kc = nck * G::CH;
+  const int nb = min(a.B, BR);
   {
-    // x[:, k0:k0+kc] (bf16, unchanged), 16-byte async copies of the live
-    // batch rows only; columns past K are zero-filled
+    // x[:, k0:k0+kc] (bf16) by 16-byte async copies of the live batch rows;
+    // columns past K are zero-filled
     const int per_row = kc / 8;
-    const int total = min(a.B, BR) * per_row;
+    const int total = nb * per_row;
     for (int i = threadIdx.x; i < total; i += CWARPS * 32) {
       const int b = i / per_row, p = i % per_row;
       const int kk = k0 + p * 8;
-      const bool ok = b < a.B && kk < a.K;
+      const bool ok = kk < a.K;
       cp_async16(xs + (size_t)b * a.xs_stride + p * 8, ok ? a.x + (size_t)b * a.K + kk : a.x, ok ? 16 : 0);
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
+    consumer_sync();
+    // per column: e with max|x| * 2^-e in [2^14, 2^15) (0 for an all-zero or
+    // non-finite column)
+    for (int b = warp; b < BR; b += CWARPS) {
+      unsigned m = 0;
+      if (b < nb) {
+        const uint32_t *row = reinterpret_cast<const uint32_t *>(xs + (size_t)b * a.xs_stride);
+        for (int i = lane; i < kc / 2; i += 32) {
+          const uint32_t v = row[i];
+          m = max(m, max(v & 0x7FFFu, (v >> 16) & 0x7FFFu));
+        }
+      }
+      m = __reduce_max_sync(0xffffffffu, m);
+      if (lane == 0) s_exp[b] = (m != 0 && m < 0x7F80u) ? max((int)(m >> 7), 1) - 127 - 14 : 0;
+    }
+    consumer_sync();
+    // in place: bf16 x -> f16 x * 2^-e (exact)
+    for (int i = threadIdx.x; i < total; i += CWARPS * 32) {
+      const int b = i / per_row, p = i % per_row;
+      uint4 *ptr = reinterpret_cast<uint4 *>(xs + (size_t)b * a.xs_stride + p * 8);
+      uint4 v = *ptr;
+      const int e = -s_exp[b];
+      uint32_t *w = reinterpret_cast<uint32_t *>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        w[j] = pack_f16x2(mul_pow2(__uint_as_float(w[j] << 16), e), mul_pow2(__uint_as_float(w[j] & 0xFFFF0000u), e));
+      *ptr = v;
+    }
   }
   consumer_sync();
 
-  float acc[NT][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-  const bool active = warp < tiles_here;
-  const uint16_t *xl = xs + (size_t)(lane >> 2) * a.xs_stride + (lane & 3) * 4;
-
-  // Blocks of a stage are processed in groups of GB with independent
-  // accumulators: the first k16 step of every block of the group is issued,
-  // then the second, then the scale FMAs, so consecutive MMAs never depend on
-  // each other and the tensor-core latency overlaps across blocks.
-  constexpr int BLK = CS * G::BPC;                           // blocks per stage
-  constexpr int GB = NT == 1 ? BLK : 2;                      // blocks per group
-  for (int it = 0; it < n_iter; it++) {
-    const int slot = it % STAGES;
-    if (!mbar_wait(&full[slot], (it / STAGES) & 1)) atomicExch(a.err, 1);
-    if (active) {
-      const uint8_t *st = stages + slot * G::STAGE;
-      const uint8_t *cw = st + warp * CS * 512 + lane * 16;
-      const uint8_t *sw = st + G::CODE_BYTES + warp * CS * G::SC_PER_CHUNK + (lane >> 2) * G::BPC * 4;
-      const int nc = min(CS, nck - it * CS);
-      uint4 wv[CS];
-      uint32_t sv[CS][G::BPC];
-#pragma unroll
-      for (int j = 0; j < CS; j++) {
-        if (j < nc) {
-          wv[j] = *reinterpret_cast<const uint4 *>(cw + j * 512);
-          if (G::BPC == 2) {
-            const uint2 t2 = *reinterpret_cast<const uint2 *>(sw + j * G::SC_PER_CHUNK);
-            sv[j][0] = t2.x;
-            sv[j][G::BPC - 1] = t2.y;
-          } else {
-            sv[j][0] = *reinterpret_cast<const uint32_t *>(sw + j * G::SC_PER_CHUNK);
-          }
-        }
-      }
-      const int kstage = it * CS * G::CH;
-#pragma unroll
-      for (int b0 = 0; b0 < BLK; b0 += GB) {
-        float t[GB][NT][4];
-#pragma unroll
-        for (int gb = 0; gb < GB; gb++)
-#pragma unroll
-          for (int nt = 0; nt < NT; nt++) t[gb][nt][0] = t[gb][nt][1] = t[gb][nt][2] = t[gb][nt][3] = 0.f;
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-#pragma unroll
-          for (int gb = 0; gb < GB; gb++) {
-            const int blk = b0 + gb, j = blk / G::BPC, bb = blk % G::BPC;
-            if (j < nc) {
-              const uint32_t *wu = reinterpret_cast<const uint32_t *>(&wv[j]);
-              uint32_t A[4];
-              if (FMT == 0)
-                decode_q4(wu[bb * 2 + h], A);
-              else
-                decode_q8(wu[h * 2], wu[h * 2 + 1], A);
-              const int kk = kstage + blk * 32 + h * 16;
-#pragma unroll
-              for (int nt = 0; nt < NT; nt++) {
-                // batch rows past B are not staged: their operand is zero
-                uint2 bx = make_uint2(0u, 0u);
-                if (nt * 8 + (lane >> 2) < a.B) bx = *reinterpret_cast<const uint2 *>(xl + (size_t)nt * 8 * a.xs_stride + kk);
-                mma_bf16(t[gb][nt], A, bx.x, bx.y);
-              }
-            }
-          }
-        }
-#pragma unroll
-        for (int gb = 0; gb < GB; gb++) {
-          const int blk = b0 + gb, j = blk / G::BPC, bb = blk % G::BPC;
-          if (j < nc) {
-            const float2 d = decode_scales(sv[j][bb], subnormal);
-#pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-              acc[nt][0] = fmaf(d.x, t[gb][nt][0], acc[nt][0]);
-              acc[nt][1] = fmaf(d.x, t[gb][nt][1], acc[nt][1]);
-              acc[nt][2] = fmaf(d.y, t[gb][nt][2], acc[nt][2]);
-              acc[nt][3] = fmaf(d.y, t[gb][nt][3], acc[nt][3]);
-            }
-          }
-        }
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
-  }
+  float2 acc[NT][2];  // [nt][row g | row g+8] x (batch column 2q, 2q+1)
+  if (subnormal)
+    consume_stages<FMT, NT, true>(a, stages, full, empty, xs, n_iter, acc);
+  else
+    consume_stages<FMT, NT, false>(a, stages, full, empty, xs, n_iter, acc);
 
   // every stage has been consumed and no copy is in flight: reuse the ring
   consumer_sync();
@@ -354,10 +406,11 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const 
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
       const int b = nt * 8 + (lane & 3) * 2;
-      red[(size_t)b * ROWS_PER_CTA + rl] = acc[nt][0];
-      red[(size_t)(b + 1) * ROWS_PER_CTA + rl] = acc[nt][1];
-      red[(size_t)b * ROWS_PER_CTA + rl + 8] = acc[nt][2];
-      red[(size_t)(b + 1) * ROWS_PER_CTA + rl + 8] = acc[nt][3];
+      const int e0 = s_exp[b], e1 = s_exp[b + 1];
+      red[(size_t)b * ROWS_PER_CTA + rl] = mul_pow2(acc[nt][0].x, e0);
+      red[(size_t)(b + 1) * ROWS_PER_CTA + rl] = mul_pow2(acc[nt][0].y, e1);
+      red[(size_t)b * ROWS_PER_CTA + rl + 8] = mul_pow2(acc[nt][1].x, e0);
+      red[(size_t)(b + 1) * ROWS_PER_CTA + rl + 8] = mul_pow2(acc[nt][1].y, e1);
     }
   }
   consumer_sync();
@@ -372,7 +425,27 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const 
     }
     return;
   }
-  const size_t NP = (size_t)a.n_tiles * 16;
+  if (a.cluster) {
+    // the S k-splits of this row group form one cluster: every CTA sums a
+    // slice of the outputs over the partials in the peers' shared memory, in
+    // split order (deterministic), then the cluster waits until all reads are
+    // done before any CTA exits
+    __syncwarp();
+    cluster_sync_all();
+    const int per = (nel + a.S - 1) / a.S;
+    const int i1 = min(nel, (s + 1) * per);
+    cg::cluster_group cl = cg::this_cluster();
+    for (int i = s * per + threadIdx.x; i < i1; i += CWARPS * 32) {
+      const int b = i / ROWS_PER_CTA, r = i % ROWS_PER_CTA;
+      float v = 0.f;
+      for (int ss = 0; ss < a.S; ss++) v += *cl.map_shared_rank(red + i, (unsigned)ss);
+      if (r < nrows) epilogue_store(a, b, row0 + r, v);
+    }
+    __syncwarp();
+    cluster_sync_all();
+    return;
+  }
+  const size_t NP = (size_t)a.NP;
   for (int i = threadIdx.x; i < nel; i += CWARPS * 32) {
     const int b = i / ROWS_PER_CTA, r = i % ROWS_PER_CTA;
     if (r < nrows) __stcg(a.ws + ((size_t)s * a.B + b) * NP + row0 + r, red[i]);
@@ -386,8 +459,20 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const 
   for (int i = threadIdx.x; i < nel; i += CWARPS * 32) {
     const int b = i / ROWS_PER_CTA, r = i % ROWS_PER_CTA;
     if (r >= nrows) continue;
+    // partials in split order; loads issued four at a time
+    const float *src = a.ws + (size_t)b * NP + row0 + r;
+    const size_t step = (size_t)a.B * NP;
     float v = 0.f;
-    for (int ss = 0; ss < a.S; ss++) v += __ldcg(a.ws + ((size_t)ss * a.B + b) * NP + row0 + r);
+    int ss = 0;
+    for (; ss + 4 <= a.S; ss += 4) {
+      const float p0 = __ldcg(src + ss * step), p1 = __ldcg(src + (ss + 1) * step);
+      const float p2 = __ldcg(src + (ss + 2) * step), p3 = __ldcg(src + (ss + 3) * step);
+      v += p0;
+      v += p1;
+      v += p2;
+      v += p3;
+    }
+    for (; ss < a.S; ss++) v += __ldcg(src + ss * step);
     epilogue_store(a, b, row0 + r, v);
   }
   if (threadIdx.x == 0) a.counters[g] = 0u;
@@ -401,39 +486,68 @@ size_t smem_bytes_t(int fmt, int NT, int batch, int xs_stride) {
 
 int xs_stride_for(int kc_max) { return kc_max + 16; }  // stride/2 = 8 (mod 32): conflict-free 8-byte loads
 
-// Resident CTAs per SM for an instantiation at a shared-memory size (cached).
+// Largest k-range of one split: splits own whole stages of CS chunks, so a
+// split spans at most ceil(stages / S) stages (the kernel's split bounds).
+int kc_max_for(const TiledGeom &g, int S) {
+  const int n_stages = g.n_chunks / CS;
+  return (n_stages + S - 1) / S * CS * g.chunk;
+}
+
+// CTAs of an instantiation that can be resident on the whole GPU at a
+// shared-memory size: per-SM occupancy x SMs for plain launches, the largest
+// number of co-resident clusters x S for clusters of S CTAs (cached).
 template <int FMT, int NT>
-int occupancy_t(size_t smem) {
+int resident_t(size_t smem, int cluster, int sms) {
   static std::mutex mu;
-  static std::map<size_t, int> cache;
+  static std::map<std::pair<size_t, int>, int> cache;
   std::lock_guard<std::mutex> lk(mu);
-  auto it = cache.find(smem);
+  const auto key = std::make_pair(smem, cluster);
+  auto it = cache.find(key);
   if (it != cache.end()) return it->second;
   auto kfn = gemv_q_kernel<FMT, NT>;
-  int n = 1;
-  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kfn, THREADS, smem) != cudaSuccess || n < 1) {
-    cudaGetLastError();
-    n = 1;
+  int n = 0;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) == cudaSuccess) {
+    if (cluster <= 1) {
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, THREADS, smem) == cudaSuccess) n = per_sm * sms;
+    } else {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1, cluster);
+      cfg.blockDim = dim3(THREADS);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 1;
+      attr.val.clusterDim.y = cluster;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kfn, &cfg) == cudaSuccess) n = clusters * cluster;
+    }
   }
-  cache[smem] = n;
+  if (n < 1) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cache[key] = n;
   return n;
 }
 
-int occupancy(int fmt, int NT, size_t smem) {
+int resident(int fmt, int NT, size_t smem, int cluster, int sms) {
   if (fmt == VXB_Q4_0) {
     switch (NT) {
-      case 1: return occupancy_t<0, 1>(smem);
-      case 2: return occupancy_t<0, 2>(smem);
-      case 3: return occupancy_t<0, 3>(smem);
-      default: return occupancy_t<0, 4>(smem);
+      case 1: return resident_t<0, 1>(smem, cluster, sms);
+      case 2: return resident_t<0, 2>(smem, cluster, sms);
+      case 3: return resident_t<0, 3>(smem, cluster, sms);
+      default: return resident_t<0, 4>(smem, cluster, sms);
     }
   }
   switch (NT) {
-    case 1: return occupancy_t<1, 1>(smem);
-    case 2: return occupancy_t<1, 2>(smem);
-    case 3: return occupancy_t<1, 3>(smem);
-    default: return occupancy_t<1, 4>(smem);
+    case 1: return resident_t<1, 1>(smem, cluster, sms);
+    case 2: return resident_t<1, 2>(smem, cluster, sms);
+    case 3: return resident_t<1, 3>(smem, cluster, sms);
+    default: return resident_t<1, 4>(smem, cluster, sms);
   }
 }
 
@@ -451,11 +565,22 @@ int launch_t(vxb_ctx *ctx, const GemvArgs &a, dim3 grid, size_t smem, cudaStream
   cfg.blockDim = dim3(THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    na++;
+  }
+  if (a.cluster) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = grid.y;
+    attr[na].val.clusterDim.z = 1;
+    na++;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = na;
   VXB_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, kfn, a));
   return VXB_OK;
 }
@@ -467,35 +592,40 @@ namespace vxb {
 size_t gemv_smem_bytes(int fmt, int N, int K, int batch, int S) {
   const TiledGeom g = tiled_geom(fmt, N, K);
   const int NT = (batch + 7) / 8;
-  const int kc_max = (g.n_chunks + S - 1) / S * g.chunk;
+  const int kc_max = kc_max_for(g, S);
   return smem_bytes_t(fmt, NT, batch, xs_stride_for(kc_max));
 }
 
 GemvPlan gemv_plan(const vxb_ctx *ctx, int fmt, int N, int K, int batch) {
   const TiledGeom g = tiled_geom(fmt, N, K);
-  const int row_groups = (g.n_tiles + CWARPS - 1) / CWARPS;
+  const int row_groups = g.n_groups;
   const int sms = ctx->num_sms > 0 ? ctx->num_sms : 148;
   // Each CTA streams at a rate set by its stage ring, so the run time is the
   // number of CTA waves times the duration of one CTA (proportional to 1/S):
   // pick the split count that minimises waves/S, with a small cost per wave.
-  // Resident CTAs per SM come from the occupancy calculator.
-  int best = 1;
+  // Up to kMaxClusterSplits splits reduce through distributed shared memory
+  // inside one cluster; more splits reduce through global memory, which costs
+  // a few more round trips. Resident CTAs per SM come from the occupancy
+  // calculator.
+  int best = 0;
   double best_cost = 1e30;
-  const int smax = std::min(32, std::max(1, g.n_chunks / 2));
+  const int smax = std::min(32, g.n_chunks / CS);
   for (int S = 1; S <= smax; S++) {
     const size_t sm = gemv_smem_bytes(fmt, N, K, batch, S);
     if (sm > 200 * 1024) continue;
-    const int per_sm = occupancy(fmt, (batch + 7) / 8, sm);
-    const int slots = per_sm * sms;
+    const int slots = resident(fmt, (batch + 7) / 8, sm, S > 1 && S <= kMaxClusterSplits ? S : 1, sms);
+    if (slots < 1) continue;
     const int waves = (row_groups * S + slots - 1) / slots;
-    const double cost = (double)waves / S + 0.03 * waves;
+    const double cost = (double)waves / S + 0.03 * waves + (S > kMaxClusterSplits ? 0.05 : 0.0);
     if (cost < best_cost - 1e-9) {
       best_cost = cost;
       best = S;
     }
   }
+  if (best == 0) best = smax;  // nothing fits: the launch reports the shared-memory need
   GemvPlan p;
   p.S = best;
+  p.cluster = best > 1 && best <= kMaxClusterSplits;
   p.pdl = true;
   return p;
 }
@@ -513,13 +643,13 @@ int gemv_launch(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const 
   const TiledGeom g = tiled_geom(fmt, N, K);
   GemvPlan p = plan_override ? *plan_override : gemv_plan(ctx, fmt, N, K, batch);
   const int NT = (batch + 7) / 8;
-  const int row_groups = (g.n_tiles + CWARPS - 1) / CWARPS;
-  const size_t ws_bytes = p.S > 1 ? (size_t)p.S * batch * g.N_pad * sizeof(float) : 0;
+  const int row_groups = g.n_groups;
+  const int NP = (N + 15) / 16 * 16;  // row stride of the split-K partials
+  const size_t ws_bytes = p.S > 1 ? (size_t)p.S * batch * NP * sizeof(float) : 0;
   if (int rc = ws_reserve(ctx, ws_bytes, (size_t)row_groups)) return rc;
   GemvArgs a;
   const uint8_t *base = (const uint8_t *)d_tiled;
-  a.codes = base + g.codes_off;
-  a.scales = base + g.codes_off + g.codes_bytes;
+  a.records = base + g.codes_off;
   a.hdr = (const uint32_t *)base;
   a.x = d_x;
   a.y = d_y;
@@ -530,11 +660,12 @@ int gemv_launch(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const 
   a.N = N;
   a.K = K;
   a.B = batch;
-  a.n_tiles = g.n_tiles;
+  a.NP = NP;
   a.n_chunks = g.n_chunks;
   a.S = p.S;
+  a.cluster = p.cluster && p.S > 1 && p.S <= kMaxClusterSplits;
   a.y_dtype = y_dtype;
-  const int kc_max = (g.n_chunks + p.S - 1) / p.S * g.chunk;
+  const int kc_max = kc_max_for(g, p.S);
   a.xs_stride = xs_stride_for(kc_max);
   const size_t smem = smem_bytes_t(fmt, NT, batch, a.xs_stride);
   if (smem > 200 * 1024) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q: split plan needs %zu bytes of shared memory", smem);
@@ -624,8 +755,9 @@ VXB_API int vxb_gemv_q_static(vxb_ctx *ctx, int fmt, const void *d_tiled, int N,
   if (((uintptr_t)d_tiled) % 256 || ((uintptr_t)d_x) % 16)
     return set_error(ctx, VXB_EINVAL, "vxb_gemv_q_static: weights must be 256-byte and activations 16-byte aligned");
   const TiledGeom g = tiled_geom(fmt, N, K);
-  const size_t per_split = (size_t)batch * g.N_pad * sizeof(float);
-  const int row_groups = (g.n_tiles + CWARPS - 1) / CWARPS;
+  const int NP = (N + 15) / 16 * 16;  // row stride of the split-K partials
+  const size_t per_split = (size_t)batch * NP * sizeof(float);
+  const int row_groups = g.n_groups;
   // the fixed array must hold the partials of at least two k-splits
   if (per_split * 2 > kStaticPartialBytes || row_groups > kStaticCounters)
     return set_error(ctx, VXB_EINVAL,
@@ -639,8 +771,7 @@ VXB_API int vxb_gemv_q_static(vxb_ctx *ctx, int fmt, const void *d_tiled, int N,
   p.S = std::max(1, std::min<int>(p.S, (int)(kStaticPartialBytes / per_split)));
   GemvArgs a;
   const uint8_t *wb = (const uint8_t *)d_tiled;
-  a.codes = wb + g.codes_off;
-  a.scales = wb + g.codes_off + g.codes_bytes;
+  a.records = wb + g.codes_off;
   a.hdr = (const uint32_t *)wb;
   a.x = d_x;
   a.y = d_y;
@@ -651,11 +782,12 @@ VXB_API int vxb_gemv_q_static(vxb_ctx *ctx, int fmt, const void *d_tiled, int N,
   a.N = N;
   a.K = K;
   a.B = batch;
-  a.n_tiles = g.n_tiles;
+  a.NP = NP;
   a.n_chunks = g.n_chunks;
   a.S = p.S;
+  a.cluster = p.cluster && p.S > 1 && p.S <= kMaxClusterSplits;
   a.y_dtype = y_dtype;
-  const int kc_max = (g.n_chunks + p.S - 1) / p.S * g.chunk;
+  const int kc_max = kc_max_for(g, p.S);
   a.xs_stride = xs_stride_for(kc_max);
   const int NT = (batch + 7) / 8;
   const size_t smem = smem_bytes_t(fmt, NT, batch, a.xs_stride);

@@ -6,8 +6,9 @@
 namespace vxb {
 
 struct GemvPlan {
-  int S;     // k-splits (CTAs per row group)
-  bool pdl;  // launch with programmatic stream serialization
+  int S;        // k-splits (CTAs per row group)
+  bool pdl;      // launch with programmatic stream serialization
+  bool cluster;  // the splits of a row group form a cluster (S <= 8)
 };
 
 GemvPlan gemv_plan(const vxb_ctx *ctx, int fmt, int N, int K, int batch);

@@ -1,0 +1,157 @@
+"""Kernel-level timing of the decode GEMV and the decode attention.
+
+    python -m vortex_b200.kernel_bench gemv [--fmt Q4_0] [--n 11008] [--k 4096] [--batch 1]
+    python -m vortex_b200.kernel_bench attn [--ctx 8192] [--dtype bf16]
+
+Each case streams its operands from HBM: the GEMV rotates over enough distinct
+weight copies to exceed twice the L2 (126 MB), the attention reads a KV cache
+far larger than L2. Launches are captured back to back in one CUDA graph and
+timed with CUDA events on the capturing stream; the figure is the average
+device time of one launch. GB/s counts algorithmic bytes: weights (codes +
+f16 scales) + bf16 activations + outputs for the GEMV, K and V of every cached
+token (+ scales for int8) + q/out for the attention.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+L2_BYTES = 126 * 2 ** 20
+
+
+def _graph_time(torch, fn, launches_per_call: int, reps: int = 20):
+    """Capture fn() once into a graph, replay `reps` times; seconds per launch."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()  # first call outside capture (one-time setup such as workspace growth)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        fn()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream()
+    e0.record(cur)
+    for _ in range(reps):
+        g.replay()
+    e1.record(cur)
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) * 1e-3 / (reps * launches_per_call)
+    del g
+    return t
+
+
+def gemv_bytes(fmt: int, N: int, K: int, B: int) -> int:
+    from . import quant as Q
+    return Q.block_bytes(fmt, N * K) + 2 * B * K + 4 * B * N
+
+
+def gemv_case(fmt, N: int, K: int, batches=(1, 4, 16), reps: int = 20, seed: int = 0, min_copies: int = 2):
+    """Time y = deq(W) x for each batch size over rotating weight copies
+    (W ~ N(0, 0.02), x ~ N(0, 1) bf16, y f32)."""
+    import torch
+
+    from . import quant as Q
+    f = Q._fmt(fmt)
+    wbytes = Q.block_bytes(f, N * K)
+    copies = max(min_copies, -(-2 * L2_BYTES // wbytes) + 1)
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    ws = []
+    for _ in range(copies):
+        w = torch.randn(N, K, device="cuda", generator=gen) * 0.02
+        ws.append(Q.TiledWeight.from_float(w, f))
+        del w
+    out = []
+    for B in batches:
+        x = torch.randn(B, K, device="cuda", generator=gen).bfloat16()
+        y = torch.empty(B, N, device="cuda")
+
+        def run():
+            for tw in ws:
+                tw.gemv(x, out=y)
+
+        t = _graph_time(torch, run, copies, reps)
+        byts = gemv_bytes(f, N, K, B)
+        out.append({"fmt": "Q4_0" if f == Q.Q4_0 else "Q8_0", "N": N, "K": K, "batch": B, "us": t * 1e6,
+                    "GBps": byts / t / 1e9, "bytes": byts, "copies": copies})
+    del ws
+    torch.cuda.empty_cache()
+    return out
+
+
+def gemv_sweep(shapes=((4096, 4096), (11008, 4096), (4096, 11008)), fmts=("Q4_0", "Q8_0"), batches=(1, 4, 16),
+               reps: int = 20):
+    res = []
+    for fmt in fmts:
+        for N, K in shapes:
+            res.extend(gemv_case(fmt, N, K, batches, reps))
+    return res
+
+
+def attn_case(ctx: int, dtype: str = "bf16", n: int = 32, Hq: int = 32, Hkv: int = 8, D: int = 128, reps: int = 10,
+              seed: int = 0):
+    """Decode attention over a paged cache: n sequences of ctx tokens, Hq
+    query heads over Hkv KV heads (GQA), head_dim D, one query token each."""
+    import torch
+
+    from . import kv_cache as KV
+    kd = KV.BF16 if dtype == "bf16" else KV.I8
+    bs = 16
+    cache = KV.PagedKVCache(1, Hkv, D, bs, max_blocks=n * (-(-ctx // bs)) + 8, max_seqs=n + 1, kv_dtype=kd)
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    for i in range(n):
+        k = torch.randn(ctx, Hkv, D, device="cuda", generator=gen).bfloat16()
+        v = torch.randn(ctx, Hkv, D, device="cuda", generator=gen).bfloat16()
+        cache.append_seq(0, i, k, v)
+        del k, v
+    q = torch.randn(n, Hq, D, device="cuda", generator=gen).bfloat16()
+    ids = list(range(n))
+    o = cache.attention(0, ids, q)
+    per = 5
+
+    def run():
+        for _ in range(per):
+            cache.attention(0, ids, q, out=o)
+
+    t = _graph_time(torch, run, per, reps)
+    per_tok = Hkv * D * 2 * (2 if kd == KV.BF16 else 1) + (Hkv * 2 * 4 if kd == KV.I8 else 0)
+    byts = n * ctx * per_tok + 2 * 2 * n * Hq * D
+    res = {"dtype": dtype, "ctx": ctx, "batch": n, "Hq": Hq, "Hkv": Hkv, "D": D, "us": t * 1e6,
+           "GBps": byts / t / 1e9, "bytes": byts}
+    del cache
+    torch.cuda.empty_cache()
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="what", required=True)
+    g = sub.add_parser("gemv")
+    g.add_argument("--fmt", default=None, help="Q4_0 or Q8_0 (default: both)")
+    g.add_argument("--n", type=int, default=None)
+    g.add_argument("--k", type=int, default=None)
+    g.add_argument("--batch", type=int, nargs="*", default=[1, 4, 16])
+    g.add_argument("--reps", type=int, default=20)
+    a = sub.add_parser("attn")
+    a.add_argument("--ctx", type=int, nargs="*", default=[1024, 8192, 32768])
+    a.add_argument("--dtype", nargs="*", default=["bf16", "int8"])
+    a.add_argument("--reps", type=int, default=10)
+    args = ap.parse_args()
+    import torch
+    torch.cuda.set_device(0)
+    if args.what == "gemv":
+        fmts = [args.fmt] if args.fmt else ["Q4_0", "Q8_0"]
+        shapes = [(args.n, args.k)] if args.n and args.k else [(4096, 4096), (11008, 4096), (4096, 11008)]
+        for r in gemv_sweep(shapes, fmts, args.batch, args.reps):
+            print(json.dumps(r), flush=True)
+    else:
+        for dt in args.dtype:
+            for c in args.ctx:
+                print(json.dumps(attn_case(c, dt, reps=args.reps)), flush=True)
+
+
+if __name__ == "__main__":
+    main()
