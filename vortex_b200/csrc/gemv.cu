@@ -67,6 +67,15 @@ struct Geo {
   static constexpr int SCT = 8 * BPC * 4;           // scale bytes of one tile in a record
   static constexpr int REC = CWARPS * (512 + SCT);  // bytes of one (row group, chunk) record
   static constexpr int STAGE = CS * REC;
+  static constexpr int XSTR = CS * CH + 16;  // elements per batch row of a stage's x slice
+};
+
+// Activations: batches up to 8 (XF16) stage the split's x once as f16 scaled
+// per batch column by 2^-e; larger batches carry an unchanged bf16 x slice in
+// every stage (no prologue, shared memory independent of K).
+template <int NT>
+struct XMode {
+  static constexpr bool F16 = NT == 1;
 };
 static_assert(Geo<0>::REC == 8 * (512 + 64) && Geo<1>::REC == 8 * (512 + 32), "record size");
 
@@ -91,6 +100,11 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
 
 __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// raise the transaction count without arriving
+__device__ __forceinline__ void mbar_expect_tx_only(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
@@ -156,6 +170,59 @@ __device__ __forceinline__ void decode_q8(uint32_t w0, uint32_t w1, uint32_t A[4
   A[3] = hsub2(__byte_perm(w1, M, 0x4342), SUB);
 }
 
+__device__ __forceinline__ uint32_t bsub2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+// bf16 operands (batches above 8, activations staged unchanged). Q4_0: nibble
+// n at bits 0-3 / 16-19 of (w >> 4i) gives bf16 0x4300|n = 128+n, minus 136:
+// the exact codes of every row.
+__device__ __forceinline__ void decode_q4_bf16(uint32_t w, uint32_t A[4]) {
+  const uint32_t M = 0x43004300u;    // bf16 128.0 x2
+  const uint32_t SUB = 0x43084308u;  // bf16 136.0 x2
+  A[0] = bsub2(lop_and_or(w, 0x000F000Fu, M), SUB);
+  A[1] = bsub2(lop_and_or(w >> 4, 0x000F000Fu, M), SUB);
+  A[2] = bsub2(lop_and_or(w >> 8, 0x000F000Fu, M), SUB);
+  A[3] = bsub2(lop_and_or(w >> 12, 0x000F000Fu, M), SUB);
+}
+
+// Q8_0 bytes u = q+128 -> f32 2^23+u by PRMT, minus 2^23+128, packed to bf16
+// (exact: |q| <= 128)
+__device__ __forceinline__ void q8_word_bf16(uint32_t w, uint32_t &lo, uint32_t &hi) {
+  const float Bm = 8388736.0f;  // 2^23 + 128
+  const float c0 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440)) - Bm;
+  const float c1 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7441)) - Bm;
+  const float c2 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7442)) - Bm;
+  const float c3 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7443)) - Bm;
+  lo = pack_bf16x2(c0, c1);
+  hi = pack_bf16x2(c2, c3);
+}
+
+__device__ __forceinline__ void decode_q8_bf16(uint32_t w0, uint32_t w1, uint32_t A[4]) {
+  q8_word_bf16(w0, A[0], A[1]);
+  q8_word_bf16(w1, A[2], A[3]);
+}
+
+__device__ __forceinline__ void mma_bf16(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void mma_bf16_z(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+}
+
 __device__ __forceinline__ void mma_f16(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
   asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -216,10 +283,13 @@ template <int FMT, int NT, bool SUBN>
 __device__ __forceinline__ void consume_stages(const GemvArgs &a, const uint8_t *stages, uint64_t *full,
                                                uint64_t *empty, const uint16_t *xs, int n_iter, float2 (&acc)[NT][2]) {
   using G = Geo<FMT>;
+  constexpr bool XF16 = XMode<NT>::F16;
+  constexpr int STG = G::STAGE + (XF16 ? 0 : 8 * NT * G::XSTR * 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
   for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = make_float2(0.f, 0.f);
-  const uint16_t *xl = xs + (size_t)(lane >> 2) * a.xs_stride + (lane & 3) * 4;
+  const int xstride = XF16 ? a.xs_stride : G::XSTR;
+  const int xlane = (lane >> 2) * xstride + (lane & 3) * 4;
   // batch rows past B are not staged: their operand is zero
   bool live[NT];
 #pragma unroll
@@ -229,12 +299,12 @@ __device__ __forceinline__ void consume_stages(const GemvArgs &a, const uint8_t 
   // accumulators: the first k16 step of every block of the group is issued,
   // then the second, then the scale FMAs, so consecutive MMAs never depend on
   // each other and the tensor-core latency overlaps across blocks.
-  constexpr int BLK = CS * G::BPC;     // blocks per stage
+  constexpr int BLK = CS * G::BPC;                      // blocks per stage
   constexpr int GB = NT == 1 ? 4 : (NT == 2 ? 2 : 1);  // blocks per group
   for (int it = 0; it < n_iter; it++) {
     const int slot = it % STAGES;
     if (!mbar_wait(&full[slot], (it / STAGES) & 1)) atomicExch(a.err, 1);
-    const uint8_t *st = stages + slot * G::STAGE;
+    const uint8_t *st = stages + slot * STG;
     const uint8_t *cw = st + warp * 512 + lane * 16;
     const uint8_t *sw = st + CWARPS * 512 + warp * G::SCT + (lane >> 2) * G::BPC * 4;
     uint4 wv[CS];
@@ -250,7 +320,8 @@ __device__ __forceinline__ void consume_stages(const GemvArgs &a, const uint8_t 
         sv[j][0] = *reinterpret_cast<const uint32_t *>(sw + j * G::REC);
       }
     }
-    const uint16_t *xk = xl + it * CS * G::CH;
+    const uint16_t *xk = XF16 ? xs + it * CS * G::CH + xlane
+                              : reinterpret_cast<const uint16_t *>(st + G::STAGE) + xlane;
 #pragma unroll
     for (int b0 = 0; b0 < BLK; b0 += GB) {
       float t[GB][NT][4];
@@ -261,18 +332,32 @@ __device__ __forceinline__ void consume_stages(const GemvArgs &a, const uint8_t 
           const int blk = b0 + gb, j = blk / G::BPC, bb = blk % G::BPC;
           const uint32_t *wu = reinterpret_cast<const uint32_t *>(&wv[j]);
           uint32_t A[4];
-          if (FMT == 0)
-            decode_q4(wu[bb * 2 + h], A);
-          else
-            decode_q8(wu[h * 2], wu[h * 2 + 1], A);
+          if (XF16) {
+            if (FMT == 0)
+              decode_q4(wu[bb * 2 + h], A);
+            else
+              decode_q8(wu[h * 2], wu[h * 2 + 1], A);
+          } else {
+            if (FMT == 0)
+              decode_q4_bf16(wu[bb * 2 + h], A);
+            else
+              decode_q8_bf16(wu[h * 2], wu[h * 2 + 1], A);
+          }
 #pragma unroll
           for (int nt = 0; nt < NT; nt++) {
             uint2 bx = make_uint2(0u, 0u);
-            if (live[nt]) bx = *reinterpret_cast<const uint2 *>(xk + (size_t)nt * 8 * a.xs_stride + blk * 32 + h * 16);
-            if (h == 0)
-              mma_f16_z(t[gb][nt], A, bx.x, bx.y);
-            else
-              mma_f16(t[gb][nt], A, bx.x, bx.y);
+            if (live[nt]) bx = *reinterpret_cast<const uint2 *>(xk + (size_t)nt * 8 * xstride + blk * 32 + h * 16);
+            if (XF16) {
+              if (h == 0)
+                mma_f16_z(t[gb][nt], A, bx.x, bx.y);
+              else
+                mma_f16(t[gb][nt], A, bx.x, bx.y);
+            } else {
+              if (h == 0)
+                mma_bf16_z(t[gb][nt], A, bx.x, bx.y);
+              else
+                mma_bf16(t[gb][nt], A, bx.x, bx.y);
+            }
           }
         }
       }
@@ -280,7 +365,7 @@ __device__ __forceinline__ void consume_stages(const GemvArgs &a, const uint8_t 
       for (int gb = 0; gb < GB; gb++) {
         const int blk = b0 + gb, j = blk / G::BPC, bb = blk % G::BPC;
         float2 d = decode_scales(sv[j][bb], SUBN);
-        if (FMT == 0) d.y *= 0.0625f;
+        if (XF16 && FMT == 0) d.y *= 0.0625f;  // rows g+8 were decoded as 16q
         const float2 dg = make_float2(d.x, d.x), dh = make_float2(d.y, d.y);
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
@@ -298,9 +383,12 @@ template <int FMT, int NT>
 __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const GemvArgs a) {
   using G = Geo<FMT>;
   constexpr int BR = 8 * NT;  // padded batch rows
+  constexpr bool XF16 = XMode<NT>::F16;
+  constexpr int XB = XF16 ? 0 : BR * G::XSTR * 2;  // bytes of a stage's x slice
+  constexpr int STG = G::STAGE + XB;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t *stages = smem;
-  uint16_t *xs = reinterpret_cast<uint16_t *>(smem + STAGES * G::STAGE);
+  uint16_t *xs = reinterpret_cast<uint16_t *>(smem + STAGES * STG);  // XF16 only
   float *red = reinterpret_cast<float *>(smem);  // reuses the stages after the main loop
   __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES];
   __shared__ int s_exp[BR];
@@ -324,14 +412,49 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const 
   __syncthreads();
 
   if (warp == CWARPS) {
-    // ---------------- producer: one bulk copy of CS records per stage
+    // ---------------- producer: one bulk copy of CS records per stage (+ the
+    // stage's x rows for large batches)
     if (lane == 0) {
       const uint8_t *src = a.records + ((size_t)g * a.n_chunks + c0) * G::REC;
-      for (int it = 0; it < n_iter; it++) {
-        const int slot = it % STAGES;
-        if (it >= STAGES && !mbar_wait(&empty[slot], ((it / STAGES) & 1) ^ 1)) atomicExch(a.err, 1);
-        mbar_expect_tx(&full[slot], (uint32_t)G::STAGE);
-        bulk_g2s(stages + slot * G::STAGE, src + (size_t)it * G::STAGE, (uint32_t)G::STAGE, &full[slot]);
+      if (XF16) {
+        for (int it = 0; it < n_iter; it++) {
+          const int slot = it % STAGES;
+          if (it >= STAGES && !mbar_wait(&empty[slot], ((it / STAGES) & 1) ^ 1)) atomicExch(a.err, 1);
+          mbar_expect_tx(&full[slot], (uint32_t)G::STAGE);
+          bulk_g2s(stages + slot * STG, src + (size_t)it * G::STAGE, (uint32_t)G::STAGE, &full[slot]);
+        }
+      } else {
+        // weights of the first stages before waiting for the kernel that
+        // produces x; each stage's single arrival comes after its x copies
+        const int pre = min(STAGES, n_iter);
+        for (int it = 0; it < pre; it++) {
+          mbar_expect_tx_only(&full[it], (uint32_t)G::STAGE);
+          bulk_g2s(stages + it * STG, src + (size_t)it * G::STAGE, (uint32_t)G::STAGE, &full[it]);
+        }
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        for (int it = 0; it < n_iter; it++) {
+          const int slot = it % STAGES;
+          uint8_t *dst = stages + slot * STG;
+          if (it >= STAGES) {
+            if (!mbar_wait(&empty[slot], ((it / STAGES) & 1) ^ 1)) atomicExch(a.err, 1);
+            mbar_expect_tx_only(&full[slot], (uint32_t)G::STAGE);
+            bulk_g2s(dst, src + (size_t)it * G::STAGE, (uint32_t)G::STAGE, &full[slot]);
+          }
+          uint16_t *xd = reinterpret_cast<uint16_t *>(dst + G::STAGE);
+          const int kst = (c0 + it * CS) * G::CH;
+          const int kv = max(0, min(CS * G::CH, a.K - kst));  // columns of x inside K
+          if (kv < CS * G::CH) {
+            for (int b = 0; b < a.B; b++)
+              for (int k = kv; k < CS * G::CH; k += 2)
+                *reinterpret_cast<uint32_t *>(xd + b * G::XSTR + k) = 0u;
+          }
+          if (kv > 0) {
+            mbar_expect_tx_only(&full[slot], (uint32_t)(a.B * kv * 2));
+            for (int b = 0; b < a.B; b++)
+              bulk_g2s(xd + b * G::XSTR, a.x + (size_t)b * a.K + kst, (uint32_t)(kv * 2), &full[slot]);
+          }
+          mbar_arrive(&full[slot]);
+        }
       }
     }
     asm volatile("griddepcontrol.launch_dependents;");
@@ -348,9 +471,11 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const 
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const bool subnormal = (__ldg(a.hdr + 1) & TILED_FLAG_SUBNORMAL_SCALES) != 0;
-  const int k0 = c0 * G::CH, kc = nck * G::CH;
-  const int nb = min(a.B, BR);
-  {
+  if (!XF16) {
+    if (threadIdx.x < BR) s_exp[threadIdx.x] = 0;
+  } else {
+    const int k0 = c0 * G::CH, kc = nck * G::CH;
+    const int nb = min(a.B, BR);
     // x[:, k0:k0+kc] (bf16) by 16-byte async copies of the live batch rows;
     // columns past K are zero-filled
     const int per_row = kc / 8;
@@ -479,9 +604,11 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const 
 }
 
 size_t smem_bytes_t(int fmt, int NT, int batch, int xs_stride) {
-  const size_t st = (size_t)STAGES * (fmt == VXB_Q4_0 ? Geo<0>::STAGE : Geo<1>::STAGE);
+  const size_t stage = fmt == VXB_Q4_0 ? Geo<0>::STAGE : Geo<1>::STAGE;
+  const size_t xstr = fmt == VXB_Q4_0 ? Geo<0>::XSTR : Geo<1>::XSTR;
   const size_t red = (size_t)8 * NT * ROWS_PER_CTA * 4;
-  return std::max(st, red) + (size_t)std::min(batch, 8 * NT) * xs_stride * 2;
+  if (NT > 1) return std::max((size_t)STAGES * (stage + (size_t)8 * NT * xstr * 2), red);
+  return std::max((size_t)STAGES * stage, red) + (size_t)std::min(batch, 8 * NT) * xs_stride * 2;
 }
 
 int xs_stride_for(int kc_max) { return kc_max + 16; }  // stride/2 = 8 (mod 32): conflict-free 8-byte loads
