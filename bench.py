@@ -28,6 +28,10 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tokens/s (7B-shape 4-bit) at 1/2/4/8 B200; dequant-GEMV HBM GB/s vs peak"
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes / algorithmic bytes of decode_attn_kernel, from an ncu capture of
+# the same kernel on batch 32, ctx 8192 (1.07446 GB read + 7.79 MB written for
+# 1.07427 GB of K/V/q/out): applied to the bench's launch to give its traffic
+ATTN_TRAFFIC_RATIO = (1.074456e9 + 7.78624e6) / 1.074266112e9
 CFG_7B = dict(vocab_size=32000, dim=4096, n_layers=32, n_heads=32, n_kv_heads=32, ffn_dim=11008)
 
 
@@ -43,6 +47,7 @@ def parse():
     ap.add_argument("--no-batch1", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-layers", type=int, default=1)
+    ap.add_argument("--no-gemv-sweep", action="store_true")
     return ap.parse_args()
 
 
@@ -275,12 +280,14 @@ def run_decode(dec, seq_ids, prompt, steps, warmup, ws, torch):
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.profiler.start()  # bounds a profiler capture to the timed region
     e0.record(stream)
     for _ in range(steps):
         tok.copy_(nxt)
         dec.step_device(seq_ids, tok, nxt)
     e1.record(stream)
     torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
     barrier(ws)
     return e0.elapsed_time(e1) * 1e-3, nxt
 
@@ -339,6 +346,18 @@ def main():
         t1, _ = run_decode(dec, sid, prompt[:1], args.steps, args.warmup, ws, torch)
         b1 = max_over_ranks(t1, ws)
 
+    # dequant-GEMV sweep (weights 4096x4096, 11008x4096, 4096x11008; Q4_0 and
+    # Q8_0; batch 1, 4, 16), each over rotating weight copies > 2x L2
+    gemv = None
+    if not args.no_gemv_sweep:
+        from vortex_b200 import kernel_bench as KB
+        rows = KB.gemv_sweep()
+        gemv = {"unit": "GB/s", "peak": hbm, "peak_source": peak_src,
+                "bytes": "N*K*(18 or 34)/32 + 2*B*K + 4*B*N per launch",
+                "cases": [{"fmt": r["fmt"], "N": r["N"], "K": r["K"], "batch": r["batch"], "us": round(r["us"], 2),
+                           "achieved": round(r["GBps"], 1), "frac": round(r["GBps"] / hbm, 3)} for r in rows]}
+        gemv["best_frac"] = max(c["frac"] for c in gemv["cases"])
+
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         per_token, desc = cpu_layer_sample(1)
@@ -360,9 +379,10 @@ def main():
             "batch1_ms_per_step": (b1 / args.steps * 1e3) if b1 else None,
             "roofline": {"kernel": "decode_attn_kernel (layer 0, batch %d)" % B, "bound": "hbm",
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                         "peak_source": peak_src, "traffic": None,
+                         "peak_source": peak_src, "traffic": attn_bytes * ATTN_TRAFFIC_RATIO,
                          "algorithmic_bytes": attn_bytes, "launch_us": t_attn * 1e6},
             "cpu_baseline": cpu,
+            "gemv": gemv,
             "clocks": clocks,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches_per_step * args.steps,
