@@ -179,6 +179,19 @@ int vxb_decode_attention(vxb_kv *kv, int layer, int n, const int64_t *h_seq_ids,
                          void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* K3: flash-attention forward (prefill). Replaces flash_attention_forward   */
+/* and multi_head_flash_attention (src/flash_attention.rs:53-159, 519-564):  */
+/* per head O = softmax(scale * Q K^T, causal mask key > query) V and        */
+/* lse = log-sum-exp of the scaled scores (natural log), as the reference's  */
+/* second output. Tensors are bf16 [B, S, heads, d] (per batch the          */
+/* reference's [N, H*d] rows, heads interleaved); K/V have Hkv heads, query */
+/* head h reads kv head h / (H / Hkv). d must be 128 (VXB_EUNSUPPORTED      */
+/* otherwise). d_lse (optional) is f32 [B, H, S]. Runs on tcgen05 / TMEM.   */
+/* ------------------------------------------------------------------------ */
+int vxb_flash_fwd(vxb_ctx *ctx, const uint16_t *d_q, const uint16_t *d_k, const uint16_t *d_v, int B, int H,
+                  int Hkv, int S, int d, float scale, int causal, uint16_t *d_o, float *d_lse, void *stream);
+
+/* ------------------------------------------------------------------------ */
 /* K5: single ops of the Llama-style block (stdlib/ai/transformer.vx).       */
 /* ------------------------------------------------------------------------ */
 /* layer_norm (RMS form with bias), stdlib/ai/transformer.vx:413-439:

@@ -1,0 +1,476 @@
+// K3: flash-attention forward on the 5th-generation tensor cores (tcgen05).
+//
+//   O[b, i, h, :] = sum_j softmax_j(scale * q_i . k_j  (j <= i if causal)) v_j
+//   lse[b, h, i]  = log sum_j exp(scale * q_i . k_j)
+//
+// Replaces flash_attention_forward / multi_head_flash_attention
+// (src/flash_attention.rs:53-159, 519-564). Inputs are [B, S, H, d] bf16 (per
+// batch the reference's [N, H*d] rows with the heads interleaved,
+// src/flash_attention.rs:545-551), d = 128; grouped K/V heads (Hkv | H).
+//
+// One CTA per (128-query tile, head, batch), 5 warps:
+//  * warp 4 (one elected thread) loads Q once and K/V tiles of 128 keys into
+//    a double-buffered ring with TMA (4-D tensor maps, 128-byte swizzle), and
+//    issues the MMAs: S = Q K^T (M=128, N=128, K=128 as 8 x K16) into TMEM
+//    columns [0,128), then O += P V (A = P from shared memory, B = V read
+//    MN-major) into TMEM columns [128,256). Completion is signalled to
+//    mbarriers with tcgen05.commit.
+//  * warps 0-3 own one query row each (TMEM lane = row): they read the row of
+//    S with tcgen05.ld, apply scale (log2 domain) and the causal / length mask,
+//    keep the running max m and sum l, rescale the row of O in TMEM when m
+//    grows, and write P = 2^(s - m) as bf16 into shared memory in the swizzled
+//    K-major layout the MMA reads.
+//  * The MMA of S for the next tile is issued as soon as the softmax warps have
+//    read the current S, so it overlaps their exponentials.
+// Every mbarrier wait is bounded (clock64); a timeout sets the context's
+// device error word and the kernel runs to completion. No multicast.
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <mutex>
+
+#include "vxb_internal.h"
+
+using namespace vxb;
+
+namespace {
+
+constexpr int D = 128;        // head dim
+constexpr int BM = 128;       // queries per CTA
+constexpr int BN = 128;       // keys per tile
+constexpr int THREADS = 160;  // 4 softmax warps + 1 load/MMA warp
+constexpr int TILE_BYTES = BM * D * 2;  // 32 KB: two 64-column slabs of [128 rows x 128 B]
+constexpr int SLAB = 128 * 128;         // bytes of one slab
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + TILE_BYTES;       // 2 stages
+constexpr int OFF_V = OFF_K + 2 * TILE_BYTES;   // 2 stages
+constexpr int OFF_P = OFF_V + 2 * TILE_BYTES;   // P = hi + lo, two bf16 tiles
+constexpr int SMEM_BYTES = OFF_P + 2 * TILE_BYTES;  // 224 KB
+constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;   // + alignment slack
+constexpr uint32_t TMEM_COLS = 256;
+
+struct FlashArgs {
+  uint16_t *o;
+  float *lse;
+  int *err;
+  int B, H, Hkv, S, n_qtiles;
+  float scale_log2;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Bounded wait for the phase of the given parity; false after ~2^31 cycles.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (clock64() - t0 > (1ll << 31)) return false;
+  }
+}
+
+__device__ __forceinline__ void wait_or_flag(uint64_t *bar, uint32_t parity, int *err) {
+  if (!mbar_wait(bar, parity)) atomicExch(err, 1);
+}
+
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int c0, int c1, int c2, int c3,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(sbo >> 4) << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor, kind::f16: bf16 x bf16 -> f32, A K-major, B K- or
+// MN-major, M = 128, N = 128.
+__host__ __device__ constexpr uint32_t idesc_bf16(bool b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
+         ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+      "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+      "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])),
+      "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+      "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])),
+      "r"(__float_as_uint(v[23])), "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])),
+      "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])),
+      "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+template <bool CAUSAL>
+__global__ void __launch_bounds__(THREADS, 1)
+    flash_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                     const __grid_constant__ CUtensorMap tv, const FlashArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t bar_q, kv_full[2], kv_empty[2], s_full, s_free, p_full, o_done;
+  __shared__ uint32_t tmem_base_s;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = a.n_qtiles - 1 - (int)blockIdx.x;  // longest causal rows first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (a.H / a.Hkv);
+  const int q0 = qt * BM;
+  const int kv_tiles = (a.S + BN - 1) / BN;
+  const int n_kv = CAUSAL ? min(qt + 1, kv_tiles) : kv_tiles;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (threadIdx.x == 32) {
+    mbar_init(&bar_q, 1);
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    mbar_init(&s_full, 1);
+    mbar_init(&s_free, 4);
+    mbar_init(&p_full, 4);
+    mbar_init(&o_done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_s;
+  const uint32_t tS = tmem, tO = tmem + BN;
+
+  if (warp == 4) {
+    // ---------------- loads and MMA issue (one thread)
+    if (lane == 0) {
+      const uint32_t sQ = smem_u32(sm + OFF_Q), sP = smem_u32(sm + OFF_P);
+      mbar_expect_tx(&bar_q, TILE_BYTES);
+      tma_load_4d(sm + OFF_Q, &tq, 0, h, q0, b, &bar_q);
+      tma_load_4d(sm + OFF_Q + SLAB, &tq, 64, h, q0, b, &bar_q);
+      auto load_kv = [&](int j, int st) {
+        mbar_expect_tx(&kv_full[st], 2 * TILE_BYTES);
+        uint8_t *k = sm + OFF_K + st * TILE_BYTES, *v = sm + OFF_V + st * TILE_BYTES;
+        tma_load_4d(k, &tk, 0, hk, j * BN, b, &kv_full[st]);
+        tma_load_4d(k + SLAB, &tk, 64, hk, j * BN, b, &kv_full[st]);
+        tma_load_4d(v, &tv, 0, hk, j * BN, b, &kv_full[st]);
+        tma_load_4d(v + SLAB, &tv, 64, hk, j * BN, b, &kv_full[st]);
+      };
+      for (int j = 0; j < min(2, n_kv); j++) load_kv(j, j);
+      wait_or_flag(&bar_q, 0, a.err);
+      constexpr uint32_t ID_QK = idesc_bf16(false), ID_PV = idesc_bf16(true);
+      auto issue_pv = [&](int j) {
+        const int st = j & 1;
+        const uint32_t sV = smem_u32(sm + OFF_V + st * TILE_BYTES);
+        // O += P_hi V + P_lo V: the K dimension runs over the keys twice
+#pragma unroll
+        for (int t = 0; t < 2 * BN / 16; t++) {
+          const int tk = t & 7;
+          // A = P (K-major over keys): slab tk/4, 32 bytes per k16 step
+          const uint64_t ad = sw128_desc(sP + (t >> 3) * TILE_BYTES + (tk >> 2) * SLAB + (tk & 3) * 32, 16, 1024);
+          // B = V read MN-major: 16 keys = two 8-row groups of 1024 bytes; the
+          // two 64-column slabs of d are 16 KB apart
+          const uint64_t bd = sw128_desc(sV + tk * 2048, SLAB, 1024);
+          umma_bf16(tO, ad, bd, ID_PV, (j > 0 || t > 0) ? 1u : 0u);
+        }
+        umma_commit(&o_done);
+        umma_commit(&kv_empty[st]);
+      };
+      for (int j = 0; j < n_kv; j++) {
+        const int st = j & 1;
+        wait_or_flag(&kv_full[st], (j >> 1) & 1, a.err);
+        if (j > 0) wait_or_flag(&s_free, (j - 1) & 1, a.err);
+        tc_fence_after();
+        const uint32_t sK = smem_u32(sm + OFF_K + st * TILE_BYTES);
+#pragma unroll
+        for (int t = 0; t < D / 16; t++) {
+          const uint32_t off = (t >> 2) * SLAB + (t & 3) * 32;
+          umma_bf16(tS, sw128_desc(sQ + off, 16, 1024), sw128_desc(sK + off, 16, 1024), ID_QK, t > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full);
+        if (j > 0) {
+          wait_or_flag(&p_full, (j - 1) & 1, a.err);
+          tc_fence_after();
+          issue_pv(j - 1);
+          if (j + 1 < n_kv) {
+            // stage of tile j-1 is free once its PV has completed
+            wait_or_flag(&kv_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, a.err);
+            load_kv(j + 1, (j + 1) & 1);
+          }
+        }
+      }
+      wait_or_flag(&p_full, (n_kv - 1) & 1, a.err);
+      tc_fence_after();
+      issue_pv(n_kv - 1);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- softmax: thread r owns query row q0 + r (TMEM lane r)
+    const int r = threadIdx.x;
+    const int row = q0 + r;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    uint8_t *prow = sm + OFF_P + r * 128;
+    float m = -INFINITY, l = 0.f;
+    for (int j = 0; j < n_kv; j++) {
+      wait_or_flag(&s_full, j & 1, a.err);
+      tc_fence_after();
+      float s[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; c++) tmem_ld32(tS + lane_off + c * 32, *reinterpret_cast<float(*)[32]>(s + c * 32));
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free);
+
+      const int k0 = j * BN;
+      const int lim = CAUSAL ? min(a.S - 1, row) : a.S - 1;  // last visible key
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; c++) {
+        const float v = (k0 + c <= lim) ? s[c] * a.scale_log2 : -INFINITY;
+        s[c] = v;
+        mx = fmaxf(mx, v);
+      }
+      const float m_new = fmaxf(m, mx);
+      const float mb = m_new == -INFINITY ? 0.f : m_new;  // rows with no visible key yet
+      const float alpha = ex2(m - mb);
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN; c++) {
+        const float p = ex2(s[c] - mb);
+        s[c] = p;
+        sum += p;
+      }
+      l = l * alpha + sum;
+      m = m_new;
+
+      if (j > 0) {
+        // O holds the tiles before j: wait for the last P.V, then rescale
+        wait_or_flag(&o_done, (j - 1) & 1, a.err);
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+          for (int c = 0; c < D / 32; c++) {
+            float o[32];
+            tmem_ld32(tO + lane_off + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; i++) o[i] *= alpha;
+            tmem_st32(tO + lane_off + c * 32, o);
+          }
+          tmem_wait_st();
+        }
+      }
+      // P as bf16 hi + lo (p - hi rounded again: 16 significant bits, so the
+      // P.V product keeps the precision of the f32 softmax) into the swizzled
+      // K-major layout: 16-byte chunk ch of the row sits at chunk position
+      // ch ^ (row % 8) of its 128-byte slab row
+#pragma unroll
+      for (int ch = 0; ch < BN / 8; ch++) {
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const float p0 = s[ch * 8 + 2 * e], p1 = s[ch * 8 + 2 * e + 1];
+          hi[e] = pack_bf16(p0, p1);
+          lo[e] = pack_bf16(p0 - __uint_as_float(hi[e] << 16), p1 - __uint_as_float(hi[e] & 0xFFFF0000u));
+        }
+        const int slab = ch >> 3, pos = (ch & 7) ^ (r & 7);
+        *reinterpret_cast<uint4 *>(prow + slab * SLAB + pos * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4 *>(prow + TILE_BYTES + slab * SLAB + pos * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full);
+    }
+    // ---------------- epilogue: O / l (bf16) and lse (natural log)
+    wait_or_flag(&o_done, (n_kv - 1) & 1, a.err);
+    tc_fence_after();
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const bool live = row < a.S;
+    uint16_t *orow = a.o + (((size_t)b * a.S + (live ? row : 0)) * a.H + h) * D;
+#pragma unroll
+    for (int c = 0; c < D / 32; c++) {
+      float o[32];
+      tmem_ld32(tO + lane_off + c * 32, o);
+      tmem_wait_ld();
+      if (live) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          uint4 w;
+          w.x = pack_bf16(o[q * 8 + 0] * inv, o[q * 8 + 1] * inv);
+          w.y = pack_bf16(o[q * 8 + 2] * inv, o[q * 8 + 3] * inv);
+          w.z = pack_bf16(o[q * 8 + 4] * inv, o[q * 8 + 5] * inv);
+          w.w = pack_bf16(o[q * 8 + 6] * inv, o[q * 8 + 7] * inv);
+          *reinterpret_cast<uint4 *>(orow + c * 32 + q * 8) = w;
+        }
+      }
+    }
+    if (live && a.lse) a.lse[((size_t)b * a.H + h) * a.S + row] = l > 0.f ? (m + __log2f(l)) * 0.69314718055994531f : -INFINITY;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+}
+
+// ---------------- host: tensor maps through the driver entry point
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn(vxb_ctx *ctx) {
+  static std::mutex mu;
+  static EncodeTiledFn fn = nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !p) {
+      cudaGetLastError();
+      set_error(ctx, VXB_ECUDA, "vxb_flash_fwd: cuTensorMapEncodeTiled is not available from the driver");
+      return nullptr;
+    }
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// [B, S, heads, 128] bf16 -> 4-D map (d, head, s, b), box (64, 1, 128, 1)
+int make_map(vxb_ctx *ctx, EncodeTiledFn fn, CUtensorMap *map, const void *base, int B, int S, int heads) {
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)heads, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)heads * D * 2, (cuuint64_t)S * heads * D * 2};
+  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(ctx, VXB_EINVAL, "vxb_flash_fwd: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return VXB_OK;
+}
+
+template <bool CAUSAL>
+int launch(vxb_ctx *ctx, const CUtensorMap &q, const CUtensorMap &k, const CUtensorMap &v, const FlashArgs &a,
+           cudaStream_t st) {
+  static bool configured[64] = {false};
+  const int dev = ctx->device & 63;
+  if (!configured[dev]) {
+    VXB_CUDA_TRY(ctx, cudaFuncSetAttribute(flash_fwd_kernel<CAUSAL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           SMEM_ALLOC));
+    configured[dev] = true;
+  }
+  dim3 grid(a.n_qtiles, a.H, a.B);
+  flash_fwd_kernel<CAUSAL><<<grid, THREADS, SMEM_ALLOC, st>>>(q, k, v, a);
+  return launch_check(ctx, "flash_fwd_kernel");
+}
+
+}  // namespace
+
+VXB_API int vxb_flash_fwd(vxb_ctx *ctx, const uint16_t *d_q, const uint16_t *d_k, const uint16_t *d_v, int B, int H,
+                          int Hkv, int S, int d, float scale, int causal, uint16_t *d_o, float *d_lse, void *stream) {
+  if (!ctx) return set_error(nullptr, VXB_EINVAL, "vxb_flash_fwd: null context");
+  if (d != D) return set_error(ctx, VXB_EUNSUPPORTED, "vxb_flash_fwd: head_dim %d (only 128 is implemented)", d);
+  if (B < 1 || H < 1 || Hkv < 1 || S < 1 || H % Hkv)
+    return set_error(ctx, VXB_EINVAL, "vxb_flash_fwd: bad shape B=%d H=%d Hkv=%d S=%d", B, H, Hkv, S);
+  if (!d_q || !d_k || !d_v || !d_o) return set_error(ctx, VXB_EINVAL, "vxb_flash_fwd: null pointer");
+  if (((uintptr_t)d_q | (uintptr_t)d_k | (uintptr_t)d_v | (uintptr_t)d_o) % 16)
+    return set_error(ctx, VXB_EINVAL, "vxb_flash_fwd: tensors must be 16-byte aligned");
+  if (!(scale > 0.f)) return set_error(ctx, VXB_EINVAL, "vxb_flash_fwd: scale must be positive");
+  if (int rc = use_device(ctx)) return rc;
+  if (int rc = ws_reserve(ctx, 0, 0)) return rc;  // device error word
+  EncodeTiledFn fn = encode_fn(ctx);
+  if (!fn) return VXB_ECUDA;
+  CUtensorMap mq, mk, mv;
+  if (int rc = make_map(ctx, fn, &mq, d_q, B, S, H)) return rc;
+  if (int rc = make_map(ctx, fn, &mk, d_k, B, S, Hkv)) return rc;
+  if (int rc = make_map(ctx, fn, &mv, d_v, B, S, Hkv)) return rc;
+  FlashArgs a;
+  a.o = d_o;
+  a.lse = d_lse;
+  a.err = ctx->d_err;
+  a.B = B;
+  a.H = H;
+  a.Hkv = Hkv;
+  a.S = S;
+  a.n_qtiles = (S + BM - 1) / BM;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  cudaStream_t st = (cudaStream_t)stream;
+  return causal ? launch<true>(ctx, mq, mk, mv, a, st) : launch<false>(ctx, mq, mk, mv, a, st);
+}

@@ -2,6 +2,7 @@
 
     python -m vortex_b200.kernel_bench gemv [--fmt Q4_0] [--n 11008] [--k 4096] [--batch 1]
     python -m vortex_b200.kernel_bench attn [--ctx 8192] [--dtype bf16]
+    python -m vortex_b200.kernel_bench flash [--b 4] [--h 32] [--s 4096] [--non-causal]
 
 Each case streams its operands from HBM: the GEMV rotates over enough distinct
 weight copies to exceed twice the L2 (126 MB), the attention reads a KV cache
@@ -126,6 +127,27 @@ def attn_case(ctx: int, dtype: str = "bf16", n: int = 32, Hq: int = 32, Hkv: int
     return res
 
 
+def flash_case(B: int = 4, H: int = 32, S: int = 4096, causal: bool = True, reps: int = 10, seed: int = 0):
+    """Flash-attention forward, q/k/v bf16 [B, S, H, 128] ~ N(0, 1), scale
+    1/sqrt(128). FLOPs count only the visible (unmasked) score pairs:
+    4 * B * H * d * S(S+1)/2 causal, 4 * B * H * d * S^2 otherwise."""
+    import torch
+
+    from . import attention as A
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    q, k, v = (torch.randn(B, S, H, 128, device="cuda", generator=gen).bfloat16() for _ in range(3))
+    o, lse = A.flash_attention(q, k, v, causal=causal)
+
+    def run():
+        A.flash_attention(q, k, v, causal=causal, out=o, lse=lse)
+
+    t = _graph_time(torch, run, 1, reps)
+    pairs = S * (S + 1) // 2 if causal else S * S
+    flops = 4 * B * H * 128 * pairs
+    return {"B": B, "H": H, "S": S, "d": 128, "causal": causal, "us": t * 1e6, "TFLOPs": flops / t / 1e12,
+            "flops": flops}
+
+
 def main():
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="what", required=True)
@@ -135,6 +157,12 @@ def main():
     g.add_argument("--k", type=int, default=None)
     g.add_argument("--batch", type=int, nargs="*", default=[1, 4, 16])
     g.add_argument("--reps", type=int, default=20)
+    f = sub.add_parser("flash")
+    f.add_argument("--b", type=int, default=4)
+    f.add_argument("--h", type=int, default=32)
+    f.add_argument("--s", type=int, default=4096)
+    f.add_argument("--non-causal", action="store_true")
+    f.add_argument("--reps", type=int, default=10)
     a = sub.add_parser("attn")
     a.add_argument("--ctx", type=int, nargs="*", default=[1024, 8192, 32768])
     a.add_argument("--dtype", nargs="*", default=["bf16", "int8"])
@@ -147,6 +175,8 @@ def main():
         shapes = [(args.n, args.k)] if args.n and args.k else [(4096, 4096), (11008, 4096), (4096, 11008)]
         for r in gemv_sweep(shapes, fmts, args.batch, args.reps):
             print(json.dumps(r), flush=True)
+    elif args.what == "flash":
+        print(json.dumps(flash_case(args.b, args.h, args.s, not args.non_causal, args.reps)), flush=True)
     else:
         for dt in args.dtype:
             for c in args.ctx:
