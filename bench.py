@@ -7,10 +7,12 @@ vocab 32000, every linear Q4_0 (block 32, f16 scales) from N(0, 0.02)
 synthetic weights, a 2048-token random-id prompt per sequence, then decode
 steps at batch 32 (headline) and batch 1. KV cache bf16, paged.
 
-Prints one JSON line (rank 0). With torchrun (N > 1) every rank runs an
-independent replica on its own GPU; value is the sum over ranks, timed as the
-max over ranks. --impl reference times the CPU oracle port of the reference
-path (rank 0 only).
+Prints one JSON line (rank 0). With torchrun (N > 1) the ranks run one
+tensor-parallel decoder (heads, FFN rows and vocabulary split over the N GPUs,
+NCCL all-reduce of the residual stream twice per layer): the batch is the same
+at every N, value = tokens/s of the job, timed as the max over ranks (strong
+scaling). --impl reference times the CPU oracle port of the reference path
+(rank 0 only).
 """
 from __future__ import annotations
 
@@ -126,7 +128,7 @@ def dist_setup(gpus):
         rank = int(os.environ["RANK"])
         local = int(os.environ.get("LOCAL_RANK", rank))
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
         return rank, ws, local
     return 0, 1, 0
 
@@ -307,9 +309,13 @@ def main():
     B = args.batch
     max_seq = args.prompt_len + args.warmup + args.steps + args.e2e_steps + 8
     t_setup = time.perf_counter()
-    dec = D.Decoder(max_batch=B, max_seq=max_seq, **CFG_7B)
+    comm = None
+    if ws > 1:
+        from vortex_b200 import comm as C
+        comm = C.Comm(ws, rank, C.share_unique_id(rank), device=local)
+    dec = D.Decoder(max_batch=B, max_seq=max_seq, comm=comm, **CFG_7B)
     dec.init_random(seed=1234, sigma=0.02)
-    rng = np.random.default_rng(2024 + rank)
+    rng = np.random.default_rng(2024)
     prompt = rng.integers(0, CFG_7B["vocab_size"], size=(B, args.prompt_len))
     seq_ids = list(range(B))
 
@@ -318,7 +324,7 @@ def main():
     t_dev, nxt = run_decode(dec, seq_ids, prompt, args.steps, args.warmup, ws, torch)
     clocks = sampler.stop()
     t_max = max_over_ranks(t_dev, ws)
-    value = ws * B * args.steps / t_max
+    value = B * args.steps / t_max
 
     # end to end through the host-buffer C ABI call (tokens H2D, next tokens D2H)
     host_tok = nxt.cpu().numpy().astype(np.int32)
@@ -327,15 +333,17 @@ def main():
     for _ in range(args.e2e_steps):
         host_tok = dec.step(seq_ids, host_tok)
     t_e2e = max_over_ranks(time.perf_counter() - t0, ws)
-    e2e = ws * B * args.e2e_steps / t_e2e
+    e2e = B * args.e2e_steps / t_e2e
     h2d = B * 4 + CFG_7B["n_layers"] * B * 16 + B * 4
     d2h = B * 4
 
-    # dominant kernel at this workload: decode attention (KV bytes >> weights)
+    # dominant kernel at this workload: decode attention (KV bytes >> weights),
+    # this rank's heads
     hbm, peak_src = measured_peaks()
-    t_attn, lens = time_attention(dec, seq_ids, (CFG_7B["n_heads"], CFG_7B["dim"] // CFG_7B["n_heads"]))
     hd = CFG_7B["dim"] // CFG_7B["n_heads"]
-    attn_bytes = sum(lens) * CFG_7B["n_kv_heads"] * hd * 2 * 2 + 2 * B * CFG_7B["dim"] * 2
+    hq_loc, hkv_loc = CFG_7B["n_heads"] // ws, CFG_7B["n_kv_heads"] // ws
+    t_attn, lens = time_attention(dec, seq_ids, (hq_loc, hd))
+    attn_bytes = sum(lens) * hkv_loc * hd * 2 * 2 + 2 * B * hq_loc * hd * 2
     achieved = attn_bytes / t_attn / 1e9
 
     # batch 1 on a freed slot
@@ -345,11 +353,12 @@ def main():
         sid = [10_000]
         t1, _ = run_decode(dec, sid, prompt[:1], args.steps, args.warmup, ws, torch)
         b1 = max_over_ranks(t1, ws)
+    barrier(ws)
 
     # dequant-GEMV sweep (weights 4096x4096, 11008x4096, 4096x11008; Q4_0 and
     # Q8_0; batch 1, 4, 16), each over rotating weight copies > 2x L2
     gemv = None
-    if not args.no_gemv_sweep:
+    if rank == 0 and not args.no_gemv_sweep:
         from vortex_b200 import kernel_bench as KB
         rows = KB.gemv_sweep()
         gemv = {"unit": "GB/s", "peak": hbm, "peak_source": peak_src,
@@ -363,19 +372,21 @@ def main():
         per_token, desc = cpu_layer_sample(1)
         cpu = {"value": 1.0 / per_token, "unit": "tokens/s", "cores": 1, "kind": "port", "sample": desc}
 
-    launches_per_step = 1 + CFG_7B["n_layers"] * 10 + 3
+    # our kernels per step (NCCL's own kernels not counted): embed, 10 per
+    # layer, final norm, LM-head GEMV, argmax (key + token with tp > 1)
+    launches_per_step = 1 + CFG_7B["n_layers"] * 10 + (3 if ws == 1 else 4)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_max / args.steps * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "7B-shape Llama decoder decode (32 layers, d4096, 32x128 heads, SwiGLU 11008, "
                                    "vocab 32000, Q4_0 linears, bf16 paged KV), random weights N(0,0.02)",
-                       "global_batch": ws * B, "batch_per_gpu": B, "seq_len": args.prompt_len,
+                       "global_batch": B, "seq_len": args.prompt_len,
                        "prompt_len": args.prompt_len, "decode_steps": args.steps,
-                       "parallelism": "replicas" if ws > 1 else "single",
+                       "parallelism": f"tp{ws}" if ws > 1 else "single",
                        "l2": "inputs larger than L2 (3.7 GB weights + KV per step)"},
-            "batch1_tokens_per_s": (ws * args.steps / b1) if b1 else None,
+            "batch1_tokens_per_s": (args.steps / b1) if b1 else None,
             "batch1_ms_per_step": (b1 / args.steps * 1e3) if b1 else None,
             "roofline": {"kernel": "decode_attn_kernel (layer 0, batch %d)" % B, "bound": "hbm",
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
@@ -389,7 +400,10 @@ def main():
             "setup_s": time.perf_counter() - t_setup,
         }
         print(json.dumps(line), flush=True)
-    dec.close()
+    barrier(ws)
+    dec.close()  # its CUDA graphs hold NCCL calls: release them before the communicator
+    if comm is not None:
+        comm.close()
     if ws > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

@@ -205,6 +205,19 @@ int vxb_swiglu(vxb_ctx *ctx, const float *d_gu, int rows, int ffn, uint16_t *d_a
 int vxb_argmax(vxb_ctx *ctx, const float *d_logits, int rows, int vocab, int32_t *d_out, void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* Tensor-parallel communicator. Replaces the nccl_ffi.rs externs            */
+/* (src/nccl_ffi.rs:12-72): NCCL (opened at run time) over NVLink/NVSwitch. */
+/* Rank 0 makes the 128-byte unique id, the caller shares it with the other */
+/* ranks, every rank joins. Collectives run on the given stream.            */
+/* ------------------------------------------------------------------------ */
+typedef struct vxb_comm vxb_comm;
+int vxb_nccl_unique_id(void *h_out128);
+int vxb_comm_init(vxb_ctx *ctx, int nranks, int rank, const void *h_unique_id128, vxb_comm **out);
+int vxb_comm_destroy(vxb_comm *comm);
+/* In-place sum over ranks of count elements of dtype VXB_F32 or VXB_BF16. */
+int vxb_allreduce_sum(vxb_comm *comm, void *d_buf, size_t count, int dtype, void *stream);
+
+/* ------------------------------------------------------------------------ */
 /* Decoder: Llama-style block stack (stdlib/ai/transformer.vx:958-1156) with  */
 /* a paged KV cache, one token per sequence per step (greedy next token).    */
 /* Stands behind the transformer_* builtins / TransformerModel::forward call */
@@ -221,6 +234,15 @@ typedef struct vxb_decoder_config {
 } vxb_decoder_config;
 typedef struct vxb_decoder vxb_decoder;
 int vxb_decoder_create(vxb_ctx *ctx, const vxb_decoder_config *cfg, vxb_decoder **out);
+/* Tensor-parallel decoder over comm's ranks (one process per GPU, every rank
+ * calls the same functions with the same arguments): QKV and gate/up are
+ * split by output rows (heads), O and down by input columns, followed by an
+ * all-reduce (sum) of the residual stream; the LM head is split by vocabulary
+ * rows with a distributed argmax. nranks must divide n_heads, n_kv_heads and
+ * vocab_size, and dim / nranks, ffn_dim / nranks must be multiples of 32.
+ * init_random and set_weight take the full model on every rank and keep the
+ * rank's part, so any rank count gives the same model. */
+int vxb_decoder_create_tp(vxb_ctx *ctx, const vxb_decoder_config *cfg, vxb_comm *comm, vxb_decoder **out);
 int vxb_decoder_destroy(vxb_decoder *d);
 /* init_random_weights (stdlib/ai/transformer.vx:661-725): linears and
  * embedding ~N(0, sigma) from a counter-based generator, norms w=1, b=0. */

@@ -81,7 +81,12 @@ SIGNATURES = {
     "vxb_rmsnorm": (_I, [_P, _P, _P, _P, _I, _I, ctypes.c_float, _P, _P]),
     "vxb_swiglu": (_I, [_P, _P, _I, _I, _P, _P]),
     "vxb_argmax": (_I, [_P, _P, _I, _I, _P, _P]),
+    "vxb_nccl_unique_id": (_I, [_P]),
+    "vxb_comm_init": (_I, [_P, _I, _I, _P, ctypes.POINTER(_P)]),
+    "vxb_comm_destroy": (_I, [_P]),
+    "vxb_allreduce_sum": (_I, [_P, _P, _SZ, _I, _P]),
     "vxb_decoder_create": (_I, [_P, _P, ctypes.POINTER(_P)]),
+    "vxb_decoder_create_tp": (_I, [_P, _P, _P, ctypes.POINTER(_P)]),
     "vxb_decoder_destroy": (_I, [_P]),
     "vxb_decoder_init_random": (_I, [_P, ctypes.c_uint64, ctypes.c_float]),
     "vxb_decoder_set_weight": (_I, [_P, _I, _I, _P, _SZ]),

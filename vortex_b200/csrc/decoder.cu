@@ -16,12 +16,24 @@
 //   x  += W2 bf16(silu(g) * u)                        (GEMV epilogue adds x)
 // then logits = Wout rmsnorm_bias(x) and the greedy argmax (transformer.vx:
 // 1120-1156, 1163-1177).
+//
+// Tensor parallel (vxb_decoder_create_tp, one process per GPU): rank r holds
+// the q heads [r*H/tp, (r+1)*H/tp) and the matching kv heads (fused QKV rows
+// and its KV cache), the gate/up rows [r*F/tp, (r+1)*F/tp), the matching
+// input columns of Wo and W2, and the vocabulary rows [r*V/tp, (r+1)*V/tp) of
+// the output projection. After the Wo and W2 GEMVs (rank 0 adds the residual
+// in the epilogue) the residual stream is summed over ranks with an NCCL
+// all-reduce, so every rank holds the full x for the norms; the greedy token
+// is a max-reduction of (logit, index) keys. All collectives are recorded in
+// the step's CUDA graph.
 #include <algorithm>
 #include <cmath>
+#include <initializer_list>
 #include <cstring>
 #include <map>
 #include <vector>
 
+#include "comm.h"
 #include "decode_attn.h"
 #include "gemv.h"
 #include "kv_cache.h"
@@ -33,7 +45,13 @@ using namespace vxb;
 struct vxb_decoder {
   vxb_ctx *ctx = nullptr;
   vxb_decoder_config cfg{};
-  int kvdim = 0, qkv_n = 0;
+  // this rank's slice: q / kv heads, q width, kv width (kvdim), ffn rows,
+  // vocabulary rows; qkv_n = rows of the fused local QKV projection
+  vxb_comm *comm = nullptr;
+  int tp = 1, rank = 0;
+  int hq = 0, hkv = 0, qdim = 0, kvdim = 0, ffn = 0, vocab = 0, qkv_n = 0;
+  unsigned long long *d_keys = nullptr;           // [max_batch] argmax keys (tp > 1)
+  float *logits_all = nullptr, *logits_full = nullptr;  // gathered shards (tp > 1)
   struct Layer {
     void *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wdown = nullptr;
     float *ln1_w = nullptr, *ln1_b = nullptr, *ln2_w = nullptr, *ln2_b = nullptr;
@@ -109,8 +127,19 @@ int fill(vxb_decoder *d, float *p, size_t n, float v) {
   return launch_check(d->ctx, "fill_f32_kernel");
 }
 
-// random N(0, sigma) weights [N, K] -> quantized blocks -> tiled (chunks of rows)
-int random_tiled(vxb_decoder *d, int N, int K, uint64_t seed, float sigma, void **tiled) {
+// One row block of a generated full matrix: rows [row0, row0 + rows) and
+// columns [col0, col0 + cols) of the [*, ld] matrix of `seed`, placed at row
+// `dst_row` of the local matrix.
+struct GenPart {
+  int dst_row, rows;
+  size_t row0, col0, ld;
+};
+
+// Random N(0, sigma) weights of a local [N, K] matrix assembled from blocks of
+// full matrices (the same values for every tensor-parallel layout), quantized
+// to blocks and tiled.
+int random_tiled(vxb_decoder *d, int N, int K, std::initializer_list<GenPart> parts, uint64_t seed, float sigma,
+                 void **tiled) {
   const int fmt = d->cfg.weight_fmt;
   const size_t tb = vxb_tiled_bytes(fmt, N, K);
   if (int rc = dalloc(d, tiled, tb)) return rc;
@@ -123,7 +152,9 @@ int random_tiled(vxb_decoder *d, int N, int K, uint64_t seed, float sigma, void 
     cudaFree(blocks);
     return set_error(d->ctx, VXB_ENOMEM, "decoder: temporary allocation for weight generation failed");
   }
-  int rc = normal_fill(d->ctx, tmp, n, seed, 0, sigma, d->stream);
+  int rc = VXB_OK;
+  for (const GenPart &p : parts)
+    if (!rc) rc = normal_fill_block(d->ctx, tmp + (size_t)p.dst_row * K, p.rows, K, p.row0, p.col0, p.ld, seed, sigma, d->stream);
   if (!rc) rc = vxb_quantize_blocks(d->ctx, fmt, tmp, n, blocks, d->stream);
   if (!rc) rc = vxb_tile_weights(d->ctx, fmt, blocks, N, K, *tiled, d->stream);
   cudaStreamSynchronize(d->stream);
@@ -138,7 +169,9 @@ int capture_step(vxb_decoder *d, int B, vxb_decoder::Graph &g);
 
 // ---------------------------------------------------------------- lifecycle
 
-VXB_API int vxb_decoder_create(vxb_ctx *ctx, const vxb_decoder_config *cfg, vxb_decoder **out) {
+namespace {
+
+int decoder_create(vxb_ctx *ctx, const vxb_decoder_config *cfg, vxb_comm *comm, vxb_decoder **out) {
   if (!ctx || !cfg || !out) return set_error(ctx, VXB_EINVAL, "vxb_decoder_create: null argument");
   *out = nullptr;
   const vxb_decoder_config &c = *cfg;
@@ -152,25 +185,42 @@ VXB_API int vxb_decoder_create(vxb_ctx *ctx, const vxb_decoder_config *cfg, vxb_
   if (c.dim % 32 || c.ffn_dim % 32) return set_error(ctx, VXB_EINVAL, "vxb_decoder_create: dim and ffn_dim must be multiples of 32");
   if (c.max_batch > 32) return set_error(ctx, VXB_EUNSUPPORTED, "vxb_decoder_create: max_batch %d > 32", c.max_batch);
   if (c.weight_fmt != VXB_Q4_0 && c.weight_fmt != VXB_Q8_0) return set_error(ctx, VXB_EINVAL, "vxb_decoder_create: weight_fmt");
+  const int tp = comm ? comm->nranks : 1;
+  if (c.n_heads % tp || c.n_kv_heads % tp || c.vocab_size % tp || (c.dim / tp) % 32 || (c.ffn_dim / tp) % 32 ||
+      c.dim % tp || c.ffn_dim % tp)
+    return set_error(ctx, VXB_EINVAL,
+                     "vxb_decoder_create_tp: %d ranks must divide n_heads, n_kv_heads and vocab_size, and dim / ranks, "
+                     "ffn_dim / ranks must be multiples of 32", tp);
   if (int rc = use_device(ctx)) return rc;
   vxb_decoder *d = new vxb_decoder();
   d->ctx = ctx;
   d->cfg = c;
+  d->comm = comm;
+  d->tp = tp;
+  d->rank = comm ? comm->rank : 0;
   if (d->cfg.kv_block_size <= 0) d->cfg.kv_block_size = 16;
   if (d->cfg.norm_eps <= 0.f) d->cfg.norm_eps = 1e-5f;
-  d->kvdim = c.n_kv_heads * hd;
-  d->qkv_n = c.dim + 2 * d->kvdim;
+  d->hq = c.n_heads / tp;
+  d->hkv = c.n_kv_heads / tp;
+  d->qdim = d->hq * hd;
+  d->kvdim = d->hkv * hd;
+  d->ffn = c.ffn_dim / tp;
+  d->vocab = c.vocab_size / tp;
+  d->qkv_n = d->qdim + 2 * d->kvdim;
   int rc = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) == cudaSuccess ? VXB_OK : VXB_ECUDA;
   const int B = c.max_batch, L = c.n_layers;
   if (!rc) rc = dalloc_t(d, &d->x, (size_t)B * c.dim);
   if (!rc) rc = dalloc_t(d, &d->qkv, (size_t)B * d->qkv_n);
-  if (!rc) rc = dalloc_t(d, &d->gu, (size_t)B * 2 * c.ffn_dim);
-  if (!rc) rc = dalloc_t(d, &d->logits, (size_t)B * c.vocab_size);
+  if (!rc) rc = dalloc_t(d, &d->gu, (size_t)B * 2 * d->ffn);
+  if (!rc) rc = dalloc_t(d, &d->logits, (size_t)B * d->vocab);
   if (!rc) rc = dalloc_t(d, &d->h, (size_t)B * (c.dim > c.ffn_dim ? c.dim : c.ffn_dim));
-  if (!rc) rc = dalloc_t(d, &d->q, (size_t)B * c.dim);
+  if (!rc) rc = dalloc_t(d, &d->q, (size_t)B * d->qdim);
   if (!rc) rc = dalloc_t(d, &d->kvnew, (size_t)B * 2 * d->kvdim);
-  if (!rc) rc = dalloc_t(d, &d->attn, (size_t)B * c.dim);
-  if (!rc) rc = dalloc_t(d, &d->act, (size_t)B * c.ffn_dim);
+  if (!rc) rc = dalloc_t(d, &d->attn, (size_t)B * d->qdim);
+  if (!rc) rc = dalloc_t(d, &d->act, (size_t)B * d->ffn);
+  if (!rc && tp > 1) rc = dalloc_t(d, &d->d_keys, (size_t)B);
+  if (!rc && tp > 1) rc = dalloc_t(d, &d->logits_all, (size_t)B * c.vocab_size);
+  if (!rc && tp > 1) rc = dalloc_t(d, &d->logits_full, (size_t)B * c.vocab_size);
   d->stage_bytes = (size_t)L * B * sizeof(KVPlace) + 2 * (size_t)B * sizeof(int32_t);
   if (!rc) rc = dalloc(d, (void **)&d->d_stage, d->stage_bytes);
   if (!rc) {
@@ -198,19 +248,19 @@ VXB_API int vxb_decoder_create(vxb_ctx *ctx, const vxb_decoder_config *cfg, vxb_
     const int bs = d->cfg.kv_block_size;
     const int mbps = (c.max_seq + bs - 1) / bs;
     const int max_blocks = L * B * mbps;
-    rc = vxb_kv_create(ctx, L, c.n_kv_heads, hd, bs, max_blocks, B, mbps, c.kv_dtype ? c.kv_dtype : VXB_BF16, &d->kv);
+    rc = vxb_kv_create(ctx, L, d->hkv, hd, bs, max_blocks, B, mbps, c.kv_dtype ? c.kv_dtype : VXB_BF16, &d->kv);
   }
   if (!rc) {
     // attention scratch for the largest batch with the split plan used in graphs
-    const DecodePlan p = decode_plan(ctx, 1, c.n_kv_heads, c.max_seq);
-    d->attn_ws_bytes = decode_ws_bytes(B, c.n_kv_heads, c.n_heads / c.n_kv_heads, hd, p.splits);
+    const DecodePlan p = decode_plan(ctx, 1, d->hkv, c.max_seq);
+    d->attn_ws_bytes = decode_ws_bytes(B, d->hkv, c.n_heads / c.n_kv_heads, hd, p.splits);
     rc = dalloc(d, (void **)&d->attn_ws, d->attn_ws_bytes);
   }
   if (!rc) {
     // GEMV split-K partials for the widest projection (at most 16 splits), so
     // that recording a step into a graph never allocates
-    size_t widest = (size_t)std::max(std::max(2 * c.ffn_dim, c.vocab_size), d->qkv_n) + 16;
-    rc = ws_reserve(ctx, (size_t)16 * B * widest * 4, (size_t)B * c.n_kv_heads + 65536);
+    size_t widest = (size_t)std::max(std::max(std::max(2 * d->ffn, d->vocab), d->qkv_n), c.dim) + 16;
+    rc = ws_reserve(ctx, (size_t)32 * B * widest * 4, (size_t)B * c.n_kv_heads + 65536);
   }
   d->layers.resize(L);
   if (rc) {
@@ -219,6 +269,18 @@ VXB_API int vxb_decoder_create(vxb_ctx *ctx, const vxb_decoder_config *cfg, vxb_
   }
   *out = d;
   return VXB_OK;
+}
+
+}  // namespace
+
+VXB_API int vxb_decoder_create(vxb_ctx *ctx, const vxb_decoder_config *cfg, vxb_decoder **out) {
+  return decoder_create(ctx, cfg, nullptr, out);
+}
+
+VXB_API int vxb_decoder_create_tp(vxb_ctx *ctx, const vxb_decoder_config *cfg, vxb_comm *comm, vxb_decoder **out) {
+  if (!comm) return set_error(ctx, VXB_EINVAL, "vxb_decoder_create_tp: null communicator");
+  if (comm->ctx != ctx) return set_error(ctx, VXB_EINVAL, "vxb_decoder_create_tp: communicator of another context");
+  return decoder_create(ctx, cfg, comm, out);
 }
 
 VXB_API int vxb_decoder_destroy(vxb_decoder *d) {
@@ -246,12 +308,24 @@ VXB_API int vxb_decoder_init_random(vxb_decoder *d, uint64_t seed, float sigma) 
   if (int rc = use_device(d->ctx)) return rc;
   const vxb_decoder_config &c = d->cfg;
   uint64_t s = seed;
+  const int r = d->rank, kvfull = c.n_kv_heads * (c.dim / c.n_heads);
+  const size_t D = c.dim, F = c.ffn_dim;
   for (int l = 0; l < c.n_layers; l++) {
     auto &L = d->layers[l];
-    int rc = random_tiled(d, d->qkv_n, c.dim, ++s, sigma, &L.wqkv);
-    if (!rc) rc = random_tiled(d, c.dim, c.dim, ++s, sigma, &L.wo);
-    if (!rc) rc = random_tiled(d, 2 * c.ffn_dim, c.dim, ++s, sigma, &L.wgu);
-    if (!rc) rc = random_tiled(d, c.dim, c.ffn_dim, ++s, sigma, &L.wdown);
+    // full fused QKV [dim + 2 kvdim, dim]: this rank's q, k and v rows
+    int rc = random_tiled(d, d->qkv_n, c.dim,
+                          {{0, d->qdim, (size_t)r * d->qdim, 0, D},
+                           {d->qdim, d->kvdim, D + (size_t)r * d->kvdim, 0, D},
+                           {d->qdim + d->kvdim, d->kvdim, D + kvfull + (size_t)r * d->kvdim, 0, D}},
+                          ++s, sigma, &L.wqkv);
+    // full Wo [dim, dim]: this rank's input columns
+    if (!rc) rc = random_tiled(d, c.dim, d->qdim, {{0, c.dim, 0, (size_t)r * d->qdim, D}}, ++s, sigma, &L.wo);
+    // full [W1; W3] [2 ffn, dim]: this rank's gate and up rows
+    if (!rc)
+      rc = random_tiled(d, 2 * d->ffn, c.dim, {{0, d->ffn, (size_t)r * d->ffn, 0, D}, {d->ffn, d->ffn, F + (size_t)r * d->ffn, 0, D}},
+                        ++s, sigma, &L.wgu);
+    // full W2 [dim, ffn]: this rank's input columns
+    if (!rc) rc = random_tiled(d, c.dim, d->ffn, {{0, c.dim, 0, (size_t)r * d->ffn, F}}, ++s, sigma, &L.wdown);
     for (float **p : {&L.ln1_w, &L.ln1_b, &L.ln2_w, &L.ln2_b})
       if (!rc) rc = dalloc_t(d, p, (size_t)c.dim);
     if (!rc) rc = fill(d, L.ln1_w, c.dim, 1.f);
@@ -277,7 +351,7 @@ VXB_API int vxb_decoder_init_random(vxb_decoder *d, uint64_t seed, float sigma) 
   if (!rc) rc = dalloc_t(d, &d->lnf_b, (size_t)c.dim);
   if (!rc) rc = fill(d, d->lnf_w, c.dim, 1.f);
   if (!rc) rc = fill(d, d->lnf_b, c.dim, 0.f);
-  if (!rc) rc = random_tiled(d, c.vocab_size, c.dim, ++s, sigma, &d->wlm);
+  if (!rc) rc = random_tiled(d, d->vocab, c.dim, {{0, d->vocab, (size_t)r * d->vocab, 0, D}}, ++s, sigma, &d->wlm);
   if (!rc) VXB_CUDA_TRY(d->ctx, cudaStreamSynchronize(d->stream));
   return rc;
 }
@@ -292,24 +366,39 @@ VXB_API int vxb_decoder_set_weight(vxb_decoder *d, int layer, int which, const v
   if (int rc = use_device(d->ctx)) return rc;
   const vxb_decoder_config &c = d->cfg;
   const int fmt = c.weight_fmt;
-  auto upload_tiled_part = [&](void **tiled, int N_total, int K, int row0, int nrows) -> int {
-    const size_t bpr = vxb_block_bytes(fmt, (size_t)K);  // bytes per row
-    if (bytes != bpr * nrows)
-      return set_error(d->ctx, VXB_EINVAL, "vxb_decoder_set_weight: expected %zu bytes, got %zu", bpr * nrows, bytes);
+  // Upload rows [row0, row0 + nrows) of a local [N_total, K] matrix from
+  // GGUF blocks; `src` holds those rows, `src_bytes` their size.
+  auto upload_blocks = [&](void **tiled, int N_total, int K, int row0, int nrows, const void *src,
+                           size_t src_bytes) -> int {
     if (!*tiled) {
       if (int rc = dalloc(d, tiled, vxb_tiled_bytes(fmt, N_total, K))) return rc;
       if (int rc = tile_header(d->ctx, fmt, N_total, K, *tiled, d->stream)) return rc;
     }
     uint8_t *blocks = nullptr;
-    if (cudaMalloc(&blocks, bytes) != cudaSuccess) {
+    if (cudaMalloc(&blocks, src_bytes) != cudaSuccess) {
       cudaGetLastError();
       return set_error(d->ctx, VXB_ENOMEM, "vxb_decoder_set_weight: staging");
     }
-    VXB_CUDA_TRY(d->ctx, cudaMemcpyAsync(blocks, h_data, bytes, cudaMemcpyHostToDevice, d->stream));
+    VXB_CUDA_TRY(d->ctx, cudaMemcpyAsync(blocks, src, src_bytes, cudaMemcpyHostToDevice, d->stream));
     int rc = tile_part(d->ctx, fmt, blocks, nrows, K, row0, N_total, *tiled, d->stream);
     cudaStreamSynchronize(d->stream);
     cudaFree(blocks);
     return rc;
+  };
+  // A full [rows_full, K_full] host matrix (GGUF blocks) of which this rank
+  // keeps rows [r0, r0 + nr) and columns [k0, k0 + nk) (multiples of 32).
+  std::vector<uint8_t> slice;
+  auto upload_tiled_part = [&](void **tiled, int N_total, int row0, int rows_full, int K_full, int r0, int nr, int k0,
+                               int nk) -> int {
+    const size_t bpr = vxb_block_bytes(fmt, (size_t)K_full);  // bytes per full row
+    if (bytes != bpr * rows_full)
+      return set_error(d->ctx, VXB_EINVAL, "vxb_decoder_set_weight: expected %zu bytes, got %zu", bpr * rows_full, bytes);
+    const uint8_t *src = (const uint8_t *)h_data + (size_t)r0 * bpr;
+    if (nk == K_full) return upload_blocks(tiled, N_total, nk, row0, nr, src, bpr * nr);
+    const size_t bb = vxb_block_bytes(fmt, 32), off = (size_t)(k0 / 32) * bb, len = (size_t)(nk / 32) * bb;
+    slice.resize(len * nr);
+    for (int i = 0; i < nr; i++) std::memcpy(slice.data() + (size_t)i * len, src + (size_t)i * bpr + off, len);
+    return upload_blocks(tiled, N_total, nk, row0, nr, slice.data(), slice.size());
   };
   auto upload_f32 = [&](float **p, size_t n) -> int {
     if (bytes != n * 4) return set_error(d->ctx, VXB_EINVAL, "vxb_decoder_set_weight: expected %zu bytes", n * 4);
@@ -330,20 +419,25 @@ VXB_API int vxb_decoder_set_weight(vxb_decoder *d, int layer, int which, const v
       }
       case 1: return upload_f32(&d->lnf_w, c.dim);
       case 2: return upload_f32(&d->lnf_b, c.dim);
-      case 3: return upload_tiled_part(&d->wlm, c.vocab_size, c.dim, 0, c.vocab_size);
+      case 3:
+        return upload_tiled_part(&d->wlm, d->vocab, 0, c.vocab_size, c.dim, d->rank * d->vocab, d->vocab, 0, c.dim);
       default: return set_error(d->ctx, VXB_EINVAL, "vxb_decoder_set_weight: which %d", which);
     }
   }
   if (layer < 0 || layer >= c.n_layers) return set_error(d->ctx, VXB_EINVAL, "vxb_decoder_set_weight: layer %d", layer);
   auto &L = d->layers[layer];
+  const int r = d->rank, kvfull = c.n_kv_heads * (c.dim / c.n_heads);
   switch (which) {
-    case 0: return upload_tiled_part(&L.wqkv, d->qkv_n, c.dim, 0, c.dim);
-    case 1: return upload_tiled_part(&L.wqkv, d->qkv_n, c.dim, c.dim, d->kvdim);
-    case 2: return upload_tiled_part(&L.wqkv, d->qkv_n, c.dim, c.dim + d->kvdim, d->kvdim);
-    case 3: return upload_tiled_part(&L.wo, c.dim, c.dim, 0, c.dim);
-    case 4: return upload_tiled_part(&L.wgu, 2 * c.ffn_dim, c.dim, 0, c.ffn_dim);
-    case 5: return upload_tiled_part(&L.wdown, c.dim, c.ffn_dim, 0, c.dim);
-    case 6: return upload_tiled_part(&L.wgu, 2 * c.ffn_dim, c.dim, c.ffn_dim, c.ffn_dim);
+    // column-parallel (this rank's output rows) and row-parallel (this rank's
+    // input columns) slices of the full matrices
+    case 0: return upload_tiled_part(&L.wqkv, d->qkv_n, 0, c.dim, c.dim, r * d->qdim, d->qdim, 0, c.dim);
+    case 1: return upload_tiled_part(&L.wqkv, d->qkv_n, d->qdim, kvfull, c.dim, r * d->kvdim, d->kvdim, 0, c.dim);
+    case 2:
+      return upload_tiled_part(&L.wqkv, d->qkv_n, d->qdim + d->kvdim, kvfull, c.dim, r * d->kvdim, d->kvdim, 0, c.dim);
+    case 3: return upload_tiled_part(&L.wo, c.dim, 0, c.dim, c.dim, 0, c.dim, r * d->qdim, d->qdim);
+    case 4: return upload_tiled_part(&L.wgu, 2 * d->ffn, 0, c.ffn_dim, c.dim, r * d->ffn, d->ffn, 0, c.dim);
+    case 5: return upload_tiled_part(&L.wdown, c.dim, 0, c.dim, c.ffn_dim, 0, c.dim, r * d->ffn, d->ffn);
+    case 6: return upload_tiled_part(&L.wgu, 2 * d->ffn, d->ffn, c.ffn_dim, c.dim, r * d->ffn, d->ffn, 0, c.dim);
     case 7: return upload_f32(&L.ln1_w, c.dim);
     case 8: return upload_f32(&L.ln1_b, c.dim);
     case 9: return upload_f32(&L.ln2_w, c.dim);
@@ -363,30 +457,41 @@ int record_step(vxb_decoder *d, int B) {
   const float eps = d->cfg.norm_eps;
   const float scale = 1.0f / sqrtf((float)hd);
   const int fmt = c.weight_fmt;
-  const DecodePlan ap = decode_plan(ctx, B, c.n_kv_heads, c.max_seq);
-  if (decode_ws_bytes(B, c.n_kv_heads, c.n_heads / c.n_kv_heads, hd, ap.splits) > d->attn_ws_bytes)
+  const DecodePlan ap = decode_plan(ctx, B, d->hkv, c.max_seq);
+  if (decode_ws_bytes(B, d->hkv, c.n_heads / c.n_kv_heads, hd, ap.splits) > d->attn_ws_bytes)
     return set_error(ctx, VXB_EINVAL, "decoder: attention scratch too small");
   int rc = embed_launch(ctx, d->emb, d->d_tokens, B, c.dim, c.vocab_size, d->x, st);
   for (int l = 0; l < c.n_layers && !rc; l++) {
     auto &L = d->layers[l];
     rc = rmsnorm_launch(ctx, d->x, L.ln1_w, L.ln1_b, B, c.dim, eps, d->h, st);
     if (!rc) rc = gemv_launch(ctx, fmt, L.wqkv, d->qkv_n, c.dim, d->h, B, VXB_F32, d->qkv, nullptr, st, nullptr);
-    if (!rc) rc = rope_launch(ctx, d->qkv, B, c.dim, d->kvdim, d->d_places, d->rope_div, d->q, d->kvnew,
-                              d->kvnew + (size_t)c.max_batch * d->kvdim, st);
+    if (!rc) rc = rope_launch(ctx, d->qkv, B, d->qdim, d->kvdim, d->d_places, d->rope_div, d->q, d->kvnew,
+                              d->kvnew + (size_t)c.max_batch * d->kvdim, st, d->rank * d->qdim / 2,
+                              d->rank * d->kvdim / 2);
     if (!rc)
       rc = kv_append_launch(d->kv, l, B, d->d_places + (size_t)l * c.max_batch, d->kvnew,
                             d->kvnew + (size_t)c.max_batch * d->kvdim, st);
     if (!rc)
-      rc = decode_attn_launch(d->kv, l, B, d->d_slots, nullptr, d->q, c.n_heads, scale, d->attn, nullptr, ap, d->attn_ws, st);
-    if (!rc) rc = gemv_launch(ctx, fmt, L.wo, c.dim, c.dim, d->attn, B, VXB_F32, d->x, d->x, st, nullptr);
+      rc = decode_attn_launch(d->kv, l, B, d->d_slots, nullptr, d->q, d->hq, scale, d->attn, nullptr, ap, d->attn_ws, st);
+    // row-parallel Wo: rank 0 adds the residual, the partials are summed over ranks
+    if (!rc) rc = gemv_launch(ctx, fmt, L.wo, c.dim, d->qdim, d->attn, B, VXB_F32, d->x, d->rank == 0 ? d->x : nullptr, st, nullptr);
+    if (!rc && d->tp > 1) rc = comm_allreduce(d->comm, d->x, (size_t)B * c.dim, VXB_F32, 0, st);
     if (!rc) rc = rmsnorm_launch(ctx, d->x, L.ln2_w, L.ln2_b, B, c.dim, eps, d->h, st);
-    if (!rc) rc = gemv_launch(ctx, fmt, L.wgu, 2 * c.ffn_dim, c.dim, d->h, B, VXB_F32, d->gu, nullptr, st, nullptr);
-    if (!rc) rc = swiglu_launch(ctx, d->gu, B, c.ffn_dim, d->act, st);
-    if (!rc) rc = gemv_launch(ctx, fmt, L.wdown, c.dim, c.ffn_dim, d->act, B, VXB_F32, d->x, d->x, st, nullptr);
+    if (!rc) rc = gemv_launch(ctx, fmt, L.wgu, 2 * d->ffn, c.dim, d->h, B, VXB_F32, d->gu, nullptr, st, nullptr);
+    if (!rc) rc = swiglu_launch(ctx, d->gu, B, d->ffn, d->act, st);
+    if (!rc) rc = gemv_launch(ctx, fmt, L.wdown, c.dim, d->ffn, d->act, B, VXB_F32, d->x, d->rank == 0 ? d->x : nullptr, st, nullptr);
+    if (!rc && d->tp > 1) rc = comm_allreduce(d->comm, d->x, (size_t)B * c.dim, VXB_F32, 0, st);
   }
   if (!rc) rc = rmsnorm_launch(ctx, d->x, d->lnf_w, d->lnf_b, B, c.dim, eps, d->h, st);
-  if (!rc) rc = gemv_launch(ctx, fmt, d->wlm, c.vocab_size, c.dim, d->h, B, VXB_F32, d->logits, nullptr, st, nullptr);
-  if (!rc) rc = argmax_launch(ctx, d->logits, B, c.vocab_size, d->d_next, st);
+  if (!rc) rc = gemv_launch(ctx, fmt, d->wlm, d->vocab, c.dim, d->h, B, VXB_F32, d->logits, nullptr, st, nullptr);
+  if (d->tp == 1) {
+    if (!rc) rc = argmax_launch(ctx, d->logits, B, c.vocab_size, d->d_next, st);
+  } else {
+    // first maximum over the vocabulary shards: max-reduce (logit, index) keys
+    if (!rc) rc = argmax_key_launch(ctx, d->logits, B, d->vocab, d->rank * d->vocab, d->d_keys, st);
+    if (!rc) rc = comm_allreduce(d->comm, d->d_keys, (size_t)B, -1, 1, st);
+    if (!rc) rc = key_to_token_launch(ctx, d->d_keys, B, d->d_next, st);
+  }
   return rc;
 }
 
@@ -481,9 +586,16 @@ VXB_API int vxb_decoder_step(vxb_decoder *d, int batch, const int64_t *h_seq_ids
   if (int rc = launch_step(d, batch, h_seq_ids, nullptr, true, h_tokens)) return rc;
   cudaStream_t st = d->stream;
   VXB_CUDA_TRY(d->ctx, cudaMemcpyAsync(d->h_next, d->d_next, batch * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
-  if (h_logits)
-    VXB_CUDA_TRY(d->ctx, cudaMemcpyAsync(h_logits, d->logits, (size_t)batch * d->cfg.vocab_size * sizeof(float),
+  if (h_logits) {
+    const float *src = d->logits;
+    if (d->tp > 1) {
+      if (int rc = comm_allgather_f32(d->comm, d->logits, d->logits_all, (size_t)batch * d->vocab, st)) return rc;
+      if (int rc = unshard_launch(d->ctx, d->logits_all, d->tp, batch, d->vocab, d->logits_full, st)) return rc;
+      src = d->logits_full;
+    }
+    VXB_CUDA_TRY(d->ctx, cudaMemcpyAsync(h_logits, src, (size_t)batch * d->cfg.vocab_size * sizeof(float),
                                          cudaMemcpyDeviceToHost, st));
+  }
   VXB_CUDA_TRY(d->ctx, cudaStreamSynchronize(st));
   std::memcpy(h_next, d->h_next, batch * sizeof(int32_t));
   return VXB_OK;
@@ -509,10 +621,20 @@ VXB_API int vxb_decoder_step_device(vxb_decoder *d, int batch, const int64_t *h_
   return rc;
 }
 
+// Logits [batch, vocab] of the last step. With tensor parallelism this is a
+// collective: every rank calls it, the vocabulary shards are all-gathered.
 VXB_API int vxb_decoder_logits(vxb_decoder *d, int batch, float *d_out, void *stream) {
   if (!d || !d_out) return set_error(d ? d->ctx : nullptr, VXB_EINVAL, "vxb_decoder_logits: null argument");
+  if (batch < 1 || batch > d->cfg.max_batch) return set_error(d->ctx, VXB_EINVAL, "vxb_decoder_logits: batch %d", batch);
+  if (int rc = use_device(d->ctx)) return rc;
+  const float *src = d->logits;
+  if (d->tp > 1) {
+    if (int rc = comm_allgather_f32(d->comm, d->logits, d->logits_all, (size_t)batch * d->vocab, d->stream)) return rc;
+    if (int rc = unshard_launch(d->ctx, d->logits_all, d->tp, batch, d->vocab, d->logits_full, d->stream)) return rc;
+    src = d->logits_full;
+  }
   VXB_CUDA_TRY(d->ctx, cudaStreamSynchronize(d->stream));
-  VXB_CUDA_TRY(d->ctx, cudaMemcpyAsync(d_out, d->logits, (size_t)batch * d->cfg.vocab_size * 4, cudaMemcpyDeviceToDevice,
+  VXB_CUDA_TRY(d->ctx, cudaMemcpyAsync(d_out, src, (size_t)batch * d->cfg.vocab_size * 4, cudaMemcpyDeviceToDevice,
                                        (cudaStream_t)stream));
   return VXB_OK;
 }

@@ -42,9 +42,11 @@ __global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restr
 // qkv: f32 [B, dim + 2*kvdim] (q | k | v); positions from the KV placements
 // of layer 0 of this step. Writes q (bf16 [B, dim]), the new keys at
 // k_out [B, kvdim] and the new values at v_out [B, kvdim] (bf16).
+// q_pair0 / k_pair0: index of the first rotation pair of this q / k slice in
+// the full vectors (tensor-parallel shards hold a slice of the heads)
 __global__ void rope_kernel(const float *__restrict__ qkv, int dim, int kvdim, const KVPlace *__restrict__ places,
                             const double *__restrict__ rope_div, uint16_t *__restrict__ q_out,
-                            uint16_t *__restrict__ k_out, uint16_t *__restrict__ v_out) {
+                            uint16_t *__restrict__ k_out, uint16_t *__restrict__ v_out, int q_pair0, int k_pair0) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
   const int b = blockIdx.x;
@@ -59,7 +61,7 @@ __global__ void rope_kernel(const float *__restrict__ qkv, int dim, int kvdim, c
     const int pi = isk ? p - npq : p;
     // theta in f64 (pos / divisor), then sin/cos
     double s, c;
-    sincos(pos / rope_div[pi], &s, &c);
+    sincos(pos / rope_div[pi + (isk ? k_pair0 : q_pair0)], &s, &c);
     const float cf = (float)c, sf = (float)s;
     const float *src = row + (isk ? dim : 0) + 2 * pi;
     const float x0 = src[0], x1 = src[1];
@@ -156,6 +158,67 @@ __global__ void normal_kernel(float *__restrict__ out, size_t n, uint64_t seed, 
   out[i] = sigma * sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
 }
 
+// The [rows, cols] block at (row0, col0) of the [*, ld] matrix that
+// normal_kernel generates with the same seed (element index row * ld + col).
+__global__ void normal_block_kernel(float *__restrict__ out, int rows, int cols, size_t row0, size_t col0, size_t ld,
+                                    uint64_t seed, float sigma) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)rows * cols) return;
+  const size_t r = i / cols, c = i % cols;
+  const uint64_t z = splitmix64(seed * 0x100000001B3ull + ((row0 + r) * ld + col0 + c));
+  const float u1 = ((float)(z >> 40) + 0.5f) * (1.0f / 16777216.0f);
+  const float u2 = (float)((z >> 16) & 0xFFFFFFu) * (1.0f / 16777216.0f);
+  out[i] = sigma * sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+}
+
+// Order-preserving key of (value, index) for a distributed first-max argmax:
+// larger value wins, then the smaller index; 0 for NaN.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+  if (v != v) return 0ull;
+  uint32_t b = __float_as_uint(v);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)b << 32) | (0xFFFFFFFFu - (uint32_t)idx);
+}
+
+// Key of the first maximum of each row of a vocab shard starting at `offset`.
+__global__ void argmax_key_kernel(const float *__restrict__ logits, int vocab, int offset,
+                                  unsigned long long *__restrict__ keys) {
+  __shared__ unsigned long long sk[32];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
+  const float *l = logits + (size_t)blockIdx.x * vocab;
+  unsigned long long best = 0ull;
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) best = max(best, argmax_key(l[i], offset + i));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) sk[warp] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long b = sk[0];
+    for (int w = 1; w < nw; w++) b = max(b, sk[w]);
+    keys[blockIdx.x] = b;
+  }
+}
+
+__global__ void key_to_token_kernel(const unsigned long long *__restrict__ keys, int rows, int32_t *__restrict__ out) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < rows) out[i] = keys[i] == 0ull ? 0 : (int32_t)(0xFFFFFFFFu - (uint32_t)(keys[i] & 0xFFFFFFFFull));
+}
+
+// [tp][rows][shard] (all-gathered vocab shards) -> [rows][tp * shard]
+__global__ void unshard_kernel(const float *__restrict__ in, int tp, int rows, int shard, float *__restrict__ out) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t n = (size_t)tp * rows * shard;
+  if (i >= n) return;
+  const int r = (int)(i / ((size_t)tp * shard));
+  const size_t col = i % ((size_t)tp * shard);
+  const int t = (int)(col / shard), c = (int)(col % shard);
+  out[i] = in[((size_t)t * rows + r) * shard + c];
+}
+
 template <typename... Args>
 int launch_pdl(vxb_ctx *ctx, void (*kfn)(Args...), dim3 grid, dim3 block, cudaStream_t st, const char *what,
                Args... args) {
@@ -184,9 +247,10 @@ int rmsnorm_launch(vxb_ctx *ctx, const float *x, const float *w, const float *b,
 }
 
 int rope_launch(vxb_ctx *ctx, const float *qkv, int rows, int dim, int kvdim, const KVPlace *places,
-                const double *rope_div, uint16_t *q_out, uint16_t *k_out, uint16_t *v_out, cudaStream_t st) {
+                const double *rope_div, uint16_t *q_out, uint16_t *k_out, uint16_t *v_out, cudaStream_t st,
+                int q_pair0, int k_pair0) {
   return launch_pdl(ctx, rope_kernel, dim3(rows), dim3(512), st, "rope_kernel", qkv, dim, kvdim, places, rope_div,
-                    q_out, k_out, v_out);
+                    q_out, k_out, v_out, q_pair0, k_pair0);
 }
 
 int swiglu_launch(vxb_ctx *ctx, const float *gu, int rows, int ffn, uint16_t *act, cudaStream_t st) {
@@ -208,6 +272,31 @@ int normal_fill(vxb_ctx *ctx, float *out, size_t n, uint64_t seed, size_t offset
   if (n == 0) return VXB_OK;
   normal_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(out, n, seed, offset, sigma);
   return launch_check(ctx, "normal_kernel");
+}
+
+int normal_fill_block(vxb_ctx *ctx, float *out, int rows, int cols, size_t row0, size_t col0, size_t ld, uint64_t seed,
+                      float sigma, cudaStream_t st) {
+  const size_t n = (size_t)rows * cols;
+  if (n == 0) return VXB_OK;
+  normal_block_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(out, rows, cols, row0, col0, ld, seed, sigma);
+  return launch_check(ctx, "normal_block_kernel");
+}
+
+int argmax_key_launch(vxb_ctx *ctx, const float *logits, int rows, int vocab, int offset, unsigned long long *keys,
+                      cudaStream_t st) {
+  return launch_pdl(ctx, argmax_key_kernel, dim3(rows), dim3(1024), st, "argmax_key_kernel", logits, vocab, offset,
+                    keys);
+}
+
+int key_to_token_launch(vxb_ctx *ctx, const unsigned long long *keys, int rows, int32_t *out, cudaStream_t st) {
+  return launch_pdl(ctx, key_to_token_kernel, dim3((rows + 127) / 128), dim3(128), st, "key_to_token_kernel", keys,
+                    rows, out);
+}
+
+int unshard_launch(vxb_ctx *ctx, const float *in, int tp, int rows, int shard, float *out, cudaStream_t st) {
+  const size_t n = (size_t)tp * rows * shard;
+  unshard_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(in, tp, rows, shard, out);
+  return launch_check(ctx, "unshard_kernel");
 }
 
 }  // namespace vxb

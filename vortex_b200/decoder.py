@@ -28,15 +28,23 @@ EMBED, FINAL_W, FINAL_B, OUTPUT = range(4)
 
 
 class Decoder:
-    def __init__(self, max_batch: int, max_seq: int, device=None, **cfg):
-        self.ctx = context(device)
+    """comm (optional): a vortex_b200.comm.Comm; the decoder is then this
+    rank's tensor-parallel part, and every rank makes the same calls."""
+
+    def __init__(self, max_batch: int, max_seq: int, device=None, comm=None, **cfg):
+        self.ctx = comm.ctx if comm is not None else context(device)
         L = N.lib()
         c = dict(LLAMA_7B)
         c.update(cfg)
         self.cfg = DecoderConfig(**{k: c[k] for k, _ in DecoderConfig._fields_ if k in c},
                                  max_batch=max_batch, max_seq=max_seq)
         p = ctypes.c_void_p()
-        N.check(L.vxb_decoder_create(self.ctx.ptr, ctypes.addressof(self.cfg), ctypes.byref(p)), self.ctx.ptr)
+        if comm is None:
+            N.check(L.vxb_decoder_create(self.ctx.ptr, ctypes.addressof(self.cfg), ctypes.byref(p)), self.ctx.ptr)
+        else:
+            N.check(L.vxb_decoder_create_tp(self.ctx.ptr, ctypes.addressof(self.cfg), comm.ptr, ctypes.byref(p)),
+                    self.ctx.ptr)
+        self.comm = comm
         self.ptr = p
         self.vocab = self.cfg.vocab_size
 
