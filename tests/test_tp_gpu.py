@@ -118,3 +118,62 @@ def test_tp2_decoder_matches_single_gpu(cuda_ok, mode):
             top2 = np.sort(lr[b])[-2:]
             if top2[1] - top2[0] > 1e-3 * np.max(np.abs(lr[b])):  # no near tie
                 assert n0[b] == nr[b]
+
+
+def _ar_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    from vortex_b200 import comm as C
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        comm = C.Comm(world, rank, C.share_unique_id(rank), device=rank)
+        res = []
+        for n in (1, 4097, 131072, 400000):  # the last one (1.6 MB) goes through NCCL
+            for it in range(3):  # reuse of both peer-buffer slots
+                g = torch.Generator(device="cuda").manual_seed(1000 * n + 10 * it + rank)
+                t = torch.randn(n, device="cuda", generator=g)
+                comm.allreduce_sum(t)
+                torch.cuda.synchronize()
+                res.append(t.cpu().numpy())
+        comm.close()
+        q.put((rank, res))
+    except Exception as e:
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_allreduce_sum_peer_memory_and_nccl_paths(cuda_ok):
+    """vxb_allreduce_sum on 2 GPUs: both ranks hold the elementwise f32 sum of
+    the two inputs (rank order), for one-shot (<= 1 MiB) and NCCL sizes."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ar_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=600) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(2):
+        assert not isinstance(got[r], str), got[r]
+    k = 0
+    for n in (1, 4097, 131072, 400000):
+        for it in range(3):
+            ins = []
+            for r in range(2):
+                g = torch.Generator(device="cuda").manual_seed(1000 * n + 10 * it + r)
+                ins.append(torch.randn(n, device="cuda", generator=g).cpu().numpy())
+            want = ins[0] + ins[1]
+            np.testing.assert_array_equal(got[0][k], got[1][k])
+            if n <= 262144:
+                np.testing.assert_array_equal(got[0][k], want)
+            else:
+                np.testing.assert_allclose(got[0][k], want, rtol=1e-6, atol=1e-6)
+            k += 1

@@ -10,6 +10,7 @@
 #include <nccl.h>
 
 #include <mutex>
+#include <vector>
 
 #include "comm.h"
 
@@ -56,11 +57,158 @@ int nccl_fail(vxb_ctx *ctx, ncclResult_t r, const char *what) {
   return set_error(ctx, VXB_ENCCL, "%s: %s", what, nccl().error_string ? nccl().error_string(r) : "NCCL error");
 }
 
+// ---------------------------------------------------------------------------
+// One-shot all-reduce (sum, f32) over peer memory. CTA b owns slice b of the
+// message: it copies its slice of the input into this rank's data slot
+// (generation parity), raises flag [b][rank] to the generation in every
+// rank's buffer (system-scope release), waits (bounded) until every rank's
+// flag [b][*] in its own buffer reached the generation, then sums slice b
+// over the ranks' slots in rank order - the same order on every rank, so all
+// ranks hold identical bits. Two slots alternate: a rank can only reuse a
+// slot two calls later, after every rank has started the call in between and
+// so has finished reading it. The generation of block b is a per-block device
+// counter (the same sequence of calls on every rank, CUDA graphs included).
+struct ArArgs {
+  uint8_t *peer[kArMaxRanks];
+  float *data;  // in / out (in place)
+  int *err;
+  size_t n;
+  int rank, nranks;
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(512) oneshot_allreduce_kernel(const ArArgs a) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int b = blockIdx.x;
+  uint8_t *mine = a.peer[a.rank];
+  uint32_t *counter = reinterpret_cast<uint32_t *>(mine + kArFlagsOff + (size_t)kArBlocks * kArMaxRanks * 4) + b;
+  __shared__ uint32_t s_gen;
+  if (threadIdx.x == 0) s_gen = *counter + 1;
+  __syncthreads();
+  const uint32_t gen = s_gen;
+  const size_t slot = (size_t)(gen & 1) * kArMaxBytes;
+  // slice of this block, in float4 units (the message is padded to them)
+  const size_t n4 = (a.n + 3) / 4;
+  const size_t per = (n4 + kArBlocks - 1) / kArBlocks;
+  const size_t i0 = (size_t)b * per, i1 = min(n4, i0 + per);
+  float4 *dst = reinterpret_cast<float4 *>(mine + slot);
+  for (size_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    float4 v;
+    const size_t e = i * 4;
+    v.x = e < a.n ? a.data[e] : 0.f;
+    v.y = e + 1 < a.n ? a.data[e + 1] : 0.f;
+    v.z = e + 2 < a.n ? a.data[e + 2] : 0.f;
+    v.w = e + 3 < a.n ? a.data[e + 3] : 0.f;
+    dst[i] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < a.nranks) {
+    __threadfence_system();
+    uint32_t *flag = reinterpret_cast<uint32_t *>(a.peer[threadIdx.x] + kArFlagsOff) + b * kArMaxRanks + a.rank;
+    st_release_sys(flag, gen);
+    // wait for rank threadIdx.x's flag in this rank's buffer
+    const uint32_t *mf = reinterpret_cast<const uint32_t *>(mine + kArFlagsOff) + b * kArMaxRanks + threadIdx.x;
+    const long long t0 = clock64();
+    while ((int)(ld_acquire_sys(mf) - gen) < 0) {
+      if (clock64() - t0 > (1ll << 31)) {
+        atomicExch(a.err, 1);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  for (size_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < a.nranks; q++) {
+      const float4 v = __ldcv(reinterpret_cast<const float4 *>(a.peer[q] + slot) + i);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    const size_t e = i * 4;
+    if (e < a.n) a.data[e] = acc.x;
+    if (e + 1 < a.n) a.data[e + 1] = acc.y;
+    if (e + 2 < a.n) a.data[e + 2] = acc.z;
+    if (e + 3 < a.n) a.data[e + 3] = acc.w;
+  }
+  if (threadIdx.x == 0) *counter = gen;
+  asm volatile("griddepcontrol.launch_dependents;");
+}
+
+// Collective set-up of the peer buffers: allocate, zero, exchange IPC handles
+// through NCCL, open every peer's buffer.
+int ar_setup(vxb_comm *c) {
+  if (c->nranks < 2 || c->nranks > kArMaxRanks) return VXB_OK;  // NCCL only
+  vxb_ctx *ctx = c->ctx;
+  if (cudaMalloc(&c->ar_local, kArBytes) != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(ctx, VXB_ENOMEM, "vxb_comm_init: peer buffer");
+  }
+  VXB_CUDA_TRY(ctx, cudaMemset(c->ar_local, 0, kArBytes));
+  cudaIpcMemHandle_t h;
+  VXB_CUDA_TRY(ctx, cudaIpcGetMemHandle(&h, c->ar_local));
+  uint8_t *d_handles = nullptr;
+  VXB_CUDA_TRY(ctx, cudaMalloc(&d_handles, sizeof(h) * (c->nranks + 1)));
+  VXB_CUDA_TRY(ctx, cudaMemcpy(d_handles + sizeof(h) * c->nranks, &h, sizeof(h), cudaMemcpyHostToDevice));
+  VXB_CUDA_TRY(ctx, cudaDeviceSynchronize());
+  const ncclResult_t r = nccl().all_gather(d_handles + sizeof(h) * c->nranks, d_handles, sizeof(h), ncclUint8,
+                                           (ncclComm_t)c->nccl, 0);
+  std::vector<cudaIpcMemHandle_t> all(c->nranks);
+  cudaError_t e = cudaStreamSynchronize(0);
+  if (e == cudaSuccess) e = cudaMemcpy(all.data(), d_handles, sizeof(h) * c->nranks, cudaMemcpyDeviceToHost);
+  cudaFree(d_handles);
+  if (r != ncclSuccess) return nccl_fail(ctx, r, "ncclAllGather of IPC handles");
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "IPC handle exchange");
+  for (int q = 0; q < c->nranks; q++) {
+    if (q == c->rank) {
+      c->ar_peer[q] = c->ar_local;
+      continue;
+    }
+    void *p = nullptr;
+    e = cudaIpcOpenMemHandle(&p, all[q], cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaIpcOpenMemHandle");
+    c->ar_peer[q] = (uint8_t *)p;
+  }
+  c->ar_ready = true;
+  return VXB_OK;
+}
+
 }  // namespace
 
 namespace vxb {
 
 int comm_allreduce(vxb_comm *c, void *buf, size_t count, int dtype, int op, cudaStream_t st) {
+  if (c->ar_ready && dtype == VXB_F32 && op == 0 && count > 0 && (count + 3) / 4 * 16 <= kArMaxBytes) {
+    if (int rc = ws_reserve(c->ctx, 0, 0)) return rc;  // device error word
+    ArArgs a;
+    for (int q = 0; q < kArMaxRanks; q++) a.peer[q] = c->ar_peer[q];
+    a.data = (float *)buf;
+    a.err = c->ctx->d_err;
+    a.n = count;
+    a.rank = c->rank;
+    a.nranks = c->nranks;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kArBlocks);
+    cfg.blockDim = dim3(512);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    VXB_CUDA_TRY(c->ctx, cudaLaunchKernelEx(&cfg, oneshot_allreduce_kernel, a));
+    return VXB_OK;
+  }
   NcclApi &n = nccl();
   const ncclDataType_t t = dtype == VXB_F32 ? ncclFloat32 : dtype == VXB_BF16 ? ncclBfloat16 : ncclUint64;
   const ncclRedOp_t o = op == 0 ? ncclSum : ncclMax;
@@ -106,12 +254,32 @@ VXB_API int vxb_comm_init(vxb_ctx *ctx, int nranks, int rank, const void *h_uniq
   c->nccl = comm;
   c->nranks = nranks;
   c->rank = rank;
+  if (int rc = ar_setup(c)) {
+    vxb_comm_destroy(c);
+    return rc;
+  }
   *out = c;
   return VXB_OK;
 }
 
+// Collective: every rank calls it. A barrier (NCCL all-reduce) first, so no
+// rank frees its peer buffer while another rank may still read it.
 VXB_API int vxb_comm_destroy(vxb_comm *c) {
   if (!c) return VXB_OK;
+  use_device(c->ctx);
+  cudaDeviceSynchronize();
+  if (c->nccl && c->ar_ready) {
+    float *one = nullptr;
+    if (cudaMalloc(&one, sizeof(float)) == cudaSuccess) {
+      nccl().all_reduce(one, one, 1, ncclFloat32, ncclSum, (ncclComm_t)c->nccl, 0);
+      cudaStreamSynchronize(0);
+      cudaFree(one);
+    }
+    cudaGetLastError();
+  }
+  for (int q = 0; q < kArMaxRanks; q++)
+    if (c->ar_peer[q] && q != c->rank) cudaIpcCloseMemHandle(c->ar_peer[q]);
+  if (c->ar_local) cudaFree(c->ar_local);
   if (c->nccl) nccl().comm_destroy((ncclComm_t)c->nccl);
   delete c;
   return VXB_OK;

@@ -3,10 +3,22 @@
 
 #include "vxb_internal.h"
 
+// One-shot all-reduce over NVLink peer memory for decode-sized messages
+// (up to kArMaxBytes of f32): every rank's buffer is mapped into every other
+// rank with CUDA IPC.
+constexpr int kArMaxRanks = 8;
+constexpr int kArBlocks = 32;                      // CTAs (message slices) per call
+constexpr size_t kArMaxBytes = (size_t)1 << 20;    // per slot
+constexpr size_t kArFlagsOff = 2 * kArMaxBytes;    // two data slots, then flags
+constexpr size_t kArBytes = kArFlagsOff + (size_t)kArBlocks * kArMaxRanks * 4 + (size_t)kArBlocks * 4;
+
 struct vxb_comm {
   vxb_ctx *ctx = nullptr;
   void *nccl = nullptr;  // ncclComm_t
   int nranks = 1, rank = 0;
+  uint8_t *ar_local = nullptr;                  // this rank's buffer (cudaMalloc)
+  uint8_t *ar_peer[kArMaxRanks] = {nullptr};    // every rank's buffer (own one included)
+  bool ar_ready = false;
 };
 
 namespace vxb {
