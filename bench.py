@@ -121,6 +121,8 @@ class ClockSampler:
 def dist_setup(gpus):
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     if ws > 1:
+        # NCCL's banner and warnings go to stderr: stdout carries the JSON line only
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         import datetime
 
         import torch

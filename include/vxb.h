@@ -215,7 +215,7 @@ int vxb_nccl_unique_id(void *h_out128);
 int vxb_comm_init(vxb_ctx *ctx, int nranks, int rank, const void *h_unique_id128, vxb_comm **out);
 int vxb_comm_destroy(vxb_comm *comm); /* collective: every rank calls it */
 /* In-place sum over ranks of count elements of dtype VXB_F32 or VXB_BF16.
- * f32 messages up to 1 MiB take a one-shot all-reduce over NVLink peer
+ * f32 messages up to 512 KiB take a one-shot all-reduce over NVLink peer
  * memory (CUDA IPC mappings made at init; sum in rank order, identical bits
  * on every rank); larger ones and bf16 go through NCCL. */
 int vxb_allreduce_sum(vxb_comm *comm, void *d_buf, size_t count, int dtype, void *stream);

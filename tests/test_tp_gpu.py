@@ -148,7 +148,7 @@ def _ar_worker(rank, world, port, q):
 
 def test_allreduce_sum_peer_memory_and_nccl_paths(cuda_ok):
     """vxb_allreduce_sum on 2 GPUs: both ranks hold the elementwise f32 sum of
-    the two inputs (rank order), for one-shot (<= 1 MiB) and NCCL sizes."""
+    the two inputs (rank order), for one-shot (<= 512 KiB) and NCCL sizes."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp

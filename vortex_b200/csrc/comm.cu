@@ -188,7 +188,7 @@ int ar_setup(vxb_comm *c) {
 namespace vxb {
 
 int comm_allreduce(vxb_comm *c, void *buf, size_t count, int dtype, int op, cudaStream_t st) {
-  if (c->ar_ready && dtype == VXB_F32 && op == 0 && count > 0 && (count + 3) / 4 * 16 <= kArMaxBytes) {
+  if (c->ar_ready && dtype == VXB_F32 && op == 0 && count > 0 && (count + 3) / 4 * 16 <= kArOneShotBytes) {
     if (int rc = ws_reserve(c->ctx, 0, 0)) return rc;  // device error word
     ArArgs a;
     for (int q = 0; q < kArMaxRanks; q++) a.peer[q] = c->ar_peer[q];

@@ -9,6 +9,9 @@
 constexpr int kArMaxRanks = 8;
 constexpr int kArBlocks = 32;                      // CTAs (message slices) per call
 constexpr size_t kArMaxBytes = (size_t)1 << 20;    // per slot
+// messages up to this size take the one-shot path (measured on 8 B200s: 18-36
+// us against NCCL's 36-40 us up to 512 KiB; NCCL wins from about 1 MiB)
+constexpr size_t kArOneShotBytes = (size_t)512 << 10;
 constexpr size_t kArFlagsOff = 2 * kArMaxBytes;    // two data slots, then flags
 constexpr size_t kArBytes = kArFlagsOff + (size_t)kArBlocks * kArMaxRanks * 4 + (size_t)kArBlocks * 4;
 
