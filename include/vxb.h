@@ -179,6 +179,18 @@ int vxb_decode_attention(vxb_kv *kv, int layer, int n, const int64_t *h_seq_ids,
                          void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* K2: prefill GEMM. Replaces weight_only_matmul (src/quantize.rs:845-852)  */
+/* and Linear::forward (src/transformer.rs:332-352) for many rows:           */
+/* y[m, n] = sum_k deq(W)[n, k] * x[m, k] over tiled weights (as vxb_gemv_q),*/
+/* x bf16 [M, K], y f32 or bf16 [M, N]. The weights are expanded per call   */
+/* into bf16 parts that sum to each weight exactly (2 for Q4_0, 3 for Q8_0) */
+/* in a context-owned scratch of 6*N*K bytes (grown on demand) and          */
+/* multiplied on tcgen05 tensor cores.                                       */
+/* ------------------------------------------------------------------------ */
+int vxb_gemm_q(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const uint16_t *d_x, int M, int y_dtype,
+               void *d_y, void *stream);
+
+/* ------------------------------------------------------------------------ */
 /* K3: flash-attention forward (prefill). Replaces flash_attention_forward   */
 /* and multi_head_flash_attention (src/flash_attention.rs:53-159, 519-564):  */
 /* per head O = softmax(scale * Q K^T, causal mask key > query) V and        */

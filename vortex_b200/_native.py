@@ -77,6 +77,7 @@ SIGNATURES = {
     "vxb_kv_block_table": (_I, [_P, _I, _I64, _P, _I, _P]),
     "vxb_kv_gather": (_I, [_P, _I, _I64, _P, _P, _P]),
     "vxb_decode_attention": (_I, [_P, _I, _I, _P, _P, _I, ctypes.c_float, _P, _P, _P]),
+    "vxb_gemm_q": (_I, [_P, _I, _P, _I, _I, _P, _I, _I, _P, _P]),
     "vxb_flash_fwd": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, ctypes.c_float, _I, _P, _P, _P]),
     "vxb_rmsnorm": (_I, [_P, _P, _P, _P, _I, _I, ctypes.c_float, _P, _P]),
     "vxb_swiglu": (_I, [_P, _P, _I, _I, _P, _P]),

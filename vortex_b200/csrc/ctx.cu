@@ -130,6 +130,7 @@ VXB_API int vxb_destroy(vxb_ctx *ctx) {
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->counters) cudaFree(ctx->counters);
   if (ctx->d_err) cudaFree(ctx->d_err);
+  if (ctx->gemm_ws) cudaFree(ctx->gemm_ws);
   if (cur >= 0) cudaSetDevice(cur);
   delete ctx;
   return VXB_OK;

@@ -25,6 +25,9 @@ struct vxb_ctx {
   size_t n_counters = 0;
   // device error word: kernels whose bounded waits time out set it to nonzero
   int *d_err = nullptr;
+  // bf16 hi/lo weight copies of the prefill GEMM (vxb_gemm_q), grown on demand
+  void *gemm_ws = nullptr;
+  size_t gemm_ws_bytes = 0;
 };
 
 namespace vxb {

@@ -3,6 +3,7 @@
     python -m vortex_b200.kernel_bench gemv [--fmt Q4_0] [--n 11008] [--k 4096] [--batch 1]
     python -m vortex_b200.kernel_bench attn [--ctx 8192] [--dtype bf16]
     python -m vortex_b200.kernel_bench flash [--b 4] [--h 32] [--s 4096] [--non-causal]
+    python -m vortex_b200.kernel_bench gemm [--m 2048] [--n 12288 ...] [--k 4096 ...]
 
 Each case streams its operands from HBM: the GEMV rotates over enough distinct
 weight copies to exceed twice the L2 (126 MB), the attention reads a KV cache
@@ -148,6 +149,27 @@ def flash_case(B: int = 4, H: int = 32, S: int = 4096, causal: bool = True, reps
             "flops": flops}
 
 
+def gemm_case(fmt="Q4_0", M: int = 2048, N: int = 11008, K: int = 4096, reps: int = 10, seed: int = 0):
+    """Prefill GEMM Y[M, N] = X[M, K] deq(W)^T, W ~ N(0, 0.02), X ~ N(0, 1)
+    bf16, Y f32. FLOPs = 2 M N K (algorithmic; the kernel runs the hi and lo
+    halves, twice that on the tensor pipe). The time includes the per-call
+    weight expansion."""
+    import torch
+
+    from . import quant as Q
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    tw = Q.TiledWeight.from_float(torch.randn(N, K, device="cuda", generator=gen) * 0.02, Q._fmt(fmt))
+    x = torch.randn(M, K, device="cuda", generator=gen).bfloat16()
+    y = tw.gemm(x)
+
+    def run():
+        tw.gemm(x, out=y)
+
+    t = _graph_time(torch, run, 1, reps)
+    flops = 2 * M * N * K
+    return {"fmt": fmt, "M": M, "N": N, "K": K, "us": t * 1e6, "TFLOPs": flops / t / 1e12, "flops": flops}
+
+
 def main():
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="what", required=True)
@@ -157,6 +179,12 @@ def main():
     g.add_argument("--k", type=int, default=None)
     g.add_argument("--batch", type=int, nargs="*", default=[1, 4, 16])
     g.add_argument("--reps", type=int, default=20)
+    m = sub.add_parser("gemm")
+    m.add_argument("--fmt", default="Q4_0")
+    m.add_argument("--m", type=int, default=2048)
+    m.add_argument("--n", type=int, nargs="*", default=[12288, 4096, 22016, 4096])
+    m.add_argument("--k", type=int, nargs="*", default=[4096, 4096, 4096, 11008])
+    m.add_argument("--reps", type=int, default=10)
     f = sub.add_parser("flash")
     f.add_argument("--b", type=int, default=4)
     f.add_argument("--h", type=int, default=32)
@@ -175,6 +203,9 @@ def main():
         shapes = [(args.n, args.k)] if args.n and args.k else [(4096, 4096), (11008, 4096), (4096, 11008)]
         for r in gemv_sweep(shapes, fmts, args.batch, args.reps):
             print(json.dumps(r), flush=True)
+    elif args.what == "gemm":
+        for n, k in zip(args.n, args.k):
+            print(json.dumps(gemm_case(args.fmt, args.m, n, k, args.reps)), flush=True)
     elif args.what == "flash":
         print(json.dumps(flash_case(args.b, args.h, args.s, not args.non_causal, args.reps)), flush=True)
     else:

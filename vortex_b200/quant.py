@@ -159,14 +159,34 @@ class TiledWeight:
         return out
 
 
+    def gemm(self, x, out=None, out_dtype=None):
+        """Y = X @ deq(W)^T for many rows (prefill GEMM on tcgen05): x bf16
+        [M, K], y f32 or bf16 [M, N]."""
+        torch = _torch()
+        if x.dtype != torch.bfloat16:
+            raise N.VxbError(N.VXB_EINVAL, "gemm expects bf16 activations")
+        x = x.contiguous()
+        M = x.numel() // self.K
+        if x.numel() != M * self.K:
+            raise N.VxbError(N.VXB_EINVAL, "activation size is not a multiple of K")
+        dt = out_dtype or (out.dtype if out is not None else torch.float32)
+        code = N.F32 if dt == torch.float32 else N.BF16
+        if out is None:
+            out = torch.empty((M, self.N), dtype=dt, device=x.device)
+        self.ctx.call("vxb_gemm_q", self.fmt, _dptr(self.tiled), self.N, self.K, _dptr(x), M, code, _dptr(out),
+                      _stream_ptr())
+        return out
+
+
 def weight_only_matmul(w: TiledWeight, activations):
     """Mirror of weight_only_matmul (src/quantize.rs:845-852) for W stored
-    [N, K]: returns activations [M, K] @ deq(W)^T as f32 [M, N]; rows are
-    processed in groups of up to 32 by the decode GEMV."""
+    [N, K]: returns activations [M, K] @ deq(W)^T as f32 [M, N]: the decode
+    GEMV for up to 32 rows, the tcgen05 GEMM above that."""
     torch = _torch()
     x = activations.to(torch.bfloat16).contiguous()
     M = x.shape[0]
+    if M > 32:
+        return w.gemm(x)
     out = torch.empty((M, w.N), dtype=torch.float32, device=x.device)
-    for m0 in range(0, M, 32):
-        w.gemv(x[m0:m0 + 32], out=out[m0:m0 + 32])
+    w.gemv(x, out=out)
     return out
