@@ -5,7 +5,8 @@ Workload (one "step" = one decode step of every sequence in the batch):
 32 layers, d_model 4096, 32 heads x 128, SwiGLU 11008, RMSNorm, RoPE,
 vocab 32000, every linear Q4_0 (block 32, f16 scales) from N(0, 0.02)
 synthetic weights, a 2048-token random-id prompt per sequence, then decode
-steps at batch 32 (headline) and batch 1. KV cache bf16, paged.
+steps at batch 32 (headline) and batch 1. KV cache bf16, paged. Prompts are
+prefilled in one pass per sequence (prefill GEMM + flash attention).
 
 Prints one JSON line (rank 0). With torchrun (N > 1) the ranks run one
 tensor-parallel decoder (heads, FFN rows and vocabulary split over the N GPUs,
@@ -267,15 +268,20 @@ def time_attention(dec, seq_ids, hd_heads, reps=20):
 
 
 def run_decode(dec, seq_ids, prompt, steps, warmup, ws, torch):
-    """Prefill token by token (untimed), warm up, then time `steps` decode
-    steps with CUDA events on the decoder's stream."""
+    """Prefill every sequence's prompt in one pass (K2 GEMM + K3 flash
+    attention; timed separately), warm up, then time `steps` decode steps with
+    CUDA events on the decoder's stream. Returns (decode seconds, next tokens,
+    prefill seconds)."""
     import numpy as np
     B = len(seq_ids)
-    tok = torch.from_numpy(prompt[:, 0].astype(np.int32)).cuda()
     nxt = torch.empty(B, dtype=torch.int32, device="cuda")
-    for t in range(prompt.shape[1]):
-        tok.copy_(torch.from_numpy(prompt[:, t].astype(np.int32)))
-        dec.step_device(seq_ids, tok, nxt)
+    torch.cuda.synchronize()
+    barrier(ws)
+    t0 = time.perf_counter()
+    first = [dec.prefill(s, prompt[i]) for i, s in enumerate(seq_ids)]
+    t_prefill = time.perf_counter() - t0
+    nxt.copy_(torch.tensor(first, dtype=torch.int32))
+    tok = nxt.clone()
     for _ in range(warmup):
         tok.copy_(nxt)
         dec.step_device(seq_ids, tok, nxt)
@@ -293,7 +299,7 @@ def run_decode(dec, seq_ids, prompt, steps, warmup, ws, torch):
     torch.cuda.synchronize()
     torch.cuda.profiler.stop()
     barrier(ws)
-    return e0.elapsed_time(e1) * 1e-3, nxt
+    return e0.elapsed_time(e1) * 1e-3, nxt, t_prefill
 
 
 def main():
@@ -323,7 +329,8 @@ def main():
 
     sampler = ClockSampler(local)
     sampler.start()
-    t_dev, nxt = run_decode(dec, seq_ids, prompt, args.steps, args.warmup, ws, torch)
+    t_dev, nxt, t_prefill = run_decode(dec, seq_ids, prompt, args.steps, args.warmup, ws, torch)
+    t_prefill = max_over_ranks(t_prefill, ws)
     clocks = sampler.stop()
     t_max = max_over_ranks(t_dev, ws)
     value = B * args.steps / t_max
@@ -353,7 +360,7 @@ def main():
     if not args.no_batch1:
         dec.free_seq(seq_ids[-1])
         sid = [10_000]
-        t1, _ = run_decode(dec, sid, prompt[:1], args.steps, args.warmup, ws, torch)
+        t1, _, _ = run_decode(dec, sid, prompt[:1], args.steps, args.warmup, ws, torch)
         b1 = max_over_ranks(t1, ws)
     barrier(ws)
 
@@ -388,6 +395,9 @@ def main():
                        "prompt_len": args.prompt_len, "decode_steps": args.steps,
                        "parallelism": f"tp{ws}" if ws > 1 else "single",
                        "l2": "inputs larger than L2 (3.7 GB weights + KV per step)"},
+            "prefill": {"tokens_per_s": B * args.prompt_len / t_prefill, "seconds": t_prefill,
+                        "sequences": B, "prompt_len": args.prompt_len,
+                        "note": "host wall time of vxb_decoder_prefill per sequence (K2 GEMM + K3 flash)"},
             "batch1_tokens_per_s": (args.steps / b1) if b1 else None,
             "batch1_ms_per_step": (b1 / args.steps * 1e3) if b1 else None,
             "roofline": {"kernel": "decode_attn_kernel (layer 0, batch %d)" % B, "bound": "hbm",

@@ -272,6 +272,13 @@ int vxb_decoder_set_weight(vxb_decoder *d, int layer, int which, const void *h_d
  * (optional) the logits [batch, vocab]. */
 int vxb_decoder_step(vxb_decoder *d, int batch, const int64_t *h_seq_ids, const int32_t *h_tokens,
                      int32_t *h_next, float *h_logits);
+/* Prompt of n tokens for a new (empty) sequence in one pass: K2 GEMMs over
+ * the n rows and the causal K3 flash attention (head_dim 128), K/V of every
+ * position cached. h_next / h_logits (optional) get the greedy next token and
+ * the last position's logits [vocab]. Synchronous; the same call on every
+ * rank with tensor parallelism. */
+int vxb_decoder_prefill(vxb_decoder *d, int64_t seq_id, const int32_t *h_tokens, int n, int32_t *h_next,
+                        float *h_logits);
 /* The same with device token buffers, ordered on `stream`. */
 int vxb_decoder_step_device(vxb_decoder *d, int batch, const int64_t *h_seq_ids,
                             const int32_t *d_tokens, int32_t *d_next, void *stream);

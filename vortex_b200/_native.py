@@ -92,6 +92,7 @@ SIGNATURES = {
     "vxb_decoder_init_random": (_I, [_P, ctypes.c_uint64, ctypes.c_float]),
     "vxb_decoder_set_weight": (_I, [_P, _I, _I, _P, _SZ]),
     "vxb_decoder_step": (_I, [_P, _I, _P, _P, _P, _P]),
+    "vxb_decoder_prefill": (_I, [_P, _I64, _P, _I, _P, _P]),
     "vxb_decoder_step_device": (_I, [_P, _I, _P, _P, _P, _P]),
     "vxb_decoder_logits": (_I, [_P, _I, _P, _P]),
     "vxb_decoder_free_seq": (_I, [_P, _I64]),

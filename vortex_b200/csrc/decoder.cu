@@ -35,6 +35,7 @@
 
 #include "comm.h"
 #include "decode_attn.h"
+#include "gemm.h"
 #include "gemv.h"
 #include "kv_cache.h"
 #include "layer_ops.h"
@@ -93,6 +94,16 @@ struct vxb_decoder {
   };
   std::map<int, Graph> graphs;  // by batch size
   std::vector<void *> allocs;
+  // prompt (prefill) activations, sized for the longest prompt seen
+  struct Prefill {
+    int cap = 0;
+    float *x = nullptr, *qkv = nullptr, *gu = nullptr;
+    uint16_t *h = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *act = nullptr;
+    int32_t *tokens = nullptr;
+    KVPlace *places = nullptr;     // [n_layers][cap]
+    float *lse = nullptr;
+    std::vector<void *> allocs;
+  } pf;
 };
 
 namespace {
@@ -290,6 +301,7 @@ VXB_API int vxb_decoder_destroy(vxb_decoder *d) {
     if (kvp.second.exec) cudaGraphExecDestroy(kvp.second.exec);
   if (d->kv) vxb_kv_destroy(d->kv);
   for (void *p : d->allocs) cudaFree(p);
+  for (void *p : d->pf.allocs) cudaFree(p);
   if (d->h_next) cudaFreeHost(d->h_next);
   for (auto &s : d->ring) {
     if (s.host) cudaFreeHost(s.host);
@@ -577,6 +589,145 @@ int launch_step(vxb_decoder *d, int B, const int64_t *seq_ids, const int32_t *d_
 }
 
 }  // namespace
+
+namespace {
+
+int pf_alloc(vxb_decoder *d, void **p, size_t bytes) {
+  if (cudaMalloc(p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    *p = nullptr;
+    return set_error(d->ctx, VXB_ENOMEM, "decoder prefill: device allocation of %zu bytes failed", bytes);
+  }
+  d->pf.allocs.push_back(*p);
+  return VXB_OK;
+}
+
+template <typename T>
+int pf_alloc_t(vxb_decoder *d, T **p, size_t count) {
+  return pf_alloc(d, reinterpret_cast<void **>(p), count * sizeof(T));
+}
+
+int pf_reserve(vxb_decoder *d, int n) {
+  auto &P = d->pf;
+  if (n <= P.cap) return VXB_OK;
+  VXB_CUDA_TRY(d->ctx, cudaStreamSynchronize(d->stream));
+  for (void *p : P.allocs) cudaFree(p);
+  P.allocs.clear();
+  P.cap = 0;
+  const vxb_decoder_config &c = d->cfg;
+  const size_t N = (size_t)n;
+  int rc = pf_alloc_t(d, &P.x, N * c.dim);
+  if (!rc) rc = pf_alloc_t(d, &P.qkv, N * d->qkv_n);
+  if (!rc) rc = pf_alloc_t(d, &P.gu, N * 2 * d->ffn);
+  if (!rc) rc = pf_alloc_t(d, &P.h, N * c.dim);
+  if (!rc) rc = pf_alloc_t(d, &P.q, N * d->qdim);
+  if (!rc) rc = pf_alloc_t(d, &P.k, N * d->kvdim);
+  if (!rc) rc = pf_alloc_t(d, &P.v, N * d->kvdim);
+  if (!rc) rc = pf_alloc_t(d, &P.attn, N * d->qdim);
+  if (!rc) rc = pf_alloc_t(d, &P.act, N * d->ffn);
+  if (!rc) rc = pf_alloc_t(d, &P.tokens, N);
+  if (!rc) rc = pf_alloc_t(d, &P.places, N * c.n_layers);
+  if (!rc) rc = pf_alloc_t(d, &P.lse, N * d->hq);
+  if (!rc) P.cap = n;
+  return rc;
+}
+
+}  // namespace
+
+// Prompt of n tokens for a new sequence in one pass (prefill): every
+// projection is a K2 GEMM over the n rows, attention is the causal K3 flash
+// kernel over the prompt, and the K/V of all n positions enter the cache.
+// h_next (optional) gets the greedy next token, h_logits (optional) the
+// logits [vocab] of the last position. Synchronous. With tensor parallelism
+// every rank calls it with the same arguments.
+VXB_API int vxb_decoder_prefill(vxb_decoder *d, int64_t seq_id, const int32_t *h_tokens, int n, int32_t *h_next,
+                                float *h_logits) {
+  if (!d || !h_tokens) return set_error(d ? d->ctx : nullptr, VXB_EINVAL, "vxb_decoder_prefill: null argument");
+  const vxb_decoder_config &c = d->cfg;
+  vxb_ctx *ctx = d->ctx;
+  if (n < 1 || n > c.max_seq) return set_error(ctx, VXB_EINVAL, "vxb_decoder_prefill: %d tokens (1..%d)", n, c.max_seq);
+  if (c.dim / c.n_heads != 128)
+    return set_error(ctx, VXB_EUNSUPPORTED, "vxb_decoder_prefill: head_dim %d (the prefill attention needs 128)",
+                     c.dim / c.n_heads);
+  if (!d->emb || !d->wlm || !d->layers[0].wqkv) return set_error(ctx, VXB_EINVAL, "decoder: weights not loaded");
+  for (int i = 0; i < n; i++)
+    if (h_tokens[i] < 0 || h_tokens[i] >= c.vocab_size)
+      return set_error(ctx, VXB_EINVAL, "vxb_decoder_prefill: token %d out of range", h_tokens[i]);
+  if (int rc = use_device(ctx)) return rc;
+  for (int l = 0; l < c.n_layers; l++) {
+    auto it = d->kv->tables.find(std::make_pair(l, seq_id));
+    if (it != d->kv->tables.end() && it->second.len > 0)
+      return set_error(ctx, VXB_EINVAL, "vxb_decoder_prefill: sequence %lld already holds tokens", (long long)seq_id);
+  }
+  cudaStream_t st = d->stream;
+  // any queued decode step still reads the staging ring and activations
+  VXB_CUDA_TRY(ctx, cudaStreamSynchronize(st));
+  if (int rc = pf_reserve(d, n)) return rc;
+  auto &P = d->pf;
+  // KV placements of every position in every layer (host allocator)
+  std::vector<KVPlace> pl((size_t)n * c.n_layers);
+  for (int l = 0; l < c.n_layers; l++)
+    for (int i = 0; i < n; i++)
+      if (int rc = kv_place(d->kv, l, seq_id, &pl[(size_t)l * n + i])) {
+        kv_unplace(d->kv, l, seq_id, i);
+        for (int ll = l - 1; ll >= 0; ll--) kv_unplace(d->kv, ll, seq_id, n);
+        return rc;
+      }
+  VXB_CUDA_TRY(ctx, cudaMemcpyAsync(P.places, pl.data(), pl.size() * sizeof(KVPlace), cudaMemcpyHostToDevice, st));
+  VXB_CUDA_TRY(ctx, cudaMemcpyAsync(P.tokens, h_tokens, (size_t)n * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+  size_t scratch_bytes = std::max(std::max(gemm_scratch_bytes(d->qkv_n, c.dim), gemm_scratch_bytes(c.dim, d->qdim)),
+                                  std::max(gemm_scratch_bytes(2 * d->ffn, c.dim), gemm_scratch_bytes(c.dim, d->ffn)));
+  void *scratch = nullptr;
+  if (int rc = gemm_ws_reserve(ctx, scratch_bytes, &scratch)) return rc;
+  const int fmt = c.weight_fmt;
+  const float eps = c.norm_eps, scale = 1.0f / sqrtf(128.f);
+  int rc = embed_launch(ctx, d->emb, P.tokens, n, c.dim, c.vocab_size, P.x, st);
+  for (int l = 0; l < c.n_layers && !rc; l++) {
+    auto &L = d->layers[l];
+    rc = rmsnorm_launch(ctx, P.x, L.ln1_w, L.ln1_b, n, c.dim, eps, P.h, st);
+    if (!rc) rc = gemm_q_launch(ctx, fmt, L.wqkv, d->qkv_n, c.dim, P.h, n, VXB_F32, P.qkv, nullptr, scratch, st);
+    if (!rc)
+      rc = rope_launch(ctx, P.qkv, n, d->qdim, d->kvdim, P.places + (size_t)l * n, d->rope_div, P.q, P.k, P.v, st,
+                       d->rank * d->qdim / 2, d->rank * d->kvdim / 2);
+    if (!rc) rc = kv_append_launch(d->kv, l, n, P.places + (size_t)l * n, P.k, P.v, st);
+    if (!rc)
+      rc = vxb_flash_fwd(ctx, P.q, P.k, P.v, 1, d->hq, d->hkv, n, 128, scale, 1, P.attn, P.lse, st);
+    if (!rc)
+      rc = gemm_q_launch(ctx, fmt, L.wo, c.dim, d->qdim, P.attn, n, VXB_F32, P.x, d->rank == 0 ? P.x : nullptr, scratch, st);
+    if (!rc && d->tp > 1) rc = comm_allreduce(d->comm, P.x, (size_t)n * c.dim, VXB_F32, 0, st);
+    if (!rc) rc = rmsnorm_launch(ctx, P.x, L.ln2_w, L.ln2_b, n, c.dim, eps, P.h, st);
+    if (!rc) rc = gemm_q_launch(ctx, fmt, L.wgu, 2 * d->ffn, c.dim, P.h, n, VXB_F32, P.gu, nullptr, scratch, st);
+    if (!rc) rc = swiglu_launch(ctx, P.gu, n, d->ffn, P.act, st);
+    if (!rc)
+      rc = gemm_q_launch(ctx, fmt, L.wdown, c.dim, d->ffn, P.act, n, VXB_F32, P.x, d->rank == 0 ? P.x : nullptr, scratch, st);
+    if (!rc && d->tp > 1) rc = comm_allreduce(d->comm, P.x, (size_t)n * c.dim, VXB_F32, 0, st);
+  }
+  // the last position's logits and greedy token (decode-step buffers, row 0)
+  const float *xl = P.x + (size_t)(n - 1) * c.dim;
+  if (!rc) rc = rmsnorm_launch(ctx, xl, d->lnf_w, d->lnf_b, 1, c.dim, eps, d->h, st);
+  if (!rc) rc = gemv_launch(ctx, fmt, d->wlm, d->vocab, c.dim, d->h, 1, VXB_F32, d->logits, nullptr, st, nullptr);
+  if (d->tp == 1) {
+    if (!rc) rc = argmax_launch(ctx, d->logits, 1, c.vocab_size, d->d_next, st);
+  } else {
+    if (!rc) rc = argmax_key_launch(ctx, d->logits, 1, d->vocab, d->rank * d->vocab, d->d_keys, st);
+    if (!rc) rc = comm_allreduce(d->comm, d->d_keys, 1, -1, 1, st);
+    if (!rc) rc = key_to_token_launch(ctx, d->d_keys, 1, d->d_next, st);
+  }
+  if (rc) return rc;
+  if (h_logits) {
+    const float *src = d->logits;
+    if (d->tp > 1) {
+      if (int r2 = comm_allgather_f32(d->comm, d->logits, d->logits_all, (size_t)d->vocab, st)) return r2;
+      if (int r2 = unshard_launch(ctx, d->logits_all, d->tp, 1, d->vocab, d->logits_full, st)) return r2;
+      src = d->logits_full;
+    }
+    VXB_CUDA_TRY(ctx, cudaMemcpyAsync(h_logits, src, (size_t)c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost, st));
+  }
+  if (h_next) VXB_CUDA_TRY(ctx, cudaMemcpyAsync(d->h_next, d->d_next, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+  VXB_CUDA_TRY(ctx, cudaStreamSynchronize(st));
+  if (h_next) *h_next = d->h_next[0];
+  return VXB_OK;
+}
 
 // One decode step through host buffers: h_tokens [B] in, h_next [B] out
 // (greedy argmax), optional h_logits [B, vocab]. Synchronous.

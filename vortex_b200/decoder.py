@@ -81,6 +81,17 @@ class Decoder:
                                              logits.ctypes.data_as(ctypes.c_void_p) if want_logits else None))
         return (nxt, logits) if want_logits else nxt
 
+    def prefill(self, seq_id: int, tokens, want_logits: bool = False):
+        """Whole prompt of a new sequence in one pass (K2 GEMM + K3 flash
+        attention); returns the greedy next token (and the last logits)."""
+        tok = np.ascontiguousarray(tokens, dtype=np.int32)
+        nxt = np.zeros(1, dtype=np.int32)
+        logits = np.zeros(self.vocab, dtype=np.float32) if want_logits else None
+        self._check(N.lib().vxb_decoder_prefill(self.ptr, int(seq_id), tok.ctypes.data_as(ctypes.c_void_p), tok.size,
+                                                nxt.ctypes.data_as(ctypes.c_void_p),
+                                                logits.ctypes.data_as(ctypes.c_void_p) if want_logits else None))
+        return (int(nxt[0]), logits) if want_logits else int(nxt[0])
+
     def step_device(self, seq_ids, d_tokens, d_next, stream=None):
         import torch
         ids = np.ascontiguousarray(seq_ids, dtype=np.int64)
