@@ -287,6 +287,26 @@ int vxb_decoder_free_seq(vxb_decoder *d, int64_t seq_id);
 int vxb_decoder_kv(vxb_decoder *d, vxb_kv **out);
 int vxb_decoder_stream(vxb_decoder *d, void **out);
 
+/* ------------------------------------------------------------------------ */
+/* f32 GPT-style model of src/transformer.rs:15-841 (TransformerModel):      */
+/* embedding + sinusoidal positions, pre-norm layers (LayerNorm 1e-5,        */
+/* biased multi-head attention with an optional [S, S] mask, entries < 0.5  */
+/* masked to -1e9; GELU feed-forward), final LayerNorm, output projection.  */
+/* create = TransformerModel::new (Xavier from the xorshift seed 42);      */
+/* parameters in params_vec order; forward = TransformerModel::forward.    */
+/* ------------------------------------------------------------------------ */
+typedef struct vxb_tmodel_config {
+    int vocab_size, d_model, n_heads, n_layers, d_ff, max_seq_len;
+} vxb_tmodel_config;
+typedef struct vxb_tmodel vxb_tmodel;
+int vxb_tmodel_create(vxb_ctx *ctx, const vxb_tmodel_config *cfg, vxb_tmodel **out);
+int vxb_tmodel_destroy(vxb_tmodel *m);
+int vxb_tmodel_param_count(const vxb_tmodel *m, size_t *n);
+int vxb_tmodel_set_params(vxb_tmodel *m, const float *h_params, size_t n);
+int vxb_tmodel_get_params(vxb_tmodel *m, float *h_params, size_t n);
+/* logits [S, vocab] f32 of S tokens; h_mask [S, S] f32 or NULL. Synchronous. */
+int vxb_tmodel_forward(vxb_tmodel *m, const int32_t *h_tokens, int S, const float *h_mask, float *h_logits);
+
 #ifdef __cplusplus
 }
 #endif

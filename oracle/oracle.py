@@ -72,6 +72,14 @@ def lib():
             "vxo_rope_embed": (None, [_P, _SZ, ctypes.c_int64, ctypes.c_int64, _P]),
             "vxo_silu": (ctypes.c_double, [ctypes.c_double]),
             "vxo_matvec": (None, [_P, _P, _SZ, _SZ, _P]),
+            "vxo_tf_param_count": (_SZ, [_P]),
+            "vxo_tf_init": (None, [_P, ctypes.c_uint64, _P]),
+            "vxo_tf_pos_encoding": (None, [_SZ, _SZ, _P]),
+            "vxo_tf_linear": (None, [_P, _SZ, _P, _P, _SZ, _SZ, _P]),
+            "vxo_tf_layernorm": (None, [_P, _SZ, _SZ, _P, _P, ctypes.c_float, _P]),
+            "vxo_tf_gelu": (None, [_P, _SZ, _P]),
+            "vxo_tf_softmax_rows": (None, [_P, _SZ, _SZ, _P]),
+            "vxo_tf_forward": (None, [_P, _P, _P, _SZ, _P, _P]),
             "vxo_int8_dot": (ctypes.c_int32, [_P, _P, _SZ]),
             "vxo_int4_dot": (ctypes.c_int32, [_P, _P, _SZ]),
         }
@@ -351,3 +359,77 @@ def int4_dot(a, b) -> int:
     a = np.ascontiguousarray(a, dtype=np.uint8)
     b = np.ascontiguousarray(b, dtype=np.uint8)
     return lib().vxo_int4_dot(_p(a), _p(b), a.size)
+
+
+# ---- f32 GPT-style model (src/transformer.rs:15-841) ----
+class TFConfig(ctypes.Structure):
+    _fields_ = [("vocab", _SZ), ("d_model", _SZ), ("n_heads", _SZ), ("n_layers", _SZ), ("d_ff", _SZ),
+                ("max_seq", _SZ)]
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def tf_config(vocab, d_model, n_heads, n_layers, d_ff, max_seq) -> TFConfig:
+    return TFConfig(vocab, d_model, n_heads, n_layers, d_ff, max_seq)
+
+
+def tf_param_count(cfg: TFConfig) -> int:
+    return lib().vxo_tf_param_count(ctypes.byref(cfg))
+
+
+def tf_init(cfg: TFConfig, seed: int = 42) -> np.ndarray:
+    """TransformerModel::new: params in params_vec order."""
+    out = np.zeros(tf_param_count(cfg), dtype=np.float32)
+    lib().vxo_tf_init(ctypes.byref(cfg), seed, _p(out))
+    return out
+
+
+def tf_pos_encoding(max_len: int, d: int) -> np.ndarray:
+    out = np.zeros((max_len, d), dtype=np.float32)
+    lib().vxo_tf_pos_encoding(max_len, d, _p(out))
+    return out
+
+
+def tf_linear(x, w, b=None) -> np.ndarray:
+    x, w = _f32(x), _f32(w)
+    m, k = x.shape
+    n = w.shape[0]
+    y = np.zeros((m, n), dtype=np.float32)
+    bb = _f32(b) if b is not None else None
+    lib().vxo_tf_linear(_p(x), m, _p(w), _p(bb) if bb is not None else None, k, n, _p(y))
+    return y
+
+
+def tf_layernorm(x, g, b, eps=1e-5) -> np.ndarray:
+    x = _f32(x)
+    rows, d = x.shape
+    y = np.zeros_like(x)
+    lib().vxo_tf_layernorm(_p(x), rows, d, _p(_f32(g)), _p(_f32(b)), eps, _p(y))
+    return y
+
+
+def tf_gelu(x) -> np.ndarray:
+    x = _f32(x)
+    y = np.zeros_like(x)
+    lib().vxo_tf_gelu(_p(x), x.size, _p(y))
+    return y
+
+
+def tf_softmax_rows(x) -> np.ndarray:
+    x = _f32(x)
+    y = np.zeros_like(x)
+    lib().vxo_tf_softmax_rows(_p(x), x.shape[0], x.shape[1], _p(y))
+    return y
+
+
+def tf_forward(cfg: TFConfig, params, tokens, mask=None) -> np.ndarray:
+    """TransformerModel::forward: logits [S, vocab] (mask [S, S] or None)."""
+    p = _f32(params)
+    t = np.ascontiguousarray(tokens, dtype=np.int64)
+    S = t.size
+    out = np.zeros((S, cfg.vocab), dtype=np.float32)
+    m = _f32(mask) if mask is not None else None
+    lib().vxo_tf_forward(ctypes.byref(cfg), _p(p), _p(t), S, _p(m) if m is not None else None, _p(out))
+    return out

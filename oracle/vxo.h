@@ -102,6 +102,20 @@ void vxo_rope_embed(const double *x, size_t n, int64_t pos, int64_t dim, double 
 double vxo_silu(double x);
 void vxo_matvec(const double *w, const double *v, size_t out_dim, size_t in_dim, double *out);
 
+/* ---- f32 GPT-style model (src/transformer.rs:15-841), oracle/vxo_tf.c ---- */
+typedef struct {
+    size_t vocab, d_model, n_heads, n_layers, d_ff, max_seq;
+} vxo_tf_config;
+size_t vxo_tf_param_count(const vxo_tf_config *c);
+void vxo_tf_init(const vxo_tf_config *c, uint64_t seed, float *params);
+void vxo_tf_pos_encoding(size_t max_len, size_t d, float *out);
+void vxo_tf_linear(const float *x, size_t m, const float *w, const float *b, size_t in, size_t out, float *y);
+void vxo_tf_layernorm(const float *x, size_t rows, size_t d, const float *g, const float *b, float eps, float *y);
+void vxo_tf_gelu(const float *x, size_t n, float *y);
+void vxo_tf_softmax_rows(const float *x, size_t rows, size_t cols, float *y);
+void vxo_tf_forward(const vxo_tf_config *c, const float *params, const int64_t *tokens, size_t S, const float *mask,
+                    float *logits);
+
 /* ---- int dot primitives (src/bytecarry.rs:491-513) ---- */
 int32_t vxo_int8_dot(const int8_t *a, const int8_t *b, size_t n);
 int32_t vxo_int4_dot(const uint8_t *a, const uint8_t *b, size_t nbytes);

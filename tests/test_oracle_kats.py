@@ -317,3 +317,47 @@ def test_golden_kats_file_matches_oracle():
         assert list(O.dequantize_blocks(O.GGML_Q8_0, bytes(case["block"]), 32)) == case["values"]
     for case in kats["f16"]:
         assert O.f16_to_f32(case["bits"]) == case["value"]
+
+
+# ---- f32 model, src/transformer.rs tests (1094-1250) ----
+
+def test_tf_matmul_kat():
+    # [2,3] x [3,2] -> [[4, 2], [10, 5]] (test_matmul); the oracle's linear
+    # takes the weight [out, in], i.e. the transposed right factor
+    a = np.array([[1, 2, 3], [4, 5, 6]], np.float32)
+    b = np.array([[1, 0], [0, 1], [1, 0]], np.float32)
+    assert np.array_equal(O.tf_linear(a, b.T), np.array([[4, 2], [10, 5]], np.float32))
+
+
+def test_tf_positional_encoding_kat():
+    pe = O.tf_pos_encoding(10, 8)  # test_positional_encoding
+    assert pe.shape == (10, 8)
+    assert abs(pe[0, 0]) < 1e-5 and abs(pe[0, 1] - 1.0) < 1e-5
+    assert np.all(pe >= -1 - 1e-6) and np.all(pe <= 1 + 1e-6)
+
+
+def test_tf_layer_norm_kat():
+    x = np.array([[1, 2, 3, 4], [5, 6, 7, 8]], np.float32)  # test_layer_norm
+    y = O.tf_layernorm(x, np.ones(4, np.float32), np.zeros(4, np.float32))
+    assert np.all(np.abs(y.sum(axis=1) / 4) < 1e-4)
+
+
+def test_tf_softmax_and_gelu_kats():
+    s = O.tf_softmax_rows(np.array([[1, 2, 3, 4]], np.float32))[0]  # test_softmax
+    assert abs(s.sum() - 1) < 1e-5 and s[0] < s[1] < s[2] < s[3]
+    g = O.tf_gelu(np.array([-2, -1, 0, 1, 2], np.float32))  # test_gelu_activation
+    assert abs(g[2]) < 1e-5 and g[3] > 0 and g[4] > 0 and g[0] < 0
+
+
+def test_tf_model_shapes_kat():
+    # small_config = TransformerConfig::new(64, 16, 2, 1, 32, 32, 0.0):
+    # test_model_creation / test_forward_pass_shape
+    c = O.tf_config(64, 16, 2, 1, 32, 32)
+    p = O.tf_init(c)
+    emb, layer, final, out = 64 * 16, 4 * (16 * 16 + 16) + (32 * 16 + 32) + (16 * 32 + 16) + 4 * 16, 2 * 16, 64 * 16 + 64
+    assert p.size == emb + layer + final + out
+    logits = O.tf_forward(c, p, [0, 1, 2, 3])
+    assert logits.shape == (4, 64) and np.all(np.isfinite(logits))
+    # Xavier bound of the embedding (fan_in 64, fan_out 16) and zero biases
+    assert np.max(np.abs(p[:emb])) <= np.sqrt(6 / 80) + 1e-7
+    assert np.all(p[emb + 16 * 16:emb + 16 * 16 + 16] == 0)

@@ -98,6 +98,12 @@ SIGNATURES = {
     "vxb_decoder_free_seq": (_I, [_P, _I64]),
     "vxb_decoder_kv": (_I, [_P, ctypes.POINTER(_P)]),
     "vxb_decoder_stream": (_I, [_P, ctypes.POINTER(_P)]),
+    "vxb_tmodel_create": (_I, [_P, _P, ctypes.POINTER(_P)]),
+    "vxb_tmodel_destroy": (_I, [_P]),
+    "vxb_tmodel_param_count": (_I, [_P, ctypes.POINTER(_SZ)]),
+    "vxb_tmodel_set_params": (_I, [_P, _P, _SZ]),
+    "vxb_tmodel_get_params": (_I, [_P, _P, _SZ]),
+    "vxb_tmodel_forward": (_I, [_P, _P, _I, _P, _P]),
 }
 
 _lib = None
