@@ -288,6 +288,32 @@ int vxb_decoder_kv(vxb_decoder *d, vxb_kv **out);
 int vxb_decoder_stream(vxb_decoder *d, void **out);
 
 /* ------------------------------------------------------------------------ */
+/* GGUF reader. Replaces parse_gguf / get_tensor (src/gguf_loader.rs:       */
+/* 341-408, 536-584) for the quantized path: the file is memory-mapped (or  */
+/* a caller buffer is parsed in place; it must outlive the handle), parse    */
+/* errors carry the reference's messages (vxb_last_error(NULL)), and Q4_0 /  */
+/* Q8_0 tensors upload as their blocks into the tiled device layout (no f32  */
+/* dequantization): rows = product of the dimensions after the first, K =   */
+/* the first (fastest) dimension.                                            */
+/* ------------------------------------------------------------------------ */
+typedef struct vxb_gguf vxb_gguf;
+int vxb_gguf_open(const char *path, vxb_gguf **out);
+int vxb_gguf_open_memory(const void *data, size_t nbytes, vxb_gguf **out);
+int vxb_gguf_close(vxb_gguf *g);
+int vxb_gguf_info(const vxb_gguf *g, uint32_t *version, int64_t *n_tensors, int64_t *n_metadata,
+                  uint64_t *data_offset, uint64_t *alignment);
+/* dims4: the dimensions as stored, padded with 1; h_data: the tensor's bytes
+ * inside the mapping (bounds-checked as get_tensor). Any output may be NULL. */
+int vxb_gguf_tensor(const vxb_gguf *g, int64_t index, char *name, size_t name_cap, int *ggml_type, int *n_dims,
+                    uint64_t *dims4, uint64_t *offset, uint64_t *nbytes, const void **h_data);
+int vxb_gguf_find_tensor(const vxb_gguf *g, const char *name, int64_t *index);
+int vxb_gguf_meta_int(const vxb_gguf *g, const char *key, int64_t *value);
+int vxb_gguf_meta_float(const vxb_gguf *g, const char *key, double *value);
+int vxb_gguf_meta_string(const vxb_gguf *g, const char *key, char *out, size_t cap, size_t *len);
+int vxb_gguf_upload_tiled(vxb_ctx *ctx, const vxb_gguf *g, int64_t index, void *d_tiled, size_t tiled_bytes,
+                          void *stream);
+
+/* ------------------------------------------------------------------------ */
 /* f32 GPT-style model of src/transformer.rs:15-841 (TransformerModel):      */
 /* embedding + sinusoidal positions, pre-norm layers (LayerNorm 1e-5,        */
 /* biased multi-head attention with an optional [S, S] mask, entries < 0.5  */

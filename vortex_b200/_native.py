@@ -98,6 +98,16 @@ SIGNATURES = {
     "vxb_decoder_free_seq": (_I, [_P, _I64]),
     "vxb_decoder_kv": (_I, [_P, ctypes.POINTER(_P)]),
     "vxb_decoder_stream": (_I, [_P, ctypes.POINTER(_P)]),
+    "vxb_gguf_open": (_I, [ctypes.c_char_p, ctypes.POINTER(_P)]),
+    "vxb_gguf_open_memory": (_I, [_P, _SZ, ctypes.POINTER(_P)]),
+    "vxb_gguf_close": (_I, [_P]),
+    "vxb_gguf_info": (_I, [_P, _P, _P, _P, _P, _P]),
+    "vxb_gguf_tensor": (_I, [_P, _I64, _P, _SZ, _P, _P, _P, _P, _P, _P]),
+    "vxb_gguf_find_tensor": (_I, [_P, ctypes.c_char_p, _P]),
+    "vxb_gguf_meta_int": (_I, [_P, ctypes.c_char_p, _P]),
+    "vxb_gguf_meta_float": (_I, [_P, ctypes.c_char_p, _P]),
+    "vxb_gguf_meta_string": (_I, [_P, ctypes.c_char_p, _P, _SZ, _P]),
+    "vxb_gguf_upload_tiled": (_I, [_P, _P, _I64, _P, _SZ, _P]),
     "vxb_tmodel_create": (_I, [_P, _P, ctypes.POINTER(_P)]),
     "vxb_tmodel_destroy": (_I, [_P]),
     "vxb_tmodel_param_count": (_I, [_P, ctypes.POINTER(_SZ)]),

@@ -126,6 +126,17 @@ class TiledWeight:
         self.ctx.call("vxb_tile_weights", self.fmt, _dptr(blocks), self.N, self.K, _dptr(self.tiled), _stream_ptr())
 
     @classmethod
+    def from_tiled(cls, tiled, fmt, n_rows: int, k_cols: int):
+        """Wrap an already tiled device buffer (e.g. from a GGUF upload)."""
+        self = cls.__new__(cls)
+        self.fmt = _fmt(fmt)
+        self.N, self.K = int(n_rows), int(k_cols)
+        self.device = tiled.device
+        self.tiled = tiled
+        self.ctx = context(tiled.device.index)
+        return self
+
+    @classmethod
     def from_float(cls, w, fmt):
         """Quantize a float32 CUDA matrix [N, K] on the device and tile it."""
         blocks = quantize_blocks(w.reshape(-1), fmt)
