@@ -8,18 +8,21 @@
 // batch the reference's [N, H*d] rows with the heads interleaved,
 // src/flash_attention.rs:545-551), d = 128; grouped K/V heads (Hkv | H).
 //
-// One CTA per (128-query tile, head, batch), 5 warps:
-//  * warp 4 (one elected thread) loads Q once and K/V tiles of 128 keys into
-//    a double-buffered ring with TMA (4-D tensor maps, 128-byte swizzle), and
-//    issues the MMAs: S = Q K^T (M=128, N=128, K=128 as 8 x K16) into TMEM
-//    columns [0,128), then O += P V (A = P from shared memory, B = V read
-//    MN-major) into TMEM columns [128,256). Completion is signalled to
-//    mbarriers with tcgen05.commit.
+// One CTA per (128-query tile, head, batch), 6 warps:
+//  * warp 5 (one elected thread) loads Q once and the K and V tiles of 128
+//    keys into two separate double-buffered rings with TMA (4-D tensor maps,
+//    128-byte swizzle); a K stage is refilled as soon as its S = Q K^T has
+//    completed, a V stage once its P.V has.
+//  * warp 4 (one elected thread) issues the MMAs: S = Q K^T (M=128, N=128,
+//    K=128 as 8 x K16) into TMEM columns [0,128), then O += P V (A = P from
+//    shared memory, B = V read MN-major) into TMEM columns [128,256).
+//    Completion is signalled to mbarriers with tcgen05.commit.
 //  * warps 0-3 own one query row each (TMEM lane = row): they read the row of
 //    S with tcgen05.ld, apply scale (log2 domain) and the causal / length mask,
-//    keep the running max m and sum l, rescale the row of O in TMEM when m
-//    grows, and write P = 2^(s - m) as bf16 into shared memory in the swizzled
-//    K-major layout the MMA reads.
+//    keep a reference max m and the sum l, and write P = 2^(s - m) as bf16
+//    into shared memory in the swizzled K-major layout the MMA reads. m moves
+//    (and the row of O in TMEM is rescaled) only when the row's max exceeds it
+//    by more than 2^8, so most tiles skip the rescale.
 //  * The MMA of S for the next tile is issued as soon as the softmax warps have
 //    read the current S, so it overlaps their exponentials.
 // Every mbarrier wait is bounded (clock64); a timeout sets the context's
@@ -40,7 +43,7 @@ namespace {
 constexpr int D = 128;        // head dim
 constexpr int BM = 128;       // queries per CTA
 constexpr int BN = 128;       // keys per tile
-constexpr int THREADS = 160;  // 4 softmax warps + 1 load/MMA warp
+constexpr int THREADS = 192;  // 4 softmax warps + MMA warp + TMA warp
 constexpr int TILE_BYTES = BM * D * 2;  // 32 KB: two 64-column slabs of [128 rows x 128 B]
 constexpr int SLAB = 128 * 128;         // bytes of one slab
 constexpr int OFF_Q = 0;
@@ -50,6 +53,9 @@ constexpr int OFF_P = OFF_V + 2 * TILE_BYTES;   // P = hi + lo, two bf16 tiles
 constexpr int SMEM_BYTES = OFF_P + 2 * TILE_BYTES;  // 224 KB
 constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;   // + alignment slack
 constexpr uint32_t TMEM_COLS = 256;
+// O is rescaled only when a row's running max grows by more than this (log2
+// units): P then stays below 2^8, exact in f32 and representable in bf16.
+constexpr float RESCALE_THRESHOLD = 8.f;
 
 struct FlashArgs {
   uint16_t *o;
@@ -59,13 +65,17 @@ struct FlashArgs {
   float scale_log2;
 };
 
+struct Bars {
+  uint64_t q, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full, s_free, p_full, o_done;
+};
+
 template <bool CAUSAL>
 __global__ void __launch_bounds__(THREADS, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                      const __grid_constant__ CUtensorMap tv, const FlashArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  __shared__ __align__(8) uint64_t bar_q, kv_full[2], kv_empty[2], s_full, s_free, p_full, o_done;
+  __shared__ __align__(8) Bars bars;
   __shared__ uint32_t tmem_base_s;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -82,15 +92,17 @@ __global__ void __launch_bounds__(THREADS, 1)
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (threadIdx.x == 32) {
-    mbar_init(&bar_q, 1);
+    mbar_init(&bars.q, 1);
     for (int i = 0; i < 2; i++) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&bars.k_full[i], 1);
+      mbar_init(&bars.k_empty[i], 1);
+      mbar_init(&bars.v_full[i], 1);
+      mbar_init(&bars.v_empty[i], 1);
     }
-    mbar_init(&s_full, 1);
-    mbar_init(&s_free, 4);
-    mbar_init(&p_full, 4);
-    mbar_init(&o_done, 1);
+    mbar_init(&bars.s_full, 1);
+    mbar_init(&bars.s_free, 4);
+    mbar_init(&bars.p_full, 4);
+    mbar_init(&bars.o_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   tc_fence_before();
@@ -99,26 +111,40 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem = tmem_base_s;
   const uint32_t tS = tmem, tO = tmem + BN;
 
-  if (warp == 4) {
-    // ---------------- loads and MMA issue (one thread)
+  if (warp == 5) {
+    // ---------------- TMA producer: Q once, then K and V of each key tile into
+    // their own double-buffered rings. K(j) waits only for S(j-2), V(j) for
+    // PV(j-2), so K tiles run ahead of the P.V products.
+    if (lane == 0) {
+      mbar_expect_tx(&bars.q, TILE_BYTES);
+      tma_load_4d(sm + OFF_Q, &tq, 0, h, q0, b, &bars.q);
+      tma_load_4d(sm + OFF_Q + SLAB, &tq, 64, h, q0, b, &bars.q);
+      for (int j = 0; j < n_kv; j++) {
+        const int st = j & 1;
+        const uint32_t ph = ((j >> 1) - 1) & 1;
+        uint8_t *k = sm + OFF_K + st * TILE_BYTES, *v = sm + OFF_V + st * TILE_BYTES;
+        if (j >= 2) wait_or_flag(&bars.k_empty[st], ph, a.err);
+        mbar_expect_tx(&bars.k_full[st], TILE_BYTES);
+        tma_load_4d(k, &tk, 0, hk, j * BN, b, &bars.k_full[st]);
+        tma_load_4d(k + SLAB, &tk, 64, hk, j * BN, b, &bars.k_full[st]);
+        if (j >= 2) wait_or_flag(&bars.v_empty[st], ph, a.err);
+        mbar_expect_tx(&bars.v_full[st], TILE_BYTES);
+        tma_load_4d(v, &tv, 0, hk, j * BN, b, &bars.v_full[st]);
+        tma_load_4d(v + SLAB, &tv, 64, hk, j * BN, b, &bars.v_full[st]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 4) {
+    // ---------------- MMA issue (one thread): S(j) then PV(j-1)
     if (lane == 0) {
       const uint32_t sQ = smem_u32(sm + OFF_Q), sP = smem_u32(sm + OFF_P);
-      mbar_expect_tx(&bar_q, TILE_BYTES);
-      tma_load_4d(sm + OFF_Q, &tq, 0, h, q0, b, &bar_q);
-      tma_load_4d(sm + OFF_Q + SLAB, &tq, 64, h, q0, b, &bar_q);
-      auto load_kv = [&](int j, int st) {
-        mbar_expect_tx(&kv_full[st], 2 * TILE_BYTES);
-        uint8_t *k = sm + OFF_K + st * TILE_BYTES, *v = sm + OFF_V + st * TILE_BYTES;
-        tma_load_4d(k, &tk, 0, hk, j * BN, b, &kv_full[st]);
-        tma_load_4d(k + SLAB, &tk, 64, hk, j * BN, b, &kv_full[st]);
-        tma_load_4d(v, &tv, 0, hk, j * BN, b, &kv_full[st]);
-        tma_load_4d(v + SLAB, &tv, 64, hk, j * BN, b, &kv_full[st]);
-      };
-      for (int j = 0; j < min(2, n_kv); j++) load_kv(j, j);
-      wait_or_flag(&bar_q, 0, a.err);
       constexpr uint32_t ID_QK = idesc_bf16(BM, BN, false), ID_PV = idesc_bf16(BM, D, true);
+      wait_or_flag(&bars.q, 0, a.err);
       auto issue_pv = [&](int j) {
         const int st = j & 1;
+        wait_or_flag(&bars.p_full, j & 1, a.err);
+        wait_or_flag(&bars.v_full[st], (j >> 1) & 1, a.err);
+        tc_fence_after();
         const uint32_t sV = smem_u32(sm + OFF_V + st * TILE_BYTES);
         // O += P_hi V + P_lo V: the K dimension runs over the keys twice
 #pragma unroll
@@ -131,13 +157,13 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint64_t bd = sw128_desc(sV + tk * 2048, SLAB, 1024);
           umma_bf16(tO, ad, bd, ID_PV, (j > 0 || t > 0) ? 1u : 0u);
         }
-        umma_commit(&o_done);
-        umma_commit(&kv_empty[st]);
+        umma_commit(&bars.o_done);
+        umma_commit(&bars.v_empty[st]);
       };
       for (int j = 0; j < n_kv; j++) {
         const int st = j & 1;
-        wait_or_flag(&kv_full[st], (j >> 1) & 1, a.err);
-        if (j > 0) wait_or_flag(&s_free, (j - 1) & 1, a.err);
+        wait_or_flag(&bars.k_full[st], (j >> 1) & 1, a.err);
+        if (j > 0) wait_or_flag(&bars.s_free, (j - 1) & 1, a.err);
         tc_fence_after();
         const uint32_t sK = smem_u32(sm + OFF_K + st * TILE_BYTES);
 #pragma unroll
@@ -145,20 +171,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t off = (t >> 2) * SLAB + (t & 3) * 32;
           umma_bf16(tS, sw128_desc(sQ + off, 16, 1024), sw128_desc(sK + off, 16, 1024), ID_QK, t > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full);
-        if (j > 0) {
-          wait_or_flag(&p_full, (j - 1) & 1, a.err);
-          tc_fence_after();
-          issue_pv(j - 1);
-          if (j + 1 < n_kv) {
-            // stage of tile j-1 is free once its PV has completed
-            wait_or_flag(&kv_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, a.err);
-            load_kv(j + 1, (j + 1) & 1);
-          }
-        }
+        umma_commit(&bars.s_full);
+        umma_commit(&bars.k_empty[st]);
+        if (j > 0) issue_pv(j - 1);
       }
-      wait_or_flag(&p_full, (n_kv - 1) & 1, a.err);
-      tc_fence_after();
       issue_pv(n_kv - 1);
     }
     __syncwarp();
@@ -168,9 +184,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int row = q0 + r;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     uint8_t *prow = sm + OFF_P + r * 128;
+    const int lim = CAUSAL ? min(a.S - 1, row) : a.S - 1;  // last visible key
+    // m: the reference max of the row (log2 domain), P = 2^(s - m) <= 2^8
     float m = -INFINITY, l = 0.f;
     for (int j = 0; j < n_kv; j++) {
-      wait_or_flag(&s_full, j & 1, a.err);
+      wait_or_flag(&bars.s_full, j & 1, a.err);
       tc_fence_after();
       float s[BN];
 #pragma unroll
@@ -178,24 +196,31 @@ __global__ void __launch_bounds__(THREADS, 1)
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free);
+      if (lane == 0) mbar_arrive(&bars.s_free);
 
       const int k0 = j * BN;
-      const int lim = CAUSAL ? min(a.S - 1, row) : a.S - 1;  // last visible key
       float mx = -INFINITY;
+      if (k0 + BN - 1 <= lim) {
 #pragma unroll
-      for (int c = 0; c < BN; c++) {
-        const float v = (k0 + c <= lim) ? s[c] * a.scale_log2 : -INFINITY;
-        s[c] = v;
-        mx = fmaxf(mx, v);
+        for (int c = 0; c < BN; c++) mx = fmaxf(mx, s[c]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < BN; c++) {
+          s[c] = (k0 + c <= lim) ? s[c] : -INFINITY;
+          mx = fmaxf(mx, s[c]);
+        }
       }
-      const float m_new = fmaxf(m, mx);
+      mx *= a.scale_log2;
+      // move the reference max only when the row's max outgrows it by more
+      // than the threshold (or the row had no visible key yet)
+      const bool grow = mx > m + RESCALE_THRESHOLD;
+      const float m_new = grow ? mx : m;
       const float mb = m_new == -INFINITY ? 0.f : m_new;  // rows with no visible key yet
-      const float alpha = ex2(m - mb);
+      const float alpha = grow ? ex2(m - mb) : 1.f;
       float sum = 0.f;
 #pragma unroll
       for (int c = 0; c < BN; c++) {
-        const float p = ex2(s[c] - mb);
+        const float p = ex2(fmaf(s[c], a.scale_log2, -mb));
         s[c] = p;
         sum += p;
       }
@@ -203,10 +228,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       m = m_new;
 
       if (j > 0) {
-        // O holds the tiles before j: wait for the last P.V, then rescale
-        wait_or_flag(&o_done, (j - 1) & 1, a.err);
+        // O holds the tiles before j: wait for the last P.V (it still reads
+        // the P buffer), then rescale the rows whose reference max moved
+        wait_or_flag(&bars.o_done, (j - 1) & 1, a.err);
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll
           for (int c = 0; c < D / 32; c++) {
             float o[32];
@@ -239,10 +265,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full);
+      if (lane == 0) mbar_arrive(&bars.p_full);
     }
     // ---------------- epilogue: O / l (bf16) and lse (natural log)
-    wait_or_flag(&o_done, (n_kv - 1) & 1, a.err);
+    wait_or_flag(&bars.o_done, (n_kv - 1) & 1, a.err);
     tc_fence_after();
     const float inv = l > 0.f ? 1.f / l : 0.f;
     const bool live = row < a.S;
@@ -296,11 +322,12 @@ EncodeTiledFn encode_fn(vxb_ctx *ctx) {
   return fn;
 }
 
-// [B, S, heads, 128] bf16 -> 4-D map (d, head, s, b), box (64, 1, 128, 1)
-int make_map(vxb_ctx *ctx, EncodeTiledFn fn, CUtensorMap *map, const void *base, int B, int S, int heads) {
+// [B, S, heads, 128] bf16 -> 4-D map (d, head, s, b), box (64, 1, box_rows, 1)
+int make_map(vxb_ctx *ctx, EncodeTiledFn fn, CUtensorMap *map, const void *base, int B, int S, int heads,
+             int box_rows) {
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)heads, (cuuint64_t)S, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)heads * D * 2, (cuuint64_t)S * heads * D * 2};
-  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t box[4] = {64, 1, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -341,9 +368,9 @@ VXB_API int vxb_flash_fwd(vxb_ctx *ctx, const uint16_t *d_q, const uint16_t *d_k
   EncodeTiledFn fn = encode_fn(ctx);
   if (!fn) return VXB_ECUDA;
   CUtensorMap mq, mk, mv;
-  if (int rc = make_map(ctx, fn, &mq, d_q, B, S, H)) return rc;
-  if (int rc = make_map(ctx, fn, &mk, d_k, B, S, Hkv)) return rc;
-  if (int rc = make_map(ctx, fn, &mv, d_v, B, S, Hkv)) return rc;
+  if (int rc = make_map(ctx, fn, &mq, d_q, B, S, H, BM)) return rc;
+  if (int rc = make_map(ctx, fn, &mk, d_k, B, S, Hkv, BN)) return rc;
+  if (int rc = make_map(ctx, fn, &mv, d_v, B, S, Hkv, BN)) return rc;
   FlashArgs a;
   a.o = d_o;
   a.lse = d_lse;
