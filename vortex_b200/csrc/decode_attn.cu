@@ -117,6 +117,11 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q4 = lane & 3;
   const int i = blockIdx.x / a.Hkv, h = blockIdx.x % a.Hkv, split = blockIdx.y;
+  // programmatic dependent launch: q, the lengths, block tables and pages
+  // come from earlier kernels; once they are complete the next kernel may
+  // launch (and prefetch its weights) while this one runs
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
   const int slot = a.slots ? a.slots[i] : a.slots_inline[i];
   const int len = slot >= 0 ? a.lens[slot] : 0;
   const int t0 = split * a.tps;
@@ -407,8 +412,17 @@ int launch_t(vxb_ctx *ctx, const DecodeArgs &a, cudaStream_t st) {
     VXB_CUDA_TRY(ctx, cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     configured[ctx->device & 63] = true;
   }
-  dim3 grid(a.n * a.Hkv, a.splits);
-  kfn<<<grid, THREADS, smem, st>>>(a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.n * a.Hkv, a.splits);
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  VXB_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, kfn, a));
   return launch_check(ctx, "decode_attn_kernel");
 }
 

@@ -65,7 +65,7 @@ struct vxb_decoder {
   vxb_kv *kv = nullptr;
   // activations sized for max_batch
   float *x = nullptr, *qkv = nullptr, *gu = nullptr, *logits = nullptr;
-  uint16_t *h = nullptr, *q = nullptr, *kvnew = nullptr, *attn = nullptr, *act = nullptr;
+  uint16_t *h = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
   int32_t *d_tokens = nullptr, *d_next = nullptr, *d_slots = nullptr;
   KVPlace *d_places = nullptr;  // [n_layers][max_batch]
   float *attn_ws = nullptr;
@@ -226,7 +226,6 @@ int decoder_create(vxb_ctx *ctx, const vxb_decoder_config *cfg, vxb_comm *comm, 
   if (!rc) rc = dalloc_t(d, &d->logits, (size_t)B * d->vocab);
   if (!rc) rc = dalloc_t(d, &d->h, (size_t)B * (c.dim > c.ffn_dim ? c.dim : c.ffn_dim));
   if (!rc) rc = dalloc_t(d, &d->q, (size_t)B * d->qdim);
-  if (!rc) rc = dalloc_t(d, &d->kvnew, (size_t)B * 2 * d->kvdim);
   if (!rc) rc = dalloc_t(d, &d->attn, (size_t)B * d->qdim);
   if (!rc) rc = dalloc_t(d, &d->act, (size_t)B * d->ffn);
   if (!rc && tp > 1) rc = dalloc_t(d, &d->d_keys, (size_t)B);
@@ -477,12 +476,9 @@ int record_step(vxb_decoder *d, int B) {
     auto &L = d->layers[l];
     rc = rmsnorm_launch(ctx, d->x, L.ln1_w, L.ln1_b, B, c.dim, eps, d->h, st);
     if (!rc) rc = gemv_launch(ctx, fmt, L.wqkv, d->qkv_n, c.dim, d->h, B, VXB_F32, d->qkv, nullptr, st, nullptr);
-    if (!rc) rc = rope_launch(ctx, d->qkv, B, d->qdim, d->kvdim, d->d_places, d->rope_div, d->q, d->kvnew,
-                              d->kvnew + (size_t)c.max_batch * d->kvdim, st, d->rank * d->qdim / 2,
-                              d->rank * d->kvdim / 2);
     if (!rc)
-      rc = kv_append_launch(d->kv, l, B, d->d_places + (size_t)l * c.max_batch, d->kvnew,
-                            d->kvnew + (size_t)c.max_batch * d->kvdim, st);
+      rc = rope_kv_launch(ctx, d->kv, l, d->qkv, B, d->qdim, d->kvdim, hd, d->d_places + (size_t)l * c.max_batch,
+                          d->rope_div, d->q, nullptr, nullptr, d->rank * d->qdim / 2, d->rank * d->kvdim / 2, st);
     if (!rc)
       rc = decode_attn_launch(d->kv, l, B, d->d_slots, nullptr, d->q, d->hq, scale, d->attn, nullptr, ap, d->attn_ws, st);
     // row-parallel Wo: rank 0 adds the residual, the partials are summed over ranks
@@ -687,9 +683,8 @@ VXB_API int vxb_decoder_prefill(vxb_decoder *d, int64_t seq_id, const int32_t *h
     rc = rmsnorm_launch(ctx, P.x, L.ln1_w, L.ln1_b, n, c.dim, eps, P.h, st);
     if (!rc) rc = gemm_q_launch(ctx, fmt, L.wqkv, d->qkv_n, c.dim, P.h, n, VXB_F32, P.qkv, nullptr, scratch, st);
     if (!rc)
-      rc = rope_launch(ctx, P.qkv, n, d->qdim, d->kvdim, P.places + (size_t)l * n, d->rope_div, P.q, P.k, P.v, st,
-                       d->rank * d->qdim / 2, d->rank * d->kvdim / 2);
-    if (!rc) rc = kv_append_launch(d->kv, l, n, P.places + (size_t)l * n, P.k, P.v, st);
+      rc = rope_kv_launch(ctx, d->kv, l, P.qkv, n, d->qdim, d->kvdim, 128, P.places + (size_t)l * n, d->rope_div, P.q,
+                          P.k, P.v, d->rank * d->qdim / 2, d->rank * d->kvdim / 2, st);
     if (!rc)
       rc = vxb_flash_fwd(ctx, P.q, P.k, P.v, 1, d->hq, d->hkv, n, 128, scale, 1, P.attn, P.lse, st);
     if (!rc)

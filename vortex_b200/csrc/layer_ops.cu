@@ -7,6 +7,10 @@
 //   embed        : token embedding row -> f32 residual stream
 //   argmax       : greedy next token, first index of the maximum (1163-1177)
 // Accumulation is f32; the GEMV inputs are rounded once to bf16.
+// Every kernel is launched with programmatic stream serialization: it waits
+// for its predecessor to complete before reading anything that kernel
+// produced, then lets the next kernel launch, so launch latency and the next
+// GEMV's weight prefetch overlap the small kernel's own work.
 #include <cuda_bf16.h>
 
 #include "layer_ops.h"
@@ -25,53 +29,153 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
   return warp_sum(t);
 }
 
-__global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w, const float *__restrict__ b,
-                               int n, float eps, uint16_t *__restrict__ out) {
+// One CTA (512 threads) per row. Rows whose length is a multiple of 4 and at
+// most 8192 are read once with 16-byte loads into registers (w and b are
+// requested before the wait on the producing kernel), so the kernel costs one
+// memory round trip and one block reduction.
+constexpr int NORM_THREADS = 512;
+constexpr int NORM_VEC = 4;  // float4 per thread
+
+__global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w,
+                                                               const float *__restrict__ b, int n, float eps,
+                                                               uint16_t *__restrict__ out) {
   __shared__ float red[32];
+  const float *xr = x + (size_t)blockIdx.x * n;
+  uint16_t *o = out + (size_t)blockIdx.x * n;
+  const int nv = n >> 2;
+  if ((n & 3) == 0 && nv <= NORM_VEC * NORM_THREADS) {
+    const float4 *x4 = reinterpret_cast<const float4 *>(xr);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w), *b4 = reinterpret_cast<const float4 *>(b);
+    float4 xv[NORM_VEC], wv[NORM_VEC], bv[NORM_VEC];
+#pragma unroll
+    for (int u = 0; u < NORM_VEC; u++) {
+      const int i = threadIdx.x + u * NORM_THREADS;
+      if (i < nv) {
+        wv[u] = __ldg(w4 + i);
+        bv[u] = __ldg(b4 + i);
+      }
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < NORM_VEC; u++) {
+      const int i = threadIdx.x + u * NORM_THREADS;
+      if (i < nv) xv[u] = x4[i];
+    }
+#pragma unroll
+    for (int u = 0; u < NORM_VEC; u++) {
+      const int i = threadIdx.x + u * NORM_THREADS;
+      if (i < nv) {
+        ss = fmaf(xv[u].x, xv[u].x, ss);
+        ss = fmaf(xv[u].y, xv[u].y, ss);
+        ss = fmaf(xv[u].z, xv[u].z, ss);
+        ss = fmaf(xv[u].w, xv[u].w, ss);
+      }
+    }
+    ss = block_sum(ss, red);
+    const float inv = 1.0f / sqrtf(ss / (float)n + eps);
+#pragma unroll
+    for (int u = 0; u < NORM_VEC; u++) {
+      const int i = threadIdx.x + u * NORM_THREADS;
+      if (i < nv) {
+        uint2 r;
+        r.x = (uint32_t)f32_to_bf16_bits(xv[u].x * inv * wv[u].x + bv[u].x) |
+              ((uint32_t)f32_to_bf16_bits(xv[u].y * inv * wv[u].y + bv[u].y) << 16);
+        r.y = (uint32_t)f32_to_bf16_bits(xv[u].z * inv * wv[u].z + bv[u].z) |
+              ((uint32_t)f32_to_bf16_bits(xv[u].w * inv * wv[u].w + bv[u].w) << 16);
+        *reinterpret_cast<uint2 *>(o + 4 * i) = r;
+      }
+    }
+    return;
+  }
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
-  const float *xr = x + (size_t)blockIdx.x * n;
   float ss = 0.f;
   for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
   ss = block_sum(ss, red);
   const float inv = 1.0f / sqrtf(ss / (float)n + eps);
-  uint16_t *o = out + (size_t)blockIdx.x * n;
   for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = f32_to_bf16_bits(xr[i] * inv * w[i] + b[i]);
 }
 
-// qkv: f32 [B, dim + 2*kvdim] (q | k | v); positions from the KV placements
-// of layer 0 of this step. Writes q (bf16 [B, dim]), the new keys at
-// k_out [B, kvdim] and the new values at v_out [B, kvdim] (bf16).
-// q_pair0 / k_pair0: index of the first rotation pair of this q / k slice in
-// the full vectors (tensor-parallel shards hold a slice of the heads)
-__global__ void rope_kernel(const float *__restrict__ qkv, int dim, int kvdim, const KVPlace *__restrict__ places,
-                            const double *__restrict__ rope_div, uint16_t *__restrict__ q_out,
-                            uint16_t *__restrict__ k_out, uint16_t *__restrict__ v_out, int q_pair0, int k_pair0) {
+// RoPE of the new token(s) fused with the KV-cache append. One CTA per
+// (row, head slot), hd/2 threads (one rotation pair each): slots [0, hq)
+// rotate query heads into q_out (bf16 [rows, hq*hd]); [hq, hq + hkv) rotate
+// key heads and [hq + hkv, hq + 2*hkv) round value heads to bf16, both
+// written into the paged cache at the row's place (bf16, or int8 with the
+// per-(token, head) absmax scale of append_token) and, when k_lin / v_lin
+// are given, into [rows, hkv*hd] buffers. The rotation angle is
+// pos / rope_div[pair] in f64 (pairs numbered from q_pair0 / k_pair0 for a
+// tensor-parallel slice of the heads); the rotation itself is f32.
+struct RopeKVArgs {
+  const float *qkv;  // f32 [rows, qdim + 2*kvdim] = (q | k | v)
+  const KVPlace *places;
+  const double *rope_div;
+  uint16_t *q_out, *k_lin, *v_lin;
+  int qdim, kvdim, hd, hq, hkv, q_pair0, k_pair0;
+  // cache (pool_k null: no cache write)
+  int layer, bs, max_seqs, mbps, is_int8;
+  void *pool_k, *pool_v;
+  float *scale_k, *scale_v;
+  int32_t *tables, *lens;
+};
+
+__global__ void rope_kv_kernel(const RopeKVArgs a) {
+  __shared__ double red[32];
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
-  const int b = blockIdx.x;
-  const double pos = (double)places[b].pos;
-  const float *row = qkv + (size_t)b * (dim + 2 * kvdim);
-  uint16_t *qo = q_out + (size_t)b * dim;
-  uint16_t *ko = k_out + (size_t)b * kvdim;
-  uint16_t *vo = v_out + (size_t)b * kvdim;
-  const int npq = dim / 2, npk = kvdim / 2;
-  for (int p = threadIdx.x; p < npq + npk; p += blockDim.x) {
-    const bool isk = p >= npq;
-    const int pi = isk ? p - npq : p;
-    // theta in f64 (pos / divisor), then sin/cos
+  const int r = blockIdx.x, slot = blockIdx.y, t = threadIdx.x;
+  const KVPlace p = a.places[r];
+  const int kind = slot < a.hq ? 0 : (slot < a.hq + a.hkv ? 1 : 2);  // q, k, v
+  const int h = kind == 0 ? slot : (kind == 1 ? slot - a.hq : slot - a.hq - a.hkv);
+  const float *row = a.qkv + (size_t)r * (a.qdim + 2 * a.kvdim);
+  const float2 xin =
+      *reinterpret_cast<const float2 *>(row + (kind == 0 ? 0 : (kind == 1 ? a.qdim : a.qdim + a.kvdim)) + h * a.hd + 2 * t);
+  float y0 = xin.x, y1 = xin.y;
+  if (kind < 2) {
+    const int pi = h * (a.hd / 2) + t;
     double s, c;
-    sincos(pos / rope_div[pi + (isk ? k_pair0 : q_pair0)], &s, &c);
+    sincos((double)p.pos / a.rope_div[pi + (kind ? a.k_pair0 : a.q_pair0)], &s, &c);
     const float cf = (float)c, sf = (float)s;
-    const float *src = row + (isk ? dim : 0) + 2 * pi;
-    const float x0 = src[0], x1 = src[1];
-    const float y0 = x0 * cf - x1 * sf, y1 = x0 * sf + x1 * cf;
-    uint16_t *dst = (isk ? ko : qo) + 2 * pi;
-    dst[0] = f32_to_bf16_bits(y0);
-    dst[1] = f32_to_bf16_bits(y1);
+    const float x0 = xin.x, x1 = xin.y;
+    y0 = x0 * cf - x1 * sf;
+    y1 = x0 * sf + x1 * cf;
   }
-  const float *vsrc = row + dim + kvdim;
-  for (int i = threadIdx.x; i < kvdim; i += blockDim.x) vo[i] = f32_to_bf16_bits(vsrc[i]);
+  const uint32_t packed = (uint32_t)f32_to_bf16_bits(y0) | ((uint32_t)f32_to_bf16_bits(y1) << 16);
+  if (kind == 0) {
+    *reinterpret_cast<uint32_t *>(a.q_out + (size_t)r * a.qdim + h * a.hd + 2 * t) = packed;
+    return;
+  }
+  uint16_t *lin = kind == 1 ? a.k_lin : a.v_lin;
+  if (lin) *reinterpret_cast<uint32_t *>(lin + (size_t)r * a.kvdim + h * a.hd + 2 * t) = packed;
+  if (!a.pool_k) return;
+  const size_t tok = ((size_t)p.block * a.hkv + h) * a.bs + p.offset;
+  if (!a.is_int8) {
+    uint16_t *pool = reinterpret_cast<uint16_t *>(kind == 1 ? a.pool_k : a.pool_v);
+    *reinterpret_cast<uint32_t *>(pool + tok * a.hd + 2 * t) = packed;
+  } else {
+    // absmax of the head's bf16 values in f64, scale absmax/127 (1 when all
+    // zero), codes round-half-away(v / scale) clamped to [-128, 127]
+    const double v0 = (double)bf16_bits_to_f32(packed & 0xFFFFu), v1 = (double)bf16_bits_to_f32(packed >> 16);
+    double m = fmax(fabs(v0), fabs(v1));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const int warp = t >> 5, nw = (blockDim.x + 31) >> 5;
+    if ((t & 31) == 0) red[warp] = m;
+    __syncthreads();
+    for (int i = 0; i < nw; i++) m = fmax(m, red[i]);
+    const double scale = m == 0.0 ? 1.0 : m / 127.0;
+    const double q0 = round(v0 / scale), q1 = round(v1 / scale);
+    const int8_t c0 = (int8_t)(isnan(q0) ? 0.0 : fmin(fmax(q0, -128.0), 127.0));
+    const int8_t c1 = (int8_t)(isnan(q1) ? 0.0 : fmin(fmax(q1, -128.0), 127.0));
+    int8_t *pool = reinterpret_cast<int8_t *>(kind == 1 ? a.pool_k : a.pool_v);
+    *reinterpret_cast<uint16_t *>(pool + tok * a.hd + 2 * t) = (uint16_t)((uint8_t)c0 | ((uint16_t)(uint8_t)c1 << 8));
+    if (t == 0) (kind == 1 ? a.scale_k : a.scale_v)[tok] = (float)scale;
+  }
+  if (kind == 1 && h == 0 && t == 0) {
+    if (p.offset == 0) a.tables[((size_t)a.layer * a.max_seqs + p.slot) * a.mbps + p.pos / a.bs] = p.block;
+    atomicMax(a.lens + (size_t)a.layer * a.max_seqs + p.slot, p.pos + 1);
+  }
 }
 
 // gu: f32 [B, 2*ffn] = (W1 x | W3 x); act = bf16(silu(g) * u)
@@ -95,7 +199,50 @@ __global__ void embed_kernel(const uint16_t *__restrict__ emb, const int32_t *__
   int t = tokens[b];
   t = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
   const uint16_t *e = emb + (size_t)t * dim;
-  for (int i = threadIdx.x; i < dim; i += blockDim.x) x[(size_t)b * dim + i] = bf16_bits_to_f32(e[i]);
+  float *xr = x + (size_t)b * dim;
+  if ((dim & 7) == 0) {
+    for (int i = threadIdx.x; i < dim / 8; i += blockDim.x) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4 *>(e) + i);
+      float4 *o = reinterpret_cast<float4 *>(xr) + 2 * i;
+      o[0] = make_float4(bf16_bits_to_f32(v.x & 0xFFFFu), bf16_bits_to_f32(v.x >> 16), bf16_bits_to_f32(v.y & 0xFFFFu),
+                         bf16_bits_to_f32(v.y >> 16));
+      o[1] = make_float4(bf16_bits_to_f32(v.z & 0xFFFFu), bf16_bits_to_f32(v.z >> 16), bf16_bits_to_f32(v.w & 0xFFFFu),
+                         bf16_bits_to_f32(v.w >> 16));
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) xr[i] = bf16_bits_to_f32(e[i]);
+}
+
+// Rows whose length is a multiple of 4 are scanned with 16-byte loads, eight
+// per thread in flight; indices seen by one thread ascend, so the first
+// maximum wins by the (value, index) comparison below.
+template <typename Visit>
+__device__ __forceinline__ void scan_row(const float *__restrict__ l, int vocab, Visit visit) {
+  if ((vocab & 3) == 0) {
+    const float4 *l4 = reinterpret_cast<const float4 *>(l);
+    const int nv = vocab >> 2;
+    for (int base = threadIdx.x; base < nv; base += 8 * blockDim.x) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int i = base + u * blockDim.x;
+        if (i < nv) v[u] = l4[i];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int i = base + u * blockDim.x;
+        if (i < nv) {
+          visit(v[u].x, 4 * i);
+          visit(v[u].y, 4 * i + 1);
+          visit(v[u].z, 4 * i + 2);
+          visit(v[u].w, 4 * i + 3);
+        }
+      }
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) visit(l[i], i);
 }
 
 __global__ void argmax_kernel(const float *__restrict__ logits, int vocab, int32_t *__restrict__ out) {
@@ -106,13 +253,12 @@ __global__ void argmax_kernel(const float *__restrict__ logits, int vocab, int32
   const float *l = logits + (size_t)blockIdx.x * vocab;
   float best = -INFINITY;
   int bi = 0x7FFFFFFF;
-  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
-    const float v = l[i];
+  scan_row(l, vocab, [&](float v, int i) {
     if (v > best || (v == best && i < bi)) {
       best = v;
       bi = i;
     }
-  }
+  });
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, best, o);
@@ -188,7 +334,7 @@ __global__ void argmax_key_kernel(const float *__restrict__ logits, int vocab, i
   asm volatile("griddepcontrol.launch_dependents;");
   const float *l = logits + (size_t)blockIdx.x * vocab;
   unsigned long long best = 0ull;
-  for (int i = threadIdx.x; i < vocab; i += blockDim.x) best = max(best, argmax_key(l[i], offset + i));
+  scan_row(l, vocab, [&](float v, int i) { best = max(best, argmax_key(v, offset + i)); });
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
@@ -243,14 +389,46 @@ namespace vxb {
 
 int rmsnorm_launch(vxb_ctx *ctx, const float *x, const float *w, const float *b, int rows, int n, float eps,
                    uint16_t *out, cudaStream_t st) {
-  return launch_pdl(ctx, rmsnorm_kernel, dim3(rows), dim3(512), st, "rmsnorm_kernel", x, w, b, n, eps, out);
+  return launch_pdl(ctx, rmsnorm_kernel, dim3(rows), dim3(NORM_THREADS), st, "rmsnorm_kernel", x, w, b, n, eps, out);
 }
 
-int rope_launch(vxb_ctx *ctx, const float *qkv, int rows, int dim, int kvdim, const KVPlace *places,
-                const double *rope_div, uint16_t *q_out, uint16_t *k_out, uint16_t *v_out, cudaStream_t st,
-                int q_pair0, int k_pair0) {
-  return launch_pdl(ctx, rope_kernel, dim3(rows), dim3(512), st, "rope_kernel", qkv, dim, kvdim, places, rope_div,
-                    q_out, k_out, v_out, q_pair0, k_pair0);
+int rope_kv_launch(vxb_ctx *ctx, vxb_kv *kv, int layer, const float *qkv, int rows, int qdim, int kvdim, int hd,
+                   const KVPlace *places, const double *rope_div, uint16_t *q_out, uint16_t *k_lin, uint16_t *v_lin,
+                   int q_pair0, int k_pair0, cudaStream_t st) {
+  if (rows <= 0) return VXB_OK;
+  if (hd % 64 || qdim % hd || kvdim % hd)
+    return set_error(ctx, VXB_EINVAL, "rope_kv: head_dim %d must be a multiple of 64 dividing %d and %d", hd, qdim, kvdim);
+  RopeKVArgs a = {};
+  a.qkv = qkv;
+  a.places = places;
+  a.rope_div = rope_div;
+  a.q_out = q_out;
+  a.k_lin = k_lin;
+  a.v_lin = v_lin;
+  a.qdim = qdim;
+  a.kvdim = kvdim;
+  a.hd = hd;
+  a.hq = qdim / hd;
+  a.hkv = kvdim / hd;
+  a.q_pair0 = q_pair0;
+  a.k_pair0 = k_pair0;
+  a.layer = layer;
+  if (kv) {
+    if (kv->num_kv_heads != a.hkv || kv->head_dim != hd)
+      return set_error(ctx, VXB_EINVAL, "rope_kv: cache holds %d heads of %d, projections %d of %d", kv->num_kv_heads,
+                       kv->head_dim, a.hkv, hd);
+    a.bs = kv->block_size;
+    a.max_seqs = kv->max_seqs;
+    a.mbps = kv->max_blocks_per_seq;
+    a.is_int8 = kv->dtype == VXB_I8;
+    a.pool_k = kv->pool_k;
+    a.pool_v = kv->pool_v;
+    a.scale_k = kv->scale_k;
+    a.scale_v = kv->scale_v;
+    a.tables = kv->d_tables;
+    a.lens = kv->d_lens;
+  }
+  return launch_pdl(ctx, rope_kv_kernel, dim3(rows, a.hq + 2 * a.hkv), dim3(hd / 2), st, "rope_kv_kernel", a);
 }
 
 int swiglu_launch(vxb_ctx *ctx, const float *gu, int rows, int ffn, uint16_t *act, cudaStream_t st) {

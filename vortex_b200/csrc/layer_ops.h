@@ -7,11 +7,14 @@ namespace vxb {
 
 int rmsnorm_launch(vxb_ctx *ctx, const float *x, const float *w, const float *b, int rows, int n, float eps,
                    uint16_t *out, cudaStream_t st);
+// RoPE of rows of f32 (q | k | v) projections fused with the KV-cache
+// append of layer `layer` at places[row] (kv null: no cache write): q to
+// q_out, k and v also to k_lin / v_lin when non-null (bf16 [rows, kvdim]).
 // q/k rotation pairs are numbered from q_pair0 / k_pair0 (tensor-parallel
-// slices of the heads)
-int rope_launch(vxb_ctx *ctx, const float *qkv, int rows, int dim, int kvdim, const KVPlace *places,
-                const double *rope_div, uint16_t *q_out, uint16_t *k_out, uint16_t *v_out, cudaStream_t st,
-                int q_pair0 = 0, int k_pair0 = 0);
+// slices of the heads).
+int rope_kv_launch(vxb_ctx *ctx, vxb_kv *kv, int layer, const float *qkv, int rows, int qdim, int kvdim, int hd,
+                   const KVPlace *places, const double *rope_div, uint16_t *q_out, uint16_t *k_lin, uint16_t *v_lin,
+                   int q_pair0, int k_pair0, cudaStream_t st);
 int swiglu_launch(vxb_ctx *ctx, const float *gu, int rows, int ffn, uint16_t *act, cudaStream_t st);
 int embed_launch(vxb_ctx *ctx, const uint16_t *emb, const int32_t *tokens, int rows, int dim, int vocab, float *x,
                  cudaStream_t st);
