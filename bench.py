@@ -381,9 +381,12 @@ def main():
         per_token, desc = cpu_layer_sample(1)
         cpu = {"value": 1.0 / per_token, "unit": "tokens/s", "cores": 1, "kind": "port", "sample": desc}
 
-    # our kernels per step (NCCL's own kernels not counted): embed, 10 per
-    # layer, final norm, LM-head GEMV, argmax (key + token with tp > 1)
-    launches_per_step = 1 + CFG_7B["n_layers"] * 10 + (3 if ws == 1 else 4)
+    # our kernels per step (NCCL's own kernels not counted): embedding; per
+    # layer RMSNorm, QKV GEMV, RoPE + KV append, decode attention, O GEMV,
+    # RMSNorm, gate/up GEMV, SwiGLU, down GEMV (+ two one-shot all-reduces with
+    # tp > 1); final RMSNorm, LM-head GEMV, argmax (argmax key, all-reduce,
+    # key -> token with tp > 1)
+    launches_per_step = 1 + CFG_7B["n_layers"] * (9 + (2 if ws > 1 else 0)) + (3 if ws == 1 else 5)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,

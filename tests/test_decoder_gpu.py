@@ -97,3 +97,32 @@ def test_decoder_7b_shapes_random_weights_smoke(cuda_ok):
         assert np.array_equal(nxt, np.argmax(logits, axis=1))
         toks = nxt
     dec.close()
+
+
+@pytest.mark.parametrize("fmt", ["Q4_0", "Q8_0"])
+@pytest.mark.parametrize("heads,kv_heads,kv_dtype", [(2, 2, "BF16"), (4, 2, "I8")])
+def test_decoder_single_sequence(cuda_ok, fmt, heads, kv_heads, kv_dtype):
+    """A batch of one takes the batch-1 GEMV (per-warp weight streams, bf16
+    Q4_0 operands): the same oracle gate as the batched path."""
+    from vortex_b200 import _native as N
+    from vortex_b200 import decoder as D
+    fmt_v = getattr(N, fmt)
+    fmt_o = O.GGML_Q4_0 if fmt == "Q4_0" else O.GGML_Q8_0
+    cfg = dict(vocab_size=512, dim=256, n_layers=2, n_heads=heads, n_kv_heads=kv_heads, ffn_dim=512, norm_eps=1e-5)
+    layers, emb_bits, fw, fb, out = _build(cfg, 9, fmt_o)
+    dec = D.Decoder(max_batch=2, max_seq=64, weight_fmt=fmt_v, kv_dtype=getattr(N, kv_dtype), **cfg)
+    _load(dec, layers, emb_bits, fw, fb, out)
+    orc = LlamaOracle(dict(cfg, kv_int8=kv_dtype == "I8"), layers, O.bf16_bits_to_f32_array(emb_bits), fw, fb, out,
+                      fmt_o)
+    tok = 17
+    for step in range(10):
+        nxt, logits = dec.step([5], np.array([tok]), want_logits=True)
+        ref = orc.step(5, tok)
+        nerr = norm_err(logits[0], ref)
+        assert nerr <= 1e-2, (step, nerr)
+        srt = np.sort(ref)
+        if srt[-1] - srt[-2] > 2e-2 * np.max(np.abs(ref)):
+            assert nxt[0] == argmax_first(ref), (step, nerr)
+        tok = int(nxt[0])
+    dec.free_seq(5)
+    dec.close()

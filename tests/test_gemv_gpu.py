@@ -83,8 +83,9 @@ def test_gemv_decode_sweep_shapes(Q, fmt, N, K, B):
 
 
 @pytest.mark.parametrize("fmt", [2, 8])
-def test_gemv_bf16_output(Q, fmt):
-    N, K, B = 4096, 4096, 32
+@pytest.mark.parametrize("B", [4, 32])
+def test_gemv_bf16_output(Q, fmt, B):
+    N, K = 4096, 4096
     w = _weights(N, K, 11)
     xbits, xf = _act(B, K, 12)
     tw, y = _run(Q, fmt, w, xbits, out_dtype=torch.bfloat16)

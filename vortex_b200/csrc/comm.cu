@@ -104,10 +104,10 @@ __global__ void __launch_bounds__(512) oneshot_allreduce_kernel(const ArArgs a) 
   for (size_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
     float4 v;
     const size_t e = i * 4;
-    v.x = e < a.n ? a.data[e] : 0.f;
-    v.y = e + 1 < a.n ? a.data[e + 1] : 0.f;
-    v.z = e + 2 < a.n ? a.data[e + 2] : 0.f;
-    v.w = e + 3 < a.n ? a.data[e + 3] : 0.f;
+    v.x = e < a.n ? __ldcg(a.data + e) : 0.f;
+    v.y = e + 1 < a.n ? __ldcg(a.data + e + 1) : 0.f;
+    v.z = e + 2 < a.n ? __ldcg(a.data + e + 2) : 0.f;
+    v.w = e + 3 < a.n ? __ldcg(a.data + e + 3) : 0.f;
     dst[i] = v;
   }
   __syncthreads();

@@ -117,13 +117,15 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q4 = lane & 3;
   const int i = blockIdx.x / a.Hkv, h = blockIdx.x % a.Hkv, split = blockIdx.y;
-  // programmatic dependent launch: q, the lengths, block tables and pages
-  // come from earlier kernels; once they are complete the next kernel may
-  // launch (and prefetch its weights) while this one runs
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // programmatic dependent launch: the next kernel may launch (and prefetch
+  // its weights) now; q, the lengths, block tables and pages come from earlier
+  // kernels and are read after the wait through L2 only (cp.async.cg,
+  // ld.global.cg): a kernel launched ahead can share an SM with an earlier
+  // kernel whose L1 lines predate the data
   asm volatile("griddepcontrol.launch_dependents;");
-  const int slot = a.slots ? a.slots[i] : a.slots_inline[i];
-  const int len = slot >= 0 ? a.lens[slot] : 0;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int slot = a.slots ? __ldcg(a.slots + i) : a.slots_inline[i];
+  const int len = slot >= 0 ? __ldcg(a.lens + slot) : 0;
   const int t0 = split * a.tps;
   const int t1 = min(len, t0 + a.tps);
   const int32_t *table = a.tables + (size_t)(slot >= 0 ? slot : 0) * a.mbps;
@@ -138,10 +140,10 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
     const bool v0 = g < a.G, v1 = g + 8 < a.G;
 #pragma unroll
     for (int ks = 0; ks < D / 16; ks++) {
-      qa[ks][0] = v0 ? qrow0[ks * 8 + q4] : 0u;
-      qa[ks][1] = v1 ? qrow1[ks * 8 + q4] : 0u;
-      qa[ks][2] = v0 ? qrow0[ks * 8 + 4 + q4] : 0u;
-      qa[ks][3] = v1 ? qrow1[ks * 8 + 4 + q4] : 0u;
+      qa[ks][0] = v0 ? __ldcg(qrow0 + ks * 8 + q4) : 0u;
+      qa[ks][1] = v1 ? __ldcg(qrow1 + ks * 8 + q4) : 0u;
+      qa[ks][2] = v0 ? __ldcg(qrow0 + ks * 8 + 4 + q4) : 0u;
+      qa[ks][3] = v1 ? __ldcg(qrow1 + ks * 8 + 4 + q4) : 0u;
     }
   }
 
@@ -157,7 +159,7 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
   auto prefetch = [&](int j, int stage) {
     const int p = pg0 + warp + j * WARPS;
     const int tok0 = p * PAGE;
-    const int block = table[tok0 / a.bs];
+    const int block = __ldcg(table + tok0 / a.bs);
     const int off = tok0 % a.bs;
     const size_t base = ((size_t)block * a.Hkv + h) * a.bs + off;  // token row index in pool
     uint8_t *st = wsm + stage * SM::STAGE;
@@ -185,6 +187,8 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
       }
       {
         // per-token scales: lanes 0-15 the K scales, lanes 16-31 the V scales
+        // (4-byte copies exist only in the L1-allocating form; a token's scale
+        // is written once, by its append, before any attention reads it)
         const bool isv = lane >= 16;
         const int r = lane & 15;
         cp_async4(st_s + 2 * SM::RAW + (isv ? SM::SC : 0) + r * 4, (isv ? a.sv : a.sk) + base + r,

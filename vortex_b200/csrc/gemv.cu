@@ -64,9 +64,9 @@ template <int FMT>
 struct Geo {
   static constexpr int CH = FMT == 0 ? 64 : 32;     // k per chunk
   static constexpr int BPC = CH / 32;               // 32-element blocks per chunk
-  static constexpr int SCT = 8 * BPC * 4;           // scale bytes of one tile in a record
-  static constexpr int REC = CWARPS * (512 + SCT);  // bytes of one (row group, chunk) record
-  static constexpr int STAGE = CS * REC;
+  static constexpr int SCT = 8 * BPC * 4;           // scale bytes of one (tile, chunk) unit
+  static constexpr int UNIT = 512 + SCT;            // bytes of one (tile, chunk) unit
+  static constexpr int STAGE = CWARPS * CS * UNIT;  // a 128-row group's CS chunks
   static constexpr int XSTR = CS * CH + 16;  // elements per batch row of a stage's x slice
 };
 
@@ -77,7 +77,7 @@ template <int NT>
 struct XMode {
   static constexpr bool F16 = NT == 1;
 };
-static_assert(Geo<0>::REC == 8 * (512 + 64) && Geo<1>::REC == 8 * (512 + 32), "record size");
+static_assert(Geo<0>::UNIT == 512 + 64 && Geo<1>::UNIT == 512 + 32, "unit size");
 
 struct GemvArgs {
   const uint8_t *records;
@@ -270,7 +270,7 @@ __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;"
 
 __device__ __forceinline__ void epilogue_store(const GemvArgs &a, int b, int row, float v) {
   const size_t o = (size_t)b * a.N + row;
-  if (a.resid) v += a.resid[o];
+  if (a.resid) v += __ldcg(a.resid + o);
   if (a.y_dtype == VXB_BF16)
     ((uint16_t *)a.y)[o] = f32_to_bf16_bits(v);
   else
@@ -305,19 +305,19 @@ __device__ __forceinline__ void consume_stages(const GemvArgs &a, const uint8_t 
     const int slot = it % STAGES;
     if (!mbar_wait(&full[slot], (it / STAGES) & 1)) atomicExch(a.err, 1);
     const uint8_t *st = stages + slot * STG;
-    const uint8_t *cw = st + warp * 512 + lane * 16;
-    const uint8_t *sw = st + CWARPS * 512 + warp * G::SCT + (lane >> 2) * G::BPC * 4;
+    const uint8_t *cw = st + warp * CS * G::UNIT + lane * 16;
+    const uint8_t *sw = st + warp * CS * G::UNIT + 512 + (lane >> 2) * G::BPC * 4;
     uint4 wv[CS];
     uint32_t sv[CS][G::BPC];
 #pragma unroll
     for (int j = 0; j < CS; j++) {
-      wv[j] = *reinterpret_cast<const uint4 *>(cw + j * G::REC);
+      wv[j] = *reinterpret_cast<const uint4 *>(cw + j * G::UNIT);
       if (G::BPC == 2) {
-        const uint2 t2 = *reinterpret_cast<const uint2 *>(sw + j * G::REC);
+        const uint2 t2 = *reinterpret_cast<const uint2 *>(sw + j * G::UNIT);
         sv[j][0] = t2.x;
         sv[j][G::BPC - 1] = t2.y;
       } else {
-        sv[j][0] = *reinterpret_cast<const uint32_t *>(sw + j * G::REC);
+        sv[j][0] = *reinterpret_cast<const uint32_t *>(sw + j * G::UNIT);
       }
     }
     const uint16_t *xk = XF16 ? xs + it * CS * G::CH + xlane
@@ -415,13 +415,21 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const 
     // ---------------- producer: one bulk copy of CS records per stage (+ the
     // stage's x rows for large batches)
     if (lane == 0) {
-      const uint8_t *src = a.records + ((size_t)g * a.n_chunks + c0) * G::REC;
+      // the group's 8 tiles are 8 contiguous streams of (tile, chunk) units;
+      // a stage holds CS units of each, tile-major
+      const uint8_t *src = a.records + ((size_t)g * CWARPS * a.n_chunks + c0) * G::UNIT;
+      const size_t tile_stride = (size_t)a.n_chunks * G::UNIT;
+      constexpr uint32_t TB = CS * G::UNIT;  // bytes of one tile in a stage
+      auto copy_stage = [&](uint8_t *dst, int it, uint64_t *bar) {
+#pragma unroll
+        for (int t = 0; t < CWARPS; t++) bulk_g2s(dst + t * TB, src + t * tile_stride + (size_t)it * TB, TB, bar);
+      };
       if (XF16) {
         for (int it = 0; it < n_iter; it++) {
           const int slot = it % STAGES;
           if (it >= STAGES && !mbar_wait(&empty[slot], ((it / STAGES) & 1) ^ 1)) atomicExch(a.err, 1);
           mbar_expect_tx(&full[slot], (uint32_t)G::STAGE);
-          bulk_g2s(stages + slot * STG, src + (size_t)it * G::STAGE, (uint32_t)G::STAGE, &full[slot]);
+          copy_stage(stages + slot * STG, it, &full[slot]);
         }
       } else {
         // weights of the first stages before waiting for the kernel that
@@ -429,7 +437,7 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const 
         const int pre = min(STAGES, n_iter);
         for (int it = 0; it < pre; it++) {
           mbar_expect_tx_only(&full[it], (uint32_t)G::STAGE);
-          bulk_g2s(stages + it * STG, src + (size_t)it * G::STAGE, (uint32_t)G::STAGE, &full[it]);
+          copy_stage(stages + it * STG, it, &full[it]);
         }
         asm volatile("griddepcontrol.wait;" ::: "memory");
         for (int it = 0; it < n_iter; it++) {
@@ -438,7 +446,7 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const 
           if (it >= STAGES) {
             if (!mbar_wait(&empty[slot], ((it / STAGES) & 1) ^ 1)) atomicExch(a.err, 1);
             mbar_expect_tx_only(&full[slot], (uint32_t)G::STAGE);
-            bulk_g2s(dst, src + (size_t)it * G::STAGE, (uint32_t)G::STAGE, &full[slot]);
+            copy_stage(dst, it, &full[slot]);
           }
           uint16_t *xd = reinterpret_cast<uint16_t *>(dst + G::STAGE);
           const int kst = (c0 + it * CS) * G::CH;
@@ -601,6 +609,388 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const 
     epilogue_store(a, b, row0 + r, v);
   }
   if (threadIdx.x == 0) a.counters[g] = 0u;
+}
+
+// ---------------------------------------------------------------------------
+// Batch 1: per-warp streams.
+//
+// Every warp owns one (16-row tile, k-part) and streams that contiguous run of
+// units through its own ring of shared-memory stages with bulk copies issued
+// by its lane 0; the first stages are requested before the wait for the
+// kernel that produces x, so the weights stream while that kernel finishes.
+// After the wait the warp copies its columns of x into shared memory. Q4_0 codes are decoded to exact bf16 values and multiplied with
+// the bf16 activations as they are (no conversion pass); Q8_0 codes decode to
+// f16 (one PRMT and one HSUB2 per two codes), so the warp converts its x
+// columns to f16 scaled by 2^-e (max|x| * 2^-e in [2^14, 2^15), exact). The
+// KQ warps of a CTA that share a tile add their partials through shared
+// memory in warp order; with S > 1 the S CTAs of a cluster hold the other
+// k-parts of the same tiles and add through distributed shared memory in CTA
+// order. No global scratch, deterministic sums.
+constexpr int SW_WARPS = 8;
+constexpr int SW_THREADS = SW_WARPS * 32;
+constexpr int SW_MAX_RING = 4;  // stages per warp ring
+
+struct StreamArgs {
+  const uint8_t *units;  // unit (tile 0, chunk 0)
+  const uint32_t *hdr;
+  const uint16_t *x;  // bf16 [K]
+  void *y;
+  const float *resid;  // optional f32 [N] added in the epilogue
+  int *err;
+  int N, K, n_chunks, y_dtype;
+  int KQ, S;      // warps per tile inside a CTA, CTAs per tile (one cluster)
+  int ring;       // stages in each warp's ring
+  int wreg;       // shared-memory bytes of one warp (ring + x columns)
+};
+
+__device__ __forceinline__ void store_out(const StreamArgs &a, int row, float v) {
+  if (a.resid) v += __ldcg(a.resid + row);
+  if (a.y_dtype == VXB_BF16)
+    ((uint16_t *)a.y)[row] = f32_to_bf16_bits(v);
+  else
+    ((float *)a.y)[row] = v;
+}
+
+// acc[0] = rows g, acc[1] = rows g+8 of the warp's tile (batch column 0 in
+// .x of the lanes with lane % 4 == 0).
+template <int FMT, bool SUBN>
+__device__ __forceinline__ void stream_consume(const StreamArgs &a, const uint8_t *src, uint8_t *ring, uint64_t *full,
+                                               const uint16_t *xs, int n_iter, float2 (&acc)[2]) {
+  using G = Geo<FMT>;
+  constexpr uint32_t STB = CS * G::UNIT;
+  const int lane = threadIdx.x & 31;
+  acc[0] = acc[1] = make_float2(0.f, 0.f);
+  const bool live = lane < 4;  // the lanes that carry batch column 0 of the B operand
+  const uint16_t *xl = xs + (lane & 3) * 4;
+  constexpr int BLK = CS * G::BPC;  // blocks per stage
+  constexpr int GB = 4;             // blocks per group of independent accumulators
+  for (int it = 0; it < n_iter; it++) {
+    const int slot = it % a.ring;
+    if (!mbar_wait(&full[slot], (it / a.ring) & 1)) atomicExch(a.err, 1);
+    const uint8_t *st = ring + slot * STB;
+    uint4 wv[CS];
+    uint32_t sv[CS][G::BPC];
+#pragma unroll
+    for (int j = 0; j < CS; j++) {
+      wv[j] = *reinterpret_cast<const uint4 *>(st + j * G::UNIT + lane * 16);
+      const uint8_t *sp = st + j * G::UNIT + 512 + (lane >> 2) * G::BPC * 4;
+      if (G::BPC == 2) {
+        const uint2 t2 = *reinterpret_cast<const uint2 *>(sp);
+        sv[j][0] = t2.x;
+        sv[j][G::BPC - 1] = t2.y;
+      } else {
+        sv[j][0] = *reinterpret_cast<const uint32_t *>(sp);
+      }
+    }
+    // the slot's data is in registers: refill it with stage it + ring
+    __syncwarp();
+    if (lane == 0 && it + a.ring < n_iter) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_expect_tx(&full[slot], STB);
+      bulk_g2s(ring + slot * STB, src + (size_t)(it + a.ring) * STB, STB, &full[slot]);
+    }
+    const uint16_t *xk = xl + it * CS * G::CH;
+#pragma unroll
+    for (int b0 = 0; b0 < BLK; b0 += GB) {
+      float t[GB][4];
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+#pragma unroll
+        for (int gb = 0; gb < GB; gb++) {
+          const int blk = b0 + gb, j = blk / G::BPC, bb = blk % G::BPC;
+          const uint32_t *wu = reinterpret_cast<const uint32_t *>(&wv[j]);
+          uint32_t A[4];
+          uint2 bx = make_uint2(0u, 0u);
+          if (live) bx = *reinterpret_cast<const uint2 *>(xk + blk * 32 + h * 16);
+          if (FMT == 0) {
+            decode_q4_bf16(wu[bb * 2 + h], A);
+            if (h == 0)
+              mma_bf16_z(t[gb], A, bx.x, bx.y);
+            else
+              mma_bf16(t[gb], A, bx.x, bx.y);
+          } else {
+            decode_q8(wu[h * 2], wu[h * 2 + 1], A);
+            if (h == 0)
+              mma_f16_z(t[gb], A, bx.x, bx.y);
+            else
+              mma_f16(t[gb], A, bx.x, bx.y);
+          }
+        }
+      }
+#pragma unroll
+      for (int gb = 0; gb < GB; gb++) {
+        const int blk = b0 + gb, j = blk / G::BPC, bb = blk % G::BPC;
+        const float2 d = decode_scales(sv[j][bb], SUBN);
+        acc[0] = __ffma2_rn(make_float2(t[gb][0], t[gb][1]), make_float2(d.x, d.x), acc[0]);
+        acc[1] = __ffma2_rn(make_float2(t[gb][2], t[gb][3]), make_float2(d.y, d.y), acc[1]);
+      }
+    }
+  }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(SW_THREADS) gemv_stream_kernel(const StreamArgs a) {
+  using G = Geo<FMT>;
+  constexpr uint32_t STB = CS * G::UNIT;  // one stage: CS units of one tile
+  constexpr int SPAN = CS * G::CH;        // columns of one stage
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[SW_WARPS][SW_MAX_RING];
+  __shared__ float red[SW_WARPS][16];  // per-warp partials [row]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int RT = SW_WARPS / a.KQ;  // tiles per CTA
+  const int tile = blockIdx.x * RT + warp / a.KQ;
+  const int P = a.KQ * a.S;  // k-parts per tile
+  const int part = blockIdx.y * a.KQ + warp % a.KQ;
+  const int n_stages = a.n_chunks / CS;
+  const int s0 = (int)((long long)part * n_stages / P);
+  const int n_iter = (int)((long long)(part + 1) * n_stages / P) - s0;
+  uint8_t *ring = smem + (size_t)warp * a.wreg;
+  uint16_t *xs = reinterpret_cast<uint16_t *>(ring + (size_t)a.ring * STB);
+  const uint8_t *src = a.units + ((size_t)tile * a.n_chunks + (size_t)s0 * CS) * G::UNIT;
+
+  if (lane == 0) {
+    for (int i = 0; i < a.ring; i++) mbar_init(&full[warp][i], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // weights do not depend on the previous kernel: request them now
+    const int pre = min(a.ring, n_iter);
+    for (int it = 0; it < pre; it++) {
+      mbar_expect_tx(&full[warp][it], STB);
+      bulk_g2s(ring + it * STB, src + (size_t)it * STB, STB, &full[warp][it]);
+    }
+  }
+  __syncwarp();
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const bool subnormal = (__ldg(a.hdr + 1) & TILED_FLAG_SUBNORMAL_SCALES) != 0;
+
+  // ---- this warp's x columns [k0, k0 + kr): 16-byte asynchronous copies
+  // through the load/store path and L2 only (the bulk-copy queue is busy with
+  // weights), zeros past K (K and k0 are multiples of 32)
+  const int k0 = s0 * SPAN, kr = n_iter * SPAN;
+  const int kv = max(0, min(kr, a.K - k0));
+  for (int i = lane; i < kr / 8; i += 32) {
+    if (i < kv / 8)
+      cp_async16(xs + i * 8, a.x + k0 + i * 8, 16);
+    else
+      reinterpret_cast<uint4 *>(xs)[i] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncwarp();
+  int e = 0;
+  if (FMT != 0) {
+    // f16 operands: e with max|x| * 2^-e in [2^14, 2^15) (0 for all-zero or
+    // non-finite x), then x * 2^-e in place
+    unsigned m = 0;
+    const uint32_t *row = reinterpret_cast<const uint32_t *>(xs);
+    for (int i = lane; i < kr / 2; i += 32) {
+      const uint32_t v = row[i];
+      m = max(m, max(v & 0x7FFFu, (v >> 16) & 0x7FFFu));
+    }
+    m = __reduce_max_sync(0xffffffffu, m);
+    e = (m != 0 && m < 0x7F80u) ? max((int)(m >> 7), 1) - 127 - 14 : 0;
+    for (int p = lane; p < kr / 8; p += 32) {
+      uint4 *ptr = reinterpret_cast<uint4 *>(xs) + p;
+      uint4 v = *ptr;
+      uint32_t *w = reinterpret_cast<uint32_t *>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        w[j] = pack_f16x2(mul_pow2(__uint_as_float(w[j] << 16), -e), mul_pow2(__uint_as_float(w[j] & 0xFFFF0000u), -e));
+      *ptr = v;
+    }
+  }
+  __syncwarp();
+
+  float2 acc[2];
+  if (subnormal)
+    stream_consume<FMT, true>(a, src, ring, full[warp], xs, n_iter, acc);
+  else
+    stream_consume<FMT, false>(a, src, ring, full[warp], xs, n_iter, acc);
+  if ((lane & 3) == 0) {
+    red[warp][lane >> 2] = mul_pow2(acc[0].x, e);
+    red[warp][(lane >> 2) + 8] = mul_pow2(acc[1].x, e);
+  }
+  __syncthreads();
+
+  // ---- the KQ warps of each tile, in warp order
+  const int nout = RT * 16;  // outputs of this CTA: (tile, row)
+  float *cta_sum = reinterpret_cast<float *>(smem);  // the rings are free now
+  for (int i = threadIdx.x; i < nout; i += SW_THREADS) {
+    float v = 0.f;
+    for (int q = 0; q < a.KQ; q++) v += red[(i / 16) * a.KQ + q][i % 16];
+    if (a.S == 1) {
+      const int row = (blockIdx.x * RT + i / 16) * 16 + i % 16;
+      if (row < a.N) store_out(a, row, v);
+    } else {
+      cta_sum[i] = v;
+    }
+  }
+  if (a.S == 1) return;
+  // ---- the S CTAs of the cluster hold the other k-parts: each sums a slice
+  // of the outputs over the peers in CTA order; nobody exits before all reads
+  // are done
+  cluster_sync_all();
+  cg::cluster_group cl = cg::this_cluster();
+  const int per = (nout + a.S - 1) / a.S;
+  const int i1 = min(nout, ((int)blockIdx.y + 1) * per);
+  for (int i = (int)blockIdx.y * per + threadIdx.x; i < i1; i += SW_THREADS) {
+    float v = 0.f;
+    for (int ss = 0; ss < a.S; ss++) v += *cl.map_shared_rank(cta_sum + i, (unsigned)ss);
+    const int row = (blockIdx.x * RT + i / 16) * 16 + i % 16;
+    if (row < a.N) store_out(a, row, v);
+  }
+  cluster_sync_all();
+}
+
+struct StreamPlan {
+  int KQ = 0, S = 0, ring = 0, wreg = 0;
+  size_t smem = 0;
+};
+
+template <int FMT>
+int stream_resident(size_t smem, int cluster, int sms) {
+  static std::mutex mu;
+  static std::map<std::pair<size_t, int>, int> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_pair(smem, cluster);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  auto kfn = gemv_stream_kernel<FMT>;
+  int n = 0;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) == cudaSuccess) {
+    if (cluster <= 1) {
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, SW_THREADS, smem) == cudaSuccess) n = per_sm * sms;
+    } else {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1, cluster);
+      cfg.blockDim = dim3(SW_THREADS);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 1;
+      attr.val.clusterDim.y = cluster;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kfn, &cfg) == cudaSuccess) n = clusters * cluster;
+    }
+  }
+  if (n < 1) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cache[key] = n;
+  return n;
+}
+
+// Split of each tile's k range into KQ warps x S CTAs and the ring depth:
+// minimise the busiest SM's stage count (CTAs spread evenly), inflated when
+// fewer than 32 warps per SM hide the latency, plus the cost of a cluster
+// reduction (about 1.5 us, some 30 stages of an SM's work) and of each wave
+// beyond the first (its CTAs start streaming only when the first wave ends).
+StreamPlan stream_plan(const vxb_ctx *ctx, const TiledGeom &g) {
+  const int sms = ctx->num_sms > 0 ? ctx->num_sms : 148;
+  const int n_stages = g.n_chunks / CS;
+  const size_t stb = (size_t)CS * (512 + g.sc_per_tile);
+  const int span = CS * g.chunk;
+  StreamPlan best;
+  double best_cost = 1e30;
+  for (int KQ : {8, 4, 2, 1}) {
+    for (int S : {1, 2, 4, 8}) {
+      const int P = KQ * S;
+      if (P > n_stages) continue;
+      const int part_max = (n_stages + P - 1) / P;
+      const size_t xbytes = ((size_t)part_max * span * 2 + 127) / 128 * 128;
+      for (int ring = 2; ring <= SW_MAX_RING; ring++) {
+        const int rg = std::min(ring, part_max);
+        if (rg < ring && ring > 2) break;
+        const size_t wreg = ((size_t)rg * stb + xbytes + 127) / 128 * 128;
+        const size_t cta_sum = (size_t)(SW_WARPS / KQ) * 16 * 4;
+        const size_t smem = std::max((size_t)SW_WARPS * wreg, cta_sum);
+        if (smem > 200 * 1024) continue;
+        const int slots = g.fmt == VXB_Q4_0 ? stream_resident<0>(smem, S, sms) : stream_resident<1>(smem, S, sms);
+        if (slots < 1) continue;
+        const int ctas = g.n_tiles / (SW_WARPS / KQ) * S;
+        const int waves = (ctas + slots - 1) / slots;
+        const double per_sm = std::min((double)ctas / sms, (double)slots / sms);
+        const double wps = per_sm * SW_WARPS;
+        const double load = (double)((ctas + sms - 1) / sms) * SW_WARPS * part_max;
+        const double cost = load * (1.0 + std::max(0.0, (32.0 - wps) / 32.0)) + (S > 1 ? 30.0 : 0.0) +
+                            40.0 * (waves - 1) - 0.5 * rg;
+        if (cost < best_cost - 1e-9) {
+          best_cost = cost;
+          best.KQ = KQ;
+          best.S = S;
+          best.ring = rg;
+          best.wreg = (int)wreg;
+          best.smem = smem;
+        }
+      }
+    }
+  }
+  return best;
+}
+
+template <int FMT>
+int stream_launch_t(vxb_ctx *ctx, const StreamArgs &a, dim3 grid, size_t smem, cudaStream_t st, bool pdl) {
+  auto kfn = gemv_stream_kernel<FMT>;
+  static bool configured[64] = {false};
+  const int dev = ctx->device & 63;
+  if (!configured[dev]) {
+    VXB_CUDA_TRY(ctx, cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(SW_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    na++;
+  }
+  if (a.S > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = a.S;
+    attr[na].val.clusterDim.z = 1;
+    na++;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  VXB_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, kfn, a));
+  return VXB_OK;
+}
+
+// y = W x (+ resid) for one activation row through the per-warp stream kernel.
+int stream_gemv(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const uint16_t *d_x, int y_dtype, void *d_y,
+                const float *d_resid, int *d_err, cudaStream_t st, bool pdl, const char *who) {
+  const TiledGeom g = tiled_geom(fmt, N, K);
+  const StreamPlan p = stream_plan(ctx, g);
+  if (p.KQ == 0) return set_error(ctx, VXB_EINVAL, "%s: no launch plan fits N=%d K=%d", who, N, K);
+  StreamArgs a;
+  const uint8_t *base = (const uint8_t *)d_tiled;
+  a.units = base + g.codes_off;
+  a.hdr = (const uint32_t *)base;
+  a.x = d_x;
+  a.y = d_y;
+  a.resid = d_resid;
+  a.err = d_err;
+  a.N = N;
+  a.K = K;
+  a.n_chunks = g.n_chunks;
+  a.y_dtype = y_dtype;
+  a.KQ = p.KQ;
+  a.S = p.S;
+  a.ring = p.ring;
+  a.wreg = p.wreg;
+  const dim3 grid(g.n_tiles / (SW_WARPS / p.KQ), p.S);
+  return fmt == VXB_Q4_0 ? stream_launch_t<0>(ctx, a, grid, p.smem, st, pdl)
+                         : stream_launch_t<1>(ctx, a, grid, p.smem, st, pdl);
 }
 
 size_t smem_bytes_t(int fmt, int NT, int batch, int xs_stride) {
@@ -767,6 +1157,11 @@ int gemv_launch(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const 
   if (((uintptr_t)d_tiled) % 256) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q: tiled weights must be 256-byte aligned");
   if (((uintptr_t)d_x) % 16) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q: activations must be 16-byte aligned");
   if (int rc = use_device(ctx)) return rc;
+  if (batch == 1 && !plan_override) {
+    if (int rc = ws_reserve(ctx, 0, 0)) return rc;  // device error word
+    return stream_gemv(ctx, fmt, d_tiled, N, K, d_x, y_dtype, d_y, d_resid, ctx->d_err, (cudaStream_t)stream, true,
+                       "vxb_gemv_q");
+  }
   const TiledGeom g = tiled_geom(fmt, N, K);
   GemvPlan p = plan_override ? *plan_override : gemv_plan(ctx, fmt, N, K, batch);
   const int NT = (batch + 7) / 8;
@@ -894,6 +1289,10 @@ VXB_API int vxb_gemv_q_static(vxb_ctx *ctx, int fmt, const void *d_tiled, int N,
   if (int rc = use_device(ctx)) return rc;
   uint8_t *base = nullptr;
   if (int rc = static_scratch(ctx, &base)) return rc;
+  if (batch == 1)  // the per-warp stream kernel needs no scratch beyond the error word
+    return stream_gemv(ctx, fmt, d_tiled, N, K, d_x, y_dtype, d_y, nullptr,
+                       (int *)(base + kStaticPartialBytes + (size_t)kStaticCounters * 4), (cudaStream_t)stream, false,
+                       "vxb_gemv_q_static");
   GemvPlan p = gemv_plan(ctx, fmt, N, K, batch);
   p.S = std::max(1, std::min<int>(p.S, (int)(kStaticPartialBytes / per_split)));
   GemvArgs a;

@@ -7,10 +7,14 @@
 //   embed        : token embedding row -> f32 residual stream
 //   argmax       : greedy next token, first index of the maximum (1163-1177)
 // Accumulation is f32; the GEMV inputs are rounded once to bf16.
-// Every kernel is launched with programmatic stream serialization: it waits
-// for its predecessor to complete before reading anything that kernel
-// produced, then lets the next kernel launch, so launch latency and the next
-// GEMV's weight prefetch overlap the small kernel's own work.
+// Every kernel is launched with programmatic stream serialization and lets
+// the next kernel of the stream launch as soon as it starts, so a chain of
+// small kernels and GEMVs launches ahead and each GEMV prefetches its weights
+// while earlier kernels run. Each kernel waits for its predecessor to
+// complete before reading anything produced on the device, and reads such
+// data through L2 only (ld.global.cg): with kernels launched ahead, an SM's
+// L1 can still hold lines that an earlier, concurrently running kernel read
+// before a later kernel rewrote them.
 #include <cuda_bf16.h>
 
 #include "layer_ops.h"
@@ -55,13 +59,13 @@ __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(const float *__re
         bv[u] = __ldg(b4 + i);
       }
     }
-    asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     float ss = 0.f;
 #pragma unroll
     for (int u = 0; u < NORM_VEC; u++) {
       const int i = threadIdx.x + u * NORM_THREADS;
-      if (i < nv) xv[u] = x4[i];
+      if (i < nv) xv[u] = __ldcg(x4 + i);
     }
 #pragma unroll
     for (int u = 0; u < NORM_VEC; u++) {
@@ -89,13 +93,16 @@ __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(const float *__re
     }
     return;
   }
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   float ss = 0.f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = __ldcg(xr + i);
+    ss = fmaf(v, v, ss);
+  }
   ss = block_sum(ss, red);
   const float inv = 1.0f / sqrtf(ss / (float)n + eps);
-  for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = f32_to_bf16_bits(xr[i] * inv * w[i] + b[i]);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = f32_to_bf16_bits(__ldcg(xr + i) * inv * w[i] + b[i]);
 }
 
 // RoPE of the new token(s) fused with the KV-cache append. One CTA per
@@ -122,15 +129,16 @@ struct RopeKVArgs {
 
 __global__ void rope_kv_kernel(const RopeKVArgs a) {
   __shared__ double red[32];
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int r = blockIdx.x, slot = blockIdx.y, t = threadIdx.x;
-  const KVPlace p = a.places[r];
+  const int4 pv = __ldcg(reinterpret_cast<const int4 *>(a.places + r));
+  const KVPlace p = {pv.x, pv.y, pv.z, pv.w};
   const int kind = slot < a.hq ? 0 : (slot < a.hq + a.hkv ? 1 : 2);  // q, k, v
   const int h = kind == 0 ? slot : (kind == 1 ? slot - a.hq : slot - a.hq - a.hkv);
   const float *row = a.qkv + (size_t)r * (a.qdim + 2 * a.kvdim);
   const float2 xin =
-      *reinterpret_cast<const float2 *>(row + (kind == 0 ? 0 : (kind == 1 ? a.qdim : a.qdim + a.kvdim)) + h * a.hd + 2 * t);
+      __ldcg(reinterpret_cast<const float2 *>(row + (kind == 0 ? 0 : (kind == 1 ? a.qdim : a.qdim + a.kvdim)) + h * a.hd + 2 * t));
   float y0 = xin.x, y1 = xin.y;
   if (kind < 2) {
     const int pi = h * (a.hd / 2) + t;
@@ -180,12 +188,12 @@ __global__ void rope_kv_kernel(const RopeKVArgs a) {
 
 // gu: f32 [B, 2*ffn] = (W1 x | W3 x); act = bf16(silu(g) * u)
 __global__ void swiglu_kernel(const float *__restrict__ gu, int ffn, int total, uint16_t *__restrict__ act) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < total) {
     const int b = i / ffn, j = i % ffn;
-    const float g = gu[(size_t)b * 2 * ffn + j], u = gu[(size_t)b * 2 * ffn + ffn + j];
+    const float g = __ldcg(gu + (size_t)b * 2 * ffn + j), u = __ldcg(gu + (size_t)b * 2 * ffn + ffn + j);
     const float sg = g * (1.0f / (1.0f + expf(0.0f - g)));
     act[i] = f32_to_bf16_bits(sg * u);
   }
@@ -193,10 +201,10 @@ __global__ void swiglu_kernel(const float *__restrict__ gu, int ffn, int total, 
 
 __global__ void embed_kernel(const uint16_t *__restrict__ emb, const int32_t *__restrict__ tokens, int dim, int vocab,
                              float *__restrict__ x) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int b = blockIdx.x;
-  int t = tokens[b];
+  int t = __ldcg(tokens + b);
   t = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
   const uint16_t *e = emb + (size_t)t * dim;
   float *xr = x + (size_t)b * dim;
@@ -227,7 +235,7 @@ __device__ __forceinline__ void scan_row(const float *__restrict__ l, int vocab,
 #pragma unroll
       for (int u = 0; u < 8; u++) {
         const int i = base + u * blockDim.x;
-        if (i < nv) v[u] = l4[i];
+        if (i < nv) v[u] = __ldcg(l4 + i);
       }
 #pragma unroll
       for (int u = 0; u < 8; u++) {
@@ -242,14 +250,14 @@ __device__ __forceinline__ void scan_row(const float *__restrict__ l, int vocab,
     }
     return;
   }
-  for (int i = threadIdx.x; i < vocab; i += blockDim.x) visit(l[i], i);
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) visit(__ldcg(l + i), i);
 }
 
 __global__ void argmax_kernel(const float *__restrict__ logits, int vocab, int32_t *__restrict__ out) {
   __shared__ float sv[32];
   __shared__ int si[32];
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const float *l = logits + (size_t)blockIdx.x * vocab;
   float best = -INFINITY;
   int bi = 0x7FFFFFFF;
@@ -330,8 +338,8 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
 __global__ void argmax_key_kernel(const float *__restrict__ logits, int vocab, int offset,
                                   unsigned long long *__restrict__ keys) {
   __shared__ unsigned long long sk[32];
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const float *l = logits + (size_t)blockIdx.x * vocab;
   unsigned long long best = 0ull;
   scan_row(l, vocab, [&](float v, int i) { best = max(best, argmax_key(v, offset + i)); });
@@ -348,10 +356,13 @@ __global__ void argmax_key_kernel(const float *__restrict__ logits, int vocab, i
 }
 
 __global__ void key_to_token_kernel(const unsigned long long *__restrict__ keys, int rows, int32_t *__restrict__ out) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < rows) out[i] = keys[i] == 0ull ? 0 : (int32_t)(0xFFFFFFFFu - (uint32_t)(keys[i] & 0xFFFFFFFFull));
+  if (i < rows) {
+    const unsigned long long k = __ldcg(keys + i);
+    out[i] = k == 0ull ? 0 : (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+  }
 }
 
 // [tp][rows][shard] (all-gathered vocab shards) -> [rows][tp * shard]

@@ -1,13 +1,13 @@
 // Geometry of the tiled weight layout (HBM format of a quantized W [N, K]).
 //
 //   [0, 256)            header: u32 magic, u32 flags, u32 fmt, u32 N, u32 K
-//   records             one per (row group gi, k-chunk c), stored [gi][c]: a
-//                       row group is 8 sixteen-row tiles (128 rows), a chunk is
-//                       64 columns (Q4_0) or 32 columns (Q8_0). A record is
-//                         8 x 512 bytes of codes (tile 0..7), then
-//                         8 x 8*BPC u32 of scales (tile 0..7),
-//                       so the data one CTA streams per stage is contiguous.
-//   codes of one tile   32 lanes x 16 bytes. Each 16-byte lane slice holds the
+//   units               one per (16-row tile t, k-chunk c), stored [t][c], so
+//                       the whole k range of one tile is one contiguous
+//                       stream. A chunk is 64 columns (Q4_0) or 32 columns
+//                       (Q8_0). A unit is
+//                         512 bytes of codes, then
+//                         8*BPC u32 of scales (BPC = 32-column blocks per chunk).
+//   codes of a unit     32 lanes x 16 bytes. Each 16-byte lane slice holds the
 //                       lane's m16n8k16 A-operand fragments: Q4_0 -> 4 u32, one
 //                       per k16 step, nibbles (value = code + 8) at bit
 //                       positions a0@0 a2@4 a4@8 a6@12 a1@16 a3@20 a5@24 a7@28;
@@ -18,7 +18,7 @@
 //                       {2q, 2q+1, 2q+8, 2q+9} of lane q (q = lane%4) hold the
 //                       matrix columns {4q, 4q+1, 4q+2, 4q+3}, so the lane's
 //                       activation operand is 8 contiguous bytes of x.
-//   scales of one tile  per row pair i (0..7), per block of the chunk: u32 =
+//   scales of a unit    per row pair i (0..7), per block of the chunk: u32 =
 //                       f16 scale of row 16t+i (low half) | row 16t+i+8 (high).
 // Rows beyond N (up to a multiple of 128) and columns beyond K (up to a
 // multiple of TILED_STAGE_CHUNKS chunks: 256 for Q4_0, 128 for Q8_0) are
@@ -42,9 +42,9 @@
 
 struct TiledGeom {
   int fmt, N, K, N_pad, K_pad, n_tiles, n_groups, n_chunks, n_blocks, chunk, bpc;
-  size_t codes_off;    // start of the records
-  size_t sc_per_tile;  // scale bytes of one tile in one record
-  size_t record;       // bytes of one (group, chunk) record
+  size_t codes_off;    // start of the units
+  size_t sc_per_tile;  // scale bytes of one unit
+  size_t unit;         // bytes of one (tile, chunk) unit: 512 + sc_per_tile
   size_t total_bytes;
 };
 
@@ -64,17 +64,17 @@ TILED_HD static inline TiledGeom tiled_geom(int fmt, int N, int K) {
   g.n_blocks = g.K_pad / 32;
   g.codes_off = 256;
   g.sc_per_tile = (size_t)8 * g.bpc * 4;
-  g.record = 8 * (512 + g.sc_per_tile);
-  g.total_bytes = (g.codes_off + (size_t)g.n_groups * g.n_chunks * g.record + 255) / 256 * 256;
+  g.unit = 512 + g.sc_per_tile;
+  g.total_bytes = (g.codes_off + (size_t)g.n_tiles * g.n_chunks * g.unit + 255) / 256 * 256;
   return g;
 }
 
-// byte offset of the codes of tile t, chunk c (lane slices follow)
+// byte offset of the unit (codes, lane slices follow) of tile t, chunk c
 TILED_HD static inline size_t tiled_codes_at(const TiledGeom &g, int t, int c) {
-  return g.codes_off + ((size_t)(t / 8) * g.n_chunks + c) * g.record + (size_t)(t % 8) * 512;
+  return g.codes_off + ((size_t)t * g.n_chunks + c) * g.unit;
 }
 
 // byte offset of the scales of tile t, chunk c
 TILED_HD static inline size_t tiled_scales_at(const TiledGeom &g, int t, int c) {
-  return g.codes_off + ((size_t)(t / 8) * g.n_chunks + c) * g.record + 8 * 512 + (size_t)(t % 8) * g.sc_per_tile;
+  return tiled_codes_at(g, t, c) + 512;
 }
