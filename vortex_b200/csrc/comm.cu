@@ -58,16 +58,20 @@ int nccl_fail(vxb_ctx *ctx, ncclResult_t r, const char *what) {
 }
 
 // ---------------------------------------------------------------------------
-// One-shot all-reduce (sum, f32) over peer memory. CTA b owns slice b of the
-// message: it copies its slice of the input into this rank's data slot
-// (generation parity), raises flag [b][rank] to the generation in every
-// rank's buffer (system-scope release), waits (bounded) until every rank's
-// flag [b][*] in its own buffer reached the generation, then sums slice b
-// over the ranks' slots in rank order - the same order on every rank, so all
-// ranks hold identical bits. Two slots alternate: a rank can only reuse a
-// slot two calls later, after every rank has started the call in between and
-// so has finished reading it. The generation of block b is a per-block device
-// counter (the same sequence of calls on every rank, CUDA graphs included).
+// One-shot all-reduce (sum, f32) over peer memory without flags: the arrival
+// of the data is the signal. Every slot of a buffer holds the empty marker
+// (0xFFFFFFFF) between uses. CTA b owns slice b of the message: it stores its
+// slice of the input (NaNs made canonical, so no value equals the marker)
+// into slot (generation g mod 3, this rank) of every rank's buffer with
+// relaxed system-scope stores, then polls the slots (g mod 3, 0..nranks-1) of
+// its own buffer until no element holds the marker (bounded), sums them in
+// rank order - the same order on every rank, so all ranks hold identical bits
+// - and writes the marker back. A rank can run at most one call ahead of the
+// slowest rank (it needs everybody's data to finish a call), so with three
+// generations a slot is written again only after its reader has emptied it.
+// The generation of block b is a per-block device counter (the same sequence
+// of calls on every rank, CUDA graphs included). No fences on the path: one
+// NVLink write latency per call.
 struct ArArgs {
   uint8_t *peer[kArMaxRanks];
   float *data;  // in / out (in place)
@@ -76,64 +80,72 @@ struct ArArgs {
   int rank, nranks;
 };
 
-__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys_v4(void *p, uint4 v) {
+  asm volatile("st.relaxed.sys.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
 }
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ uint4 ld_relaxed_sys_v4(const void *p) {
+  uint4 v;
+  asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
   return v;
 }
 
+__device__ __forceinline__ uint32_t canon_bits(float f) { return f != f ? 0x7FC00000u : __float_as_uint(f); }
+
 __global__ void __launch_bounds__(512) oneshot_allreduce_kernel(const ArArgs a) {
+  asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int b = blockIdx.x;
-  uint8_t *mine = a.peer[a.rank];
-  uint32_t *counter = reinterpret_cast<uint32_t *>(mine + kArFlagsOff + (size_t)kArBlocks * kArMaxRanks * 4) + b;
   __shared__ uint32_t s_gen;
-  if (threadIdx.x == 0) s_gen = *counter + 1;
+  __shared__ uint8_t *s_peer[kArMaxRanks];  // indexed by rank below (no local-memory copy of the argument)
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int q = 0; q < kArMaxRanks; q++) s_peer[q] = a.peer[q];
+  }
+  __syncthreads();
+  uint8_t *mine = s_peer[a.rank];
+  uint32_t *counter = reinterpret_cast<uint32_t *>(mine + kArCountersOff) + b;
+  if (threadIdx.x == 0) s_gen = __ldcg(counter) + 1;
   __syncthreads();
   const uint32_t gen = s_gen;
-  const size_t slot = (size_t)(gen & 1) * kArMaxBytes;
-  // slice of this block, in float4 units (the message is padded to them)
+  const size_t gbase = (size_t)(gen % kArGens) * kArMaxRanks * kArSlotBytes;
+  // slice of this block, in 16-byte units (the message is padded to them)
   const size_t n4 = (a.n + 3) / 4;
   const size_t per = (n4 + kArBlocks - 1) / kArBlocks;
   const size_t i0 = (size_t)b * per, i1 = min(n4, i0 + per);
-  float4 *dst = reinterpret_cast<float4 *>(mine + slot);
   for (size_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-    float4 v;
     const size_t e = i * 4;
-    v.x = e < a.n ? __ldcg(a.data + e) : 0.f;
-    v.y = e + 1 < a.n ? __ldcg(a.data + e + 1) : 0.f;
-    v.z = e + 2 < a.n ? __ldcg(a.data + e + 2) : 0.f;
-    v.w = e + 3 < a.n ? __ldcg(a.data + e + 3) : 0.f;
-    dst[i] = v;
+    uint4 v;
+    v.x = canon_bits(e < a.n ? __ldcg(a.data + e) : 0.f);
+    v.y = canon_bits(e + 1 < a.n ? __ldcg(a.data + e + 1) : 0.f);
+    v.z = canon_bits(e + 2 < a.n ? __ldcg(a.data + e + 2) : 0.f);
+    v.w = canon_bits(e + 3 < a.n ? __ldcg(a.data + e + 3) : 0.f);
+    for (int q = 0; q < a.nranks; q++)
+      st_relaxed_sys_v4(s_peer[q] + gbase + (size_t)a.rank * kArSlotBytes + i * 16, v);
   }
-  __syncthreads();
-  if (threadIdx.x < a.nranks) {
-    __threadfence_system();
-    uint32_t *flag = reinterpret_cast<uint32_t *>(a.peer[threadIdx.x] + kArFlagsOff) + b * kArMaxRanks + a.rank;
-    st_release_sys(flag, gen);
-    // wait for rank threadIdx.x's flag in this rank's buffer
-    const uint32_t *mf = reinterpret_cast<const uint32_t *>(mine + kArFlagsOff) + b * kArMaxRanks + threadIdx.x;
-    const long long t0 = clock64();
-    while ((int)(ld_acquire_sys(mf) - gen) < 0) {
-      if (clock64() - t0 > (1ll << 31)) {
-        atomicExch(a.err, 1);
-        break;
-      }
-    }
-  }
-  __syncthreads();
   for (size_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int q = 0; q < a.nranks; q++) {
-      const float4 v = __ldcv(reinterpret_cast<const float4 *>(a.peer[q] + slot) + i);
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
+      uint8_t *slot = mine + gbase + (size_t)q * kArSlotBytes + i * 16;
+      uint4 v = ld_relaxed_sys_v4(slot);
+      const long long t0 = clock64();
+      while (v.x == kArEmpty || v.y == kArEmpty || v.z == kArEmpty || v.w == kArEmpty) {
+        if (clock64() - t0 > (1ll << 31)) {
+          atomicExch(a.err, 1);
+          break;
+        }
+        v = ld_relaxed_sys_v4(slot);
+      }
+      acc.x += __uint_as_float(v.x);
+      acc.y += __uint_as_float(v.y);
+      acc.z += __uint_as_float(v.z);
+      acc.w += __uint_as_float(v.w);
+      st_relaxed_sys_v4(slot, make_uint4(kArEmpty, kArEmpty, kArEmpty, kArEmpty));
     }
     const size_t e = i * 4;
     if (e < a.n) a.data[e] = acc.x;
@@ -141,8 +153,8 @@ __global__ void __launch_bounds__(512) oneshot_allreduce_kernel(const ArArgs a) 
     if (e + 2 < a.n) a.data[e + 2] = acc.z;
     if (e + 3 < a.n) a.data[e + 3] = acc.w;
   }
+  __syncthreads();
   if (threadIdx.x == 0) *counter = gen;
-  asm volatile("griddepcontrol.launch_dependents;");
 }
 
 // Collective set-up of the peer buffers: allocate, zero, exchange IPC handles
@@ -154,7 +166,8 @@ int ar_setup(vxb_comm *c) {
     cudaGetLastError();
     return set_error(ctx, VXB_ENOMEM, "vxb_comm_init: peer buffer");
   }
-  VXB_CUDA_TRY(ctx, cudaMemset(c->ar_local, 0, kArBytes));
+  VXB_CUDA_TRY(ctx, cudaMemset(c->ar_local, 0xFF, kArCountersOff));  // every slot empty
+  VXB_CUDA_TRY(ctx, cudaMemset(c->ar_local + kArCountersOff, 0, kArBytes - kArCountersOff));
   cudaIpcMemHandle_t h;
   VXB_CUDA_TRY(ctx, cudaIpcGetMemHandle(&h, c->ar_local));
   uint8_t *d_handles = nullptr;

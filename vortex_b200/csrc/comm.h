@@ -3,17 +3,20 @@
 
 #include "vxb_internal.h"
 
-// One-shot all-reduce over NVLink peer memory for decode-sized messages
-// (up to kArMaxBytes of f32): every rank's buffer is mapped into every other
-// rank with CUDA IPC.
+// One-shot all-reduce over NVLink peer memory for decode-sized messages (up
+// to kArOneShotBytes of f32): every rank's buffer is mapped into every other
+// rank with CUDA IPC. A buffer holds, for each of three generations, one slot
+// per source rank (filled with the empty marker between uses), then the
+// per-block generation counters.
 constexpr int kArMaxRanks = 8;
-constexpr int kArBlocks = 32;                      // CTAs (message slices) per call
-constexpr size_t kArMaxBytes = (size_t)1 << 20;    // per slot
-// messages up to this size take the one-shot path (measured on 8 B200s: 18-36
-// us against NCCL's 36-40 us up to 512 KiB; NCCL wins from about 1 MiB)
+constexpr int kArBlocks = 32;  // CTAs (message slices) per call
+constexpr int kArGens = 3;     // generations rotating through the slots
+// messages up to this size take the one-shot path (NCCL above)
 constexpr size_t kArOneShotBytes = (size_t)512 << 10;
-constexpr size_t kArFlagsOff = 2 * kArMaxBytes;    // two data slots, then flags
-constexpr size_t kArBytes = kArFlagsOff + (size_t)kArBlocks * kArMaxRanks * 4 + (size_t)kArBlocks * 4;
+constexpr size_t kArSlotBytes = kArOneShotBytes;  // per (generation, source rank)
+constexpr size_t kArCountersOff = (size_t)kArGens * kArMaxRanks * kArSlotBytes;
+constexpr size_t kArBytes = kArCountersOff + (size_t)kArBlocks * 4;
+constexpr uint32_t kArEmpty = 0xFFFFFFFFu;  // a NaN bit pattern no sent value has
 
 struct vxb_comm {
   vxb_ctx *ctx = nullptr;

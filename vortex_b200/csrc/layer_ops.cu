@@ -253,7 +253,7 @@ __device__ __forceinline__ void scan_row(const float *__restrict__ l, int vocab,
   for (int i = threadIdx.x; i < vocab; i += blockDim.x) visit(__ldcg(l + i), i);
 }
 
-__global__ void argmax_kernel(const float *__restrict__ logits, int vocab, int32_t *__restrict__ out) {
+__global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ logits, int vocab, int32_t *__restrict__ out) {
   __shared__ float sv[32];
   __shared__ int si[32];
   asm volatile("griddepcontrol.launch_dependents;");
@@ -335,8 +335,8 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
 }
 
 // Key of the first maximum of each row of a vocab shard starting at `offset`.
-__global__ void argmax_key_kernel(const float *__restrict__ logits, int vocab, int offset,
-                                  unsigned long long *__restrict__ keys) {
+__global__ void __launch_bounds__(1024) argmax_key_kernel(const float *__restrict__ logits, int vocab, int offset,
+                                                          unsigned long long *__restrict__ keys) {
   __shared__ unsigned long long sk[32];
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
