@@ -37,6 +37,7 @@
 //    (clock64); a timeout sets the context's device error word and the kernel
 //    runs to completion.
 #include <algorithm>
+#include <cstring>
 #include <map>
 #include <mutex>
 
@@ -45,6 +46,7 @@
 #include <cuda_fp16.h>
 
 #include "gemv.h"
+#include "tc_common.h"
 #include "tiled_layout.h"
 #include "vxb_internal.h"
 
@@ -57,7 +59,14 @@ constexpr int CWARPS = 8;                   // consumer warps (one 16-row tile e
 constexpr int THREADS = (CWARPS + 1) * 32;  // + one producer warp
 constexpr int ROWS_PER_CTA = CWARPS * 16;
 constexpr int STAGES = 3;
-constexpr int CS = 4;  // chunks (records) per stage
+constexpr int CS = 4;  // chunks (units of a tile) per stage
+// batches above 8: stages of 2 chunks in a 6-deep ring (the same shared
+// memory, twice the look-ahead), each stage's activations as 2-D TMA boxes
+// of 64 columns x B rows with 128-byte swizzle
+constexpr int BCS = 2;
+constexpr int BSTAGES = 6;
+constexpr int XBOX_K = 64;              // columns per activation box (128 bytes)
+constexpr int XBOX_BYTES = 32 * 128;    // one box, rows padded to 32 (a 1024-byte multiple)
 constexpr int kMaxClusterSplits = 8;  // portable cluster size
 
 template <int FMT>
@@ -67,6 +76,11 @@ struct Geo {
   static constexpr int SCT = 8 * BPC * 4;           // scale bytes of one (tile, chunk) unit
   static constexpr int UNIT = 512 + SCT;            // bytes of one (tile, chunk) unit
   static constexpr int STAGE = CWARPS * CS * UNIT;  // a 128-row group's CS chunks
+  // batch path: weights of one stage (1024-byte aligned) + its x boxes
+  static constexpr int BW = CWARPS * BCS * UNIT;
+  static constexpr int BWP = (BW + 1023) / 1024 * 1024;
+  static constexpr int NXB = BCS * CH / XBOX_K;  // x boxes per stage (Q4_0 2, Q8_0 1)
+  static constexpr int BSTG = BWP + NXB * XBOX_BYTES;
   static constexpr int XSTR = CS * CH + 16;  // elements per batch row of a stage's x slice
 };
 
@@ -279,17 +293,32 @@ __device__ __forceinline__ void epilogue_store(const GemvArgs &a, int b, int row
 
 // Consumer main loop over n_iter full stages: acc[nt][0] = rows g, acc[nt][1]
 // = rows g+8 of the warp's tile, batch columns (2q, 2q+1) of n-tile nt.
+// Batch <= 8: stages of CS chunks, x staged once for the split as f16 (xs).
+// Batch > 8: stages of BCS chunks whose activations follow the weights as
+// swizzled TMA boxes (row n of a box at n * 128 bytes, 16-byte chunk c of the
+// row at chunk position c ^ (n % 8)).
 template <int FMT, int NT, bool SUBN>
 __device__ __forceinline__ void consume_stages(const GemvArgs &a, const uint8_t *stages, uint64_t *full,
                                                uint64_t *empty, const uint16_t *xs, int n_iter, float2 (&acc)[NT][2]) {
   using G = Geo<FMT>;
   constexpr bool XF16 = XMode<NT>::F16;
-  constexpr int STG = G::STAGE + (XF16 ? 0 : 8 * NT * G::XSTR * 2);
+  constexpr int KCS = XF16 ? CS : BCS;          // chunks per stage
+  constexpr int NSTG = XF16 ? STAGES : BSTAGES;  // ring depth
+  constexpr int STG = XF16 ? G::STAGE : G::BSTG;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
   for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = make_float2(0.f, 0.f);
-  const int xstride = XF16 ? a.xs_stride : G::XSTR;
-  const int xlane = (lane >> 2) * xstride + (lane & 3) * 4;
+  const int xlane = (lane >> 2) * a.xs_stride + (lane & 3) * 4;  // XF16
+  // batch path: byte offset of the lane's 8-byte operand inside a box, for
+  // the four 16-column positions C = 0, 2, 4, 6 of the 16-byte chunk index
+  // ((C | (q >> 1)) ^ n) with n % 8 = lane / 4 for every n-tile
+  uint32_t boff[4];
+  {
+    const int q = lane & 3, sw = lane >> 2;
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+      boff[c] = (uint32_t)(sw * 128 + ((((2 * c) | (q >> 1)) ^ sw) << 4) + (q & 1) * 8);
+  }
   // batch rows past B are not staged: their operand is zero
   bool live[NT];
 #pragma unroll
@@ -299,18 +328,19 @@ __device__ __forceinline__ void consume_stages(const GemvArgs &a, const uint8_t 
   // accumulators: the first k16 step of every block of the group is issued,
   // then the second, then the scale FMAs, so consecutive MMAs never depend on
   // each other and the tensor-core latency overlaps across blocks.
-  constexpr int BLK = CS * G::BPC;                      // blocks per stage
-  constexpr int GB = NT == 1 ? 4 : (NT == 2 ? 2 : 1);  // blocks per group
+  constexpr int BLK = KCS * G::BPC;                          // blocks per stage
+  constexpr int GB0 = NT == 1 ? 4 : (NT == 2 ? 2 : 1);
+  constexpr int GB = GB0 < BLK ? GB0 : BLK;                   // blocks per group
   for (int it = 0; it < n_iter; it++) {
-    const int slot = it % STAGES;
-    if (!mbar_wait(&full[slot], (it / STAGES) & 1)) atomicExch(a.err, 1);
+    const int slot = it % NSTG;
+    if (!mbar_wait(&full[slot], (it / NSTG) & 1)) atomicExch(a.err, 1);
     const uint8_t *st = stages + slot * STG;
-    const uint8_t *cw = st + warp * CS * G::UNIT + lane * 16;
-    const uint8_t *sw = st + warp * CS * G::UNIT + 512 + (lane >> 2) * G::BPC * 4;
-    uint4 wv[CS];
-    uint32_t sv[CS][G::BPC];
+    const uint8_t *cw = st + warp * KCS * G::UNIT + lane * 16;
+    const uint8_t *sw = st + warp * KCS * G::UNIT + 512 + (lane >> 2) * G::BPC * 4;
+    uint4 wv[KCS];
+    uint32_t sv[KCS][G::BPC];
 #pragma unroll
-    for (int j = 0; j < CS; j++) {
+    for (int j = 0; j < KCS; j++) {
       wv[j] = *reinterpret_cast<const uint4 *>(cw + j * G::UNIT);
       if (G::BPC == 2) {
         const uint2 t2 = *reinterpret_cast<const uint2 *>(sw + j * G::UNIT);
@@ -320,8 +350,8 @@ __device__ __forceinline__ void consume_stages(const GemvArgs &a, const uint8_t 
         sv[j][0] = *reinterpret_cast<const uint32_t *>(sw + j * G::UNIT);
       }
     }
-    const uint16_t *xk = XF16 ? xs + it * CS * G::CH + xlane
-                              : reinterpret_cast<const uint16_t *>(st + G::STAGE) + xlane;
+    const uint16_t *xk = xs + it * CS * G::CH + xlane;  // XF16
+    const uint8_t *xbox = st + G::BWP;                   // batch path
 #pragma unroll
     for (int b0 = 0; b0 < BLK; b0 += GB) {
       float t[GB][NT][4];
@@ -343,10 +373,18 @@ __device__ __forceinline__ void consume_stages(const GemvArgs &a, const uint8_t 
             else
               decode_q8_bf16(wu[h * 2], wu[h * 2 + 1], A);
           }
+          // column of this k16 step inside the stage, its box and 16-column position
+          const int kk = blk * 32 + h * 16;
 #pragma unroll
           for (int nt = 0; nt < NT; nt++) {
             uint2 bx = make_uint2(0u, 0u);
-            if (live[nt]) bx = *reinterpret_cast<const uint2 *>(xk + (size_t)nt * 8 * xstride + blk * 32 + h * 16);
+            if (live[nt]) {
+              if (XF16)
+                bx = *reinterpret_cast<const uint2 *>(xk + (size_t)nt * 8 * a.xs_stride + kk);
+              else
+                bx = *reinterpret_cast<const uint2 *>(xbox + (kk / XBOX_K) * XBOX_BYTES + nt * 8 * 128 +
+                                                      boff[(kk % XBOX_K) / 16]);
+            }
             if (XF16) {
               if (h == 0)
                 mma_f16_z(t[gb][nt], A, bx.x, bx.y);
@@ -380,30 +418,35 @@ __device__ __forceinline__ void consume_stages(const GemvArgs &a, const uint8_t 
 }
 
 template <int FMT, int NT>
-__global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2)
+    gemv_q_kernel(const __grid_constant__ CUtensorMap xmap, const GemvArgs a) {
   using G = Geo<FMT>;
   constexpr int BR = 8 * NT;  // padded batch rows
   constexpr bool XF16 = XMode<NT>::F16;
-  constexpr int XB = XF16 ? 0 : BR * G::XSTR * 2;  // bytes of a stage's x slice
-  constexpr int STG = G::STAGE + XB;
-  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int KCS = XF16 ? CS : BCS;           // chunks per stage
+  constexpr int NSTG = XF16 ? STAGES : BSTAGES;  // ring depth
+  constexpr int STG = XF16 ? G::STAGE : G::BSTG;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  // the batch path's swizzled boxes need 1024-byte alignment
+  uint8_t *smem = XF16 ? smem_raw
+                       : reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t *stages = smem;
-  uint16_t *xs = reinterpret_cast<uint16_t *>(smem + STAGES * STG);  // XF16 only
+  uint16_t *xs = reinterpret_cast<uint16_t *>(smem + NSTG * STG);  // XF16 only
   float *red = reinterpret_cast<float *>(smem);  // reuses the stages after the main loop
-  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES];
+  __shared__ __align__(8) uint64_t full[NSTG], empty[NSTG];
   __shared__ int s_exp[BR];
   __shared__ int s_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = blockIdx.x, s = blockIdx.y;
   // k-splits own whole stages (the chunk count is a multiple of CS)
-  const int n_stages = a.n_chunks / CS;
+  const int n_stages = a.n_chunks / KCS;
   const int st0 = (int)((long long)s * n_stages / a.S);
   const int n_iter = (int)((long long)(s + 1) * n_stages / a.S) - st0;
-  const int c0 = st0 * CS, nck = n_iter * CS;
+  const int c0 = st0 * KCS, nck = n_iter * KCS;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < STAGES; i++) {
+    for (int i = 0; i < NSTG; i++) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], CWARPS);
     }
@@ -419,48 +462,43 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const 
       // a stage holds CS units of each, tile-major
       const uint8_t *src = a.records + ((size_t)g * CWARPS * a.n_chunks + c0) * G::UNIT;
       const size_t tile_stride = (size_t)a.n_chunks * G::UNIT;
-      constexpr uint32_t TB = CS * G::UNIT;  // bytes of one tile in a stage
+      constexpr uint32_t TB = KCS * G::UNIT;  // bytes of one tile in a stage
+      constexpr uint32_t WB = CWARPS * TB;    // weight bytes of a stage
       auto copy_stage = [&](uint8_t *dst, int it, uint64_t *bar) {
 #pragma unroll
         for (int t = 0; t < CWARPS; t++) bulk_g2s(dst + t * TB, src + t * tile_stride + (size_t)it * TB, TB, bar);
       };
       if (XF16) {
         for (int it = 0; it < n_iter; it++) {
-          const int slot = it % STAGES;
-          if (it >= STAGES && !mbar_wait(&empty[slot], ((it / STAGES) & 1) ^ 1)) atomicExch(a.err, 1);
-          mbar_expect_tx(&full[slot], (uint32_t)G::STAGE);
+          const int slot = it % NSTG;
+          if (it >= NSTG && !mbar_wait(&empty[slot], ((it / NSTG) & 1) ^ 1)) atomicExch(a.err, 1);
+          mbar_expect_tx(&full[slot], WB);
           copy_stage(stages + slot * STG, it, &full[slot]);
         }
       } else {
         // weights of the first stages before waiting for the kernel that
-        // produces x; each stage's single arrival comes after its x copies
-        const int pre = min(STAGES, n_iter);
+        // produces x; each stage's single arrival comes after its x boxes
+        // (columns past K arrive as zeros)
+        const int pre = min(NSTG, n_iter);
         for (int it = 0; it < pre; it++) {
-          mbar_expect_tx_only(&full[it], (uint32_t)G::STAGE);
+          mbar_expect_tx_only(&full[it], WB);
           copy_stage(stages + it * STG, it, &full[it]);
         }
         asm volatile("griddepcontrol.wait;" ::: "memory");
+        const uint32_t xbytes = (uint32_t)(G::NXB * a.B * XBOX_K * 2);
         for (int it = 0; it < n_iter; it++) {
-          const int slot = it % STAGES;
+          const int slot = it % NSTG;
           uint8_t *dst = stages + slot * STG;
-          if (it >= STAGES) {
-            if (!mbar_wait(&empty[slot], ((it / STAGES) & 1) ^ 1)) atomicExch(a.err, 1);
-            mbar_expect_tx_only(&full[slot], (uint32_t)G::STAGE);
+          if (it >= NSTG) {
+            if (!mbar_wait(&empty[slot], ((it / NSTG) & 1) ^ 1)) atomicExch(a.err, 1);
+            mbar_expect_tx_only(&full[slot], WB);
             copy_stage(dst, it, &full[slot]);
           }
-          uint16_t *xd = reinterpret_cast<uint16_t *>(dst + G::STAGE);
-          const int kst = (c0 + it * CS) * G::CH;
-          const int kv = max(0, min(CS * G::CH, a.K - kst));  // columns of x inside K
-          if (kv < CS * G::CH) {
-            for (int b = 0; b < a.B; b++)
-              for (int k = kv; k < CS * G::CH; k += 2)
-                *reinterpret_cast<uint32_t *>(xd + b * G::XSTR + k) = 0u;
-          }
-          if (kv > 0) {
-            mbar_expect_tx_only(&full[slot], (uint32_t)(a.B * kv * 2));
-            for (int b = 0; b < a.B; b++)
-              bulk_g2s(xd + b * G::XSTR, a.x + (size_t)b * a.K + kst, (uint32_t)(kv * 2), &full[slot]);
-          }
+          const int kst = (c0 + it * KCS) * G::CH;
+          mbar_expect_tx_only(&full[slot], xbytes);
+#pragma unroll
+          for (int xb = 0; xb < G::NXB; xb++)
+            vxb::tc::tma_load_2d(dst + G::BWP + xb * XBOX_BYTES, &xmap, kst + xb * XBOX_K, 0, &full[slot]);
           mbar_arrive(&full[slot]);
         }
       }
@@ -565,14 +603,31 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2) gemv_q_kernel(const 
     // done before any CTA exits
     __syncwarp();
     cluster_sync_all();
-    const int per = (nel + a.S - 1) / a.S;
+    // four consecutive outputs per thread and 16-byte distributed loads, the
+    // S peers' loads all issued before the sum (nel and the slices are
+    // multiples of 4)
+    const int per = ((nel / 4 + a.S - 1) / a.S) * 4;
     const int i1 = min(nel, (s + 1) * per);
     cg::cluster_group cl = cg::this_cluster();
-    for (int i = s * per + threadIdx.x; i < i1; i += CWARPS * 32) {
-      const int b = i / ROWS_PER_CTA, r = i % ROWS_PER_CTA;
-      float v = 0.f;
-      for (int ss = 0; ss < a.S; ss++) v += *cl.map_shared_rank(red + i, (unsigned)ss);
-      if (r < nrows) epilogue_store(a, b, row0 + r, v);
+    for (int i = s * per + 4 * threadIdx.x; i < i1; i += 4 * CWARPS * 32) {
+      float4 pv[kMaxClusterSplits];
+#pragma unroll
+      for (int ss = 0; ss < kMaxClusterSplits; ss++)
+        if (ss < a.S) pv[ss] = *reinterpret_cast<const float4 *>(cl.map_shared_rank(red + i, (unsigned)ss));
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int ss = 0; ss < kMaxClusterSplits; ss++)
+        if (ss < a.S) {
+          v.x += pv[ss].x;
+          v.y += pv[ss].y;
+          v.z += pv[ss].z;
+          v.w += pv[ss].w;
+        }
+      const int b = i / ROWS_PER_CTA, r = i % ROWS_PER_CTA;  // 4 rows of one batch column
+      if (r < nrows) epilogue_store(a, b, row0 + r, v.x);
+      if (r + 1 < nrows) epilogue_store(a, b, row0 + r + 1, v.y);
+      if (r + 2 < nrows) epilogue_store(a, b, row0 + r + 2, v.z);
+      if (r + 3 < nrows) epilogue_store(a, b, row0 + r + 3, v.w);
     }
     __syncwarp();
     cluster_sync_all();
@@ -995,10 +1050,44 @@ int stream_gemv(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const 
 
 size_t smem_bytes_t(int fmt, int NT, int batch, int xs_stride) {
   const size_t stage = fmt == VXB_Q4_0 ? Geo<0>::STAGE : Geo<1>::STAGE;
-  const size_t xstr = fmt == VXB_Q4_0 ? Geo<0>::XSTR : Geo<1>::XSTR;
+  const size_t bstage = fmt == VXB_Q4_0 ? Geo<0>::BSTG : Geo<1>::BSTG;
   const size_t red = (size_t)8 * NT * ROWS_PER_CTA * 4;
-  if (NT > 1) return std::max((size_t)STAGES * (stage + (size_t)8 * NT * xstr * 2), red);
+  // + 1024 bytes to align the batch path's ring for the swizzled boxes
+  if (NT > 1) return std::max((size_t)BSTAGES * bstage, red) + 1024;
   return std::max((size_t)STAGES * stage, red) + (size_t)std::min(batch, 8 * NT) * xs_stride * 2;
+}
+
+// Tensor map of the activations x [B, K] bf16 for the batch path: boxes of
+// 64 columns x B rows, 128-byte swizzle, columns past K read as zero.
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int x_tensor_map(vxb_ctx *ctx, const uint16_t *x, int B, int K, CUtensorMap *map) {
+  static std::mutex mu;
+  static EncodeTiledFn fn = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!fn) {
+      void *p = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+          q != cudaDriverEntryPointSuccess || !p) {
+        cudaGetLastError();
+        return set_error(ctx, VXB_ECUDA, "vxb_gemv_q: cuTensorMapEncodeTiled is not available from the driver");
+      }
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)B};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {(cuuint32_t)XBOX_K, (cuuint32_t)B};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t *>(x), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return VXB_OK;
 }
 
 int xs_stride_for(int kc_max) { return kc_max + 16; }  // stride/2 = 8 (mod 32): conflict-free 8-byte loads
@@ -1071,6 +1160,10 @@ int resident(int fmt, int NT, size_t smem, int cluster, int sms) {
 template <int FMT, int NT>
 int launch_t(vxb_ctx *ctx, const GemvArgs &a, dim3 grid, size_t smem, cudaStream_t st, bool pdl) {
   auto kfn = gemv_q_kernel<FMT, NT>;
+  CUtensorMap xmap;  // the batch path's activation boxes (unused for batch <= 8)
+  memset(&xmap, 0, sizeof(xmap));
+  if (NT > 1)
+    if (int rc = x_tensor_map(ctx, a.x, a.B, a.K, &xmap)) return rc;
   static bool configured[64] = {false};
   const int dev = ctx->device & 63;
   if (!configured[dev]) {
@@ -1098,7 +1191,7 @@ int launch_t(vxb_ctx *ctx, const GemvArgs &a, dim3 grid, size_t smem, cudaStream
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  VXB_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, kfn, a));
+  VXB_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, kfn, xmap, a));
   return VXB_OK;
 }
 
