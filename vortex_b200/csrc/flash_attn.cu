@@ -10,19 +10,22 @@
 //
 // One CTA per (128-query tile, head, batch), 6 warps:
 //  * warp 5 (one elected thread) loads Q once and the K and V tiles of 128
-//    keys into two separate double-buffered rings with TMA (4-D tensor maps,
-//    128-byte swizzle); a K stage is refilled as soon as its S = Q K^T has
-//    completed, a V stage once its P.V has.
+//    keys into two separate 3-stage rings with TMA (4-D tensor maps, 128-byte
+//    swizzle); a K stage is refilled as soon as its S = Q K^T has completed,
+//    a V stage once its P.V has.
 //  * warp 4 (one elected thread) issues the MMAs: S = Q K^T (M=128, N=128,
-//    K=128 as 8 x K16) into TMEM columns [0,128), then O += P V (A = P from
-//    shared memory, B = V read MN-major) into TMEM columns [128,256).
-//    Completion is signalled to mbarriers with tcgen05.commit.
+//    K=128 as 8 x K16) into TMEM columns [0,128), then O += P V with A = P
+//    read from TMEM and B = V read MN-major from shared memory, into TMEM
+//    columns [128,256). Completion is signalled to mbarriers with
+//    tcgen05.commit.
 //  * warps 0-3 own one query row each (TMEM lane = row): they read the row of
 //    S with tcgen05.ld, apply scale (log2 domain) and the causal / length mask,
-//    keep a reference max m and the sum l, and write P = 2^(s - m) as bf16
-//    into shared memory in the swizzled K-major layout the MMA reads. m moves
-//    (and the row of O in TMEM is rescaled) only when the row's max exceeds it
-//    by more than 2^8, so most tiles skip the rescale.
+//    keep a reference max m and the sum l, and store P = 2^(s - m) as bf16
+//    hi + lo with tcgen05.st into one of two TMEM P buffers (columns
+//    [256,384) and [384,512)), so the exponentials of tile j+1 need not wait
+//    for the P.V of tile j. m moves (and the row of O in TMEM is rescaled)
+//    only when the row's max exceeds it by more than 2^8, so most tiles skip
+//    the rescale.
 //  * The MMA of S for the next tile is issued as soon as the softmax warps have
 //    read the current S, so it overlaps their exponentials.
 // Every mbarrier wait is bounded (clock64); a timeout sets the context's
@@ -46,13 +49,16 @@ constexpr int BN = 128;       // keys per tile
 constexpr int THREADS = 192;  // 4 softmax warps + MMA warp + TMA warp
 constexpr int TILE_BYTES = BM * D * 2;  // 32 KB: two 64-column slabs of [128 rows x 128 B]
 constexpr int SLAB = 128 * 128;         // bytes of one slab
+constexpr int KV_STAGES = 3;
 constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + TILE_BYTES;       // 2 stages
-constexpr int OFF_V = OFF_K + 2 * TILE_BYTES;   // 2 stages
-constexpr int OFF_P = OFF_V + 2 * TILE_BYTES;   // P = hi + lo, two bf16 tiles
-constexpr int SMEM_BYTES = OFF_P + 2 * TILE_BYTES;  // 224 KB
-constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;   // + alignment slack
-constexpr uint32_t TMEM_COLS = 256;
+constexpr int OFF_K = OFF_Q + TILE_BYTES;                  // KV_STAGES stages
+constexpr int OFF_V = OFF_K + KV_STAGES * TILE_BYTES;      // KV_STAGES stages
+constexpr int SMEM_BYTES = OFF_V + KV_STAGES * TILE_BYTES;  // 224 KB
+constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;              // + alignment slack
+// TMEM columns: S [0,128), O [128,256), P buffers [256,384) and [384,512),
+// each P = bf16 hi (64 columns of key pairs) then lo (64 columns)
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t COL_O = 128, COL_P = 256;
 // O is rescaled only when a row's running max grows by more than this (log2
 // units): P then stays below 2^8, exact in f32 and representable in bf16.
 constexpr float RESCALE_THRESHOLD = 8.f;
@@ -66,7 +72,8 @@ struct FlashArgs {
 };
 
 struct Bars {
-  uint64_t q, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full, s_free, p_full, o_done;
+  uint64_t q, k_full[KV_STAGES], k_empty[KV_STAGES], v_full[KV_STAGES], v_empty[KV_STAGES], s_full, s_free, p_full,
+      o_done, p_free[2];
 };
 
 template <bool CAUSAL>
@@ -93,7 +100,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   if (threadIdx.x == 32) {
     mbar_init(&bars.q, 1);
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < KV_STAGES; i++) {
       mbar_init(&bars.k_full[i], 1);
       mbar_init(&bars.k_empty[i], 1);
       mbar_init(&bars.v_full[i], 1);
@@ -103,31 +110,33 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(&bars.s_free, 4);
     mbar_init(&bars.p_full, 4);
     mbar_init(&bars.o_done, 1);
+    mbar_init(&bars.p_free[0], 1);
+    mbar_init(&bars.p_free[1], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base_s;
-  const uint32_t tS = tmem, tO = tmem + BN;
+  const uint32_t tS = tmem, tO = tmem + COL_O;
 
   if (warp == 5) {
     // ---------------- TMA producer: Q once, then K and V of each key tile into
-    // their own double-buffered rings. K(j) waits only for S(j-2), V(j) for
-    // PV(j-2), so K tiles run ahead of the P.V products.
+    // their own rings. K(j) waits only for S(j-3), V(j) for PV(j-3), so K
+    // tiles run ahead of the P.V products.
     if (lane == 0) {
       mbar_expect_tx(&bars.q, TILE_BYTES);
       tma_load_4d(sm + OFF_Q, &tq, 0, h, q0, b, &bars.q);
       tma_load_4d(sm + OFF_Q + SLAB, &tq, 64, h, q0, b, &bars.q);
       for (int j = 0; j < n_kv; j++) {
-        const int st = j & 1;
-        const uint32_t ph = ((j >> 1) - 1) & 1;
+        const int st = j % KV_STAGES;
+        const uint32_t ph = ((j / KV_STAGES) - 1) & 1;
         uint8_t *k = sm + OFF_K + st * TILE_BYTES, *v = sm + OFF_V + st * TILE_BYTES;
-        if (j >= 2) wait_or_flag(&bars.k_empty[st], ph, a.err);
+        if (j >= KV_STAGES) wait_or_flag(&bars.k_empty[st], ph, a.err);
         mbar_expect_tx(&bars.k_full[st], TILE_BYTES);
         tma_load_4d(k, &tk, 0, hk, j * BN, b, &bars.k_full[st]);
         tma_load_4d(k + SLAB, &tk, 64, hk, j * BN, b, &bars.k_full[st]);
-        if (j >= 2) wait_or_flag(&bars.v_empty[st], ph, a.err);
+        if (j >= KV_STAGES) wait_or_flag(&bars.v_empty[st], ph, a.err);
         mbar_expect_tx(&bars.v_full[st], TILE_BYTES);
         tma_load_4d(v, &tv, 0, hk, j * BN, b, &bars.v_full[st]);
         tma_load_4d(v + SLAB, &tv, 64, hk, j * BN, b, &bars.v_full[st]);
@@ -137,32 +146,33 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 4) {
     // ---------------- MMA issue (one thread): S(j) then PV(j-1)
     if (lane == 0) {
-      const uint32_t sQ = smem_u32(sm + OFF_Q), sP = smem_u32(sm + OFF_P);
+      const uint32_t sQ = smem_u32(sm + OFF_Q);
       constexpr uint32_t ID_QK = idesc_bf16(BM, BN, false), ID_PV = idesc_bf16(BM, D, true);
       wait_or_flag(&bars.q, 0, a.err);
       auto issue_pv = [&](int j) {
-        const int st = j & 1;
+        const int st = j % KV_STAGES;
         wait_or_flag(&bars.p_full, j & 1, a.err);
-        wait_or_flag(&bars.v_full[st], (j >> 1) & 1, a.err);
+        wait_or_flag(&bars.v_full[st], (j / KV_STAGES) & 1, a.err);
         tc_fence_after();
         const uint32_t sV = smem_u32(sm + OFF_V + st * TILE_BYTES);
+        const uint32_t tP = tmem + COL_P + (uint32_t)(j & 1) * 128;
         // O += P_hi V + P_lo V: the K dimension runs over the keys twice
 #pragma unroll
         for (int t = 0; t < 2 * BN / 16; t++) {
           const int tk = t & 7;
-          // A = P (K-major over keys): slab tk/4, 32 bytes per k16 step
-          const uint64_t ad = sw128_desc(sP + (t >> 3) * TILE_BYTES + (tk >> 2) * SLAB + (tk & 3) * 32, 16, 1024);
+          // A = P from TMEM: 16 keys = 8 columns of bf16 pairs (hi, then lo)
           // B = V read MN-major: 16 keys = two 8-row groups of 1024 bytes; the
           // two 64-column slabs of d are 16 KB apart
           const uint64_t bd = sw128_desc(sV + tk * 2048, SLAB, 1024);
-          umma_bf16(tO, ad, bd, ID_PV, (j > 0 || t > 0) ? 1u : 0u);
+          umma_bf16_ts(tO, tP + (uint32_t)t * 8, bd, ID_PV, (j > 0 || t > 0) ? 1u : 0u);
         }
         umma_commit(&bars.o_done);
         umma_commit(&bars.v_empty[st]);
+        umma_commit(&bars.p_free[j & 1]);
       };
       for (int j = 0; j < n_kv; j++) {
-        const int st = j & 1;
-        wait_or_flag(&bars.k_full[st], (j >> 1) & 1, a.err);
+        const int st = j % KV_STAGES;
+        wait_or_flag(&bars.k_full[st], (j / KV_STAGES) & 1, a.err);
         if (j > 0) wait_or_flag(&bars.s_free, (j - 1) & 1, a.err);
         tc_fence_after();
         const uint32_t sK = smem_u32(sm + OFF_K + st * TILE_BYTES);
@@ -183,7 +193,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int r = threadIdx.x;
     const int row = q0 + r;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    uint8_t *prow = sm + OFF_P + r * 128;
     const int lim = CAUSAL ? min(a.S - 1, row) : a.S - 1;  // last visible key
     // m: the reference max of the row (log2 domain), P = 2^(s - m) <= 2^8
     float m = -INFINITY, l = 0.f;
@@ -227,42 +236,45 @@ __global__ void __launch_bounds__(THREADS, 1)
       l = l * alpha + sum;
       m = m_new;
 
-      if (j > 0) {
-        // O holds the tiles before j: wait for the last P.V (it still reads
-        // the P buffer), then rescale the rows whose reference max moved
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // O holds the tiles before j: wait for the last P.V, then rescale the
+        // rows whose reference max moved
         wait_or_flag(&bars.o_done, (j - 1) & 1, a.err);
         tc_fence_after();
-        if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll
-          for (int c = 0; c < D / 32; c++) {
-            float o[32];
-            tmem_ld32(tO + lane_off + c * 32, o);
-            tmem_wait_ld();
+        for (int c = 0; c < D / 32; c++) {
+          float o[32];
+          tmem_ld32(tO + lane_off + c * 32, o);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; i++) o[i] *= alpha;
-            tmem_st32(tO + lane_off + c * 32, o);
-          }
-          tmem_wait_st();
+          for (int i = 0; i < 32; i++) o[i] *= alpha;
+          tmem_st32(tO + lane_off + c * 32, o);
         }
+        tmem_wait_st();
+      }
+      // P buffer j % 2 is free once P.V of tile j - 2 has completed
+      if (j >= 2) {
+        wait_or_flag(&bars.p_free[j & 1], ((j >> 1) - 1) & 1, a.err);
+        tc_fence_after();
       }
       // P as bf16 hi + lo (p - hi rounded again: 16 significant bits, so the
-      // P.V product keeps the precision of the f32 softmax) into the swizzled
-      // K-major layout: 16-byte chunk ch of the row sits at chunk position
-      // ch ^ (row % 8) of its 128-byte slab row
+      // P.V product keeps the precision of the f32 softmax) into the row's
+      // TMEM lane: key pairs (2c, 2c+1) in column c, hi in columns 0-63, lo
+      // in columns 64-127
+      const uint32_t tP = tmem + COL_P + (uint32_t)(j & 1) * 128 + lane_off;
 #pragma unroll
-      for (int ch = 0; ch < BN / 8; ch++) {
-        uint32_t hi[4], lo[4];
+      for (int c = 0; c < BN / 64; c++) {
+        uint32_t hi[32], lo[32];
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const float p0 = s[ch * 8 + 2 * e], p1 = s[ch * 8 + 2 * e + 1];
+        for (int e = 0; e < 32; e++) {
+          const float p0 = s[c * 64 + 2 * e], p1 = s[c * 64 + 2 * e + 1];
           hi[e] = pack_bf16(p0, p1);
           lo[e] = pack_bf16(p0 - __uint_as_float(hi[e] << 16), p1 - __uint_as_float(hi[e] & 0xFFFF0000u));
         }
-        const int slab = ch >> 3, pos = (ch & 7) ^ (r & 7);
-        *reinterpret_cast<uint4 *>(prow + slab * SLAB + pos * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4 *>(prow + TILE_BYTES + slab * SLAB + pos * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        tmem_st32u(tP + c * 32, hi);
+        tmem_st32u(tP + 64 + c * 32, lo);
       }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars.p_full);
