@@ -434,11 +434,18 @@ int launch_t(vxb_ctx *ctx, const DecodeArgs &a, cudaStream_t st) {
 
 namespace vxb {
 
+// Token splits per (sequence, kv head): a CTA streams its pages at a rate
+// set by its own pipeline, so the CTAs should fill one wave of the resident
+// slots (3 per SM) rather than spill a small second wave; with many pairs one
+// split each. At most 16 splits: the merge in the last-arriving CTA grows with
+// the split count (measured at batch 1: 12 splits 13 us, 34 splits 19 us).
 DecodePlan decode_plan(const vxb_ctx *ctx, int n, int Hkv, int max_len) {
   DecodePlan p;
   const int sms = ctx->num_sms > 0 ? ctx->num_sms : 148;
   const int pairs = n * Hkv;
-  int splits = (3 * sms + pairs - 1) / pairs;
+  const int slots = 3 * sms;
+  int splits = pairs >= slots ? 1 : slots / pairs;
+  splits = min(splits, 16);
   const int max_split = max(1, (max_len + 63) / 64);
   splits = max(1, min(splits, max_split));
   int tps = (max_len + splits - 1) / splits;
