@@ -15,13 +15,14 @@
 //    X 16 KB + 16 KB per term per stage), loaded by TMA with 128-byte swizzle
 //    (no multicast);
 //  * one thread issues tcgen05.mma (M=128, N=128, K=16; bf16 -> f32), one per
-//    term and k16 step, into one of two TMEM partials (128 columns each, the
-//    stage's 64 k), and releases the stage with tcgen05.commit;
-//  * four epilogue warps (one output row per thread) add each stage's partial
+//    term and k16 step, into one of two TMEM partials (128 columns each, 4
+//    stages = 256 k per partial), and releases each stage with tcgen05.commit;
+//  * four epilogue warps (one output row per thread) add each partial
 //    (tcgen05.ld) to the row's f32 sums in registers with round-to-nearest
-//    adds, so the long K reduction keeps IEEE f32 accuracy while the tensor
-//    core fills the other partial; then they write Y (f32 or bf16) with the
-//    optional residual.
+//    adds, so the long K reduction keeps f32 accuracy (the tensor core's own
+//    accumulation runs over 256 k at most) while the tensor core fills the
+//    other partial; then they write Y (f32 or bf16) with the optional
+//    residual.
 // Every mbarrier wait is bounded; a timeout sets the context's device error
 // word and the kernel runs to completion.
 #include <cuda.h>
@@ -40,6 +41,9 @@ using namespace vxb::tc;
 namespace {
 
 constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3;
+// k stages accumulated inside one TMEM partial before the epilogue adds it to
+// the f32 row sums (256 columns of k per tensor-core accumulation)
+constexpr int DRAIN = 4;
 constexpr int THREADS = 192;  // warp 0: TMA, warp 1: MMA, warps 2-5: epilogue
 constexpr int A_BYTES = BM * BK * 2;          // 16 KB
 constexpr int B_BYTES = BN * BK * 2;          // 16 KB per weight term
@@ -112,9 +116,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t ID = idesc_bf16(BM, BN, false);
       for (int kb = 0; kb < nk; kb++) {
-        const int st = kb % STAGES, pb = kb & 1;
+        const int st = kb % STAGES, grp = kb / DRAIN, pb = grp & 1;
+        const bool first = kb % DRAIN == 0, last = kb % DRAIN == DRAIN - 1 || kb == nk - 1;
         wait_or_flag(&full[st], (kb / STAGES) & 1, a.err);
-        if (kb >= 2) wait_or_flag(&pfree[pb], ((kb >> 1) - 1) & 1, a.err);
+        if (first && grp >= 2) wait_or_flag(&pfree[pb], ((grp >> 1) - 1) & 1, a.err);
         tc_fence_after();
         const uint32_t sa = smem_u32(sm + st * STAGE_BYTES);
         const uint32_t td = tmem + pb * BN;
@@ -123,10 +128,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint64_t ad = sw128_desc(sa + t * 32, 16, 1024);
 #pragma unroll
           for (int u = 0; u < TERMS; u++)
-            umma_bf16(td, ad, sw128_desc(sa + A_BYTES + u * B_BYTES + t * 32, 16, 1024), ID, (t > 0 || u > 0) ? 1u : 0u);
+            umma_bf16(td, ad, sw128_desc(sa + A_BYTES + u * B_BYTES + t * 32, 16, 1024), ID,
+                      (!first || t > 0 || u > 0) ? 1u : 0u);
         }
         umma_commit(&empty[st]);
-        umma_commit(&pfull[pb]);
+        if (last) umma_commit(&pfull[pb]);
       }
     }
     __syncwarp();
@@ -138,9 +144,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     float acc[BN];
 #pragma unroll
     for (int i = 0; i < BN; i++) acc[i] = 0.f;
-    for (int kb = 0; kb < nk; kb++) {
-      const int pb = kb & 1;
-      wait_or_flag(&pfull[pb], (kb >> 1) & 1, a.err);
+    const int ngrp = (nk + DRAIN - 1) / DRAIN;
+    for (int grp = 0; grp < ngrp; grp++) {
+      const int pb = grp & 1;
+      wait_or_flag(&pfull[pb], (grp >> 1) & 1, a.err);
       tc_fence_after();
 #pragma unroll
       for (int c = 0; c < BN / 32; c++) {
