@@ -11,13 +11,13 @@
 // bits. Each weight is split once per call into bf16 terms, t0 = bf16(w),
 // t1 = bf16(w - t0) (and t2 = bf16(w - t0 - t1) for Q8_0), whose sum is w
 // exactly. The GEMM then runs sum_t X * t^T into one f32 accumulator:
-//  * CTA tile 128 rows of X x 128 rows of W, k in stages of 64 (a 3-deep ring:
-//    X 16 KB + 16 KB per term per stage), loaded by TMA with 128-byte swizzle
+//  * CTA tile 128 rows of X x 256 rows of W, k in stages of 64 (a 2-deep ring:
+//    X 16 KB + 32 KB per term per stage), loaded by TMA with 128-byte swizzle
 //    (no multicast);
-//  * one thread issues tcgen05.mma (M=128, N=128, K=16; bf16 -> f32), one per
-//    term and k16 step, into one of two TMEM partials (128 columns each, 4
+//  * one thread issues tcgen05.mma (M=128, N=256, K=16; bf16 -> f32), one per
+//    term and k16 step, into one of two TMEM partials (256 columns each, 4
 //    stages = 256 k per partial), and releases each stage with tcgen05.commit;
-//  * four epilogue warps (one output row per thread) add each partial
+//  * eight epilogue warps (one output row and 128 columns per thread) add each partial
 //    (tcgen05.ld) to the row's f32 sums in registers with round-to-nearest
 //    adds, so the long K reduction keeps f32 accuracy (the tensor core's own
 //    accumulation runs over 256 k at most) while the tensor core fills the
@@ -40,18 +40,21 @@ using namespace vxb::tc;
 
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3;
+constexpr int BM = 128, BN = 256, BK = 64;
 // k stages accumulated inside one TMEM partial before the epilogue adds it to
 // the f32 row sums (256 columns of k per tensor-core accumulation)
 constexpr int DRAIN = 4;
-constexpr int THREADS = 192;  // warp 0: TMA, warp 1: MMA, warps 2-5: epilogue
+constexpr int THREADS = 320;  // warp 0: TMA, warp 1: MMA, warps 2-9: epilogue
+constexpr int EPI_WARPS = 8;  // two per TMEM lane quadrant, one per 128-column half
 constexpr int A_BYTES = BM * BK * 2;          // 16 KB
-constexpr int B_BYTES = BN * BK * 2;          // 16 KB per weight term
+constexpr int B_BYTES = BN * BK * 2;          // 32 KB per weight term
 constexpr uint32_t TMEM_COLS = 2 * BN;        // two stage partials
 
 template <int TERMS>
 struct GemmGeo {
   static constexpr int STAGE_BYTES = A_BYTES + TERMS * B_BYTES;
+  // ring depth: as many stages as fit (Q4_0: 4 x 48 KB, Q8_0: 3 x 64 KB)
+  static constexpr int STAGES = (227 * 1024 - 1024) / STAGE_BYTES;
   static constexpr int SMEM_ALLOC = STAGES * STAGE_BYTES + 1024;
 };
 static_assert(GemmGeo<3>::SMEM_ALLOC <= 227 * 1024, "shared memory");
@@ -68,6 +71,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     gemm_terms_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
                       const GemmArgs a) {
   constexpr int STAGE_BYTES = GemmGeo<TERMS>::STAGE_BYTES;
+  constexpr int STAGES = GemmGeo<TERMS>::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], pfull[2], pfree[2];
@@ -88,7 +92,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&pfull[i], 1);
-      mbar_init(&pfree[i], 4);
+      mbar_init(&pfree[i], EPI_WARPS);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -137,22 +141,23 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue: warp w owns TMEM lanes 32 * (w % 4) .. +31; each
-    // stage's partial is added in f32 (round to nearest) to the row's sums
-    const int q = warp & 3;
+    // ---------------- epilogue: warp w owns TMEM lanes 32 * (w % 4) .. +31
+    // and columns [128 * half, 128 * half + 128) of the tile; each partial is
+    // added in f32 (round to nearest) to the row's sums
+    const int q = warp & 3, half = (warp - 2) >> 2;
     const int row = m0 + q * 32 + lane;
-    float acc[BN];
+    float acc[128];
 #pragma unroll
-    for (int i = 0; i < BN; i++) acc[i] = 0.f;
+    for (int i = 0; i < 128; i++) acc[i] = 0.f;
     const int ngrp = (nk + DRAIN - 1) / DRAIN;
     for (int grp = 0; grp < ngrp; grp++) {
       const int pb = grp & 1;
       wait_or_flag(&pfull[pb], (grp >> 1) & 1, a.err);
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < BN / 32; c++) {
+      for (int c = 0; c < 128 / 32; c++) {
         float v[32];
-        tmem_ld32(tmem + pb * BN + ((uint32_t)(q * 32) << 16) + c * 32, v);
+        tmem_ld32(tmem + pb * BN + half * 128 + ((uint32_t)(q * 32) << 16) + c * 32, v);
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; i++) acc[c * 32 + i] += v[i];
@@ -163,8 +168,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     if (row < a.M) {
 #pragma unroll
-      for (int c = 0; c < BN / 32; c++) {
-        const int col0 = n0 + c * 32;
+      for (int c = 0; c < 128 / 32; c++) {
+        const int col0 = n0 + half * 128 + c * 32;
         if (col0 >= a.N) break;
         const size_t o = (size_t)row * a.N + col0;
         const int nv = min(32, a.N - col0);
