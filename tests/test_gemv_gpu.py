@@ -61,7 +61,7 @@ def test_device_quantizer_and_tiling_bit_exact(Q, fmt, N, K):
 
 @pytest.mark.parametrize("fmt", [2, 8])
 @pytest.mark.parametrize("N,K", [(16, 32), (17, 96), (1000, 160), (1024, 256), (300, 4096)])
-@pytest.mark.parametrize("B", [1, 3, 8, 9, 32])
+@pytest.mark.parametrize("B", [1, 2, 3, 4, 5, 8, 9, 32])
 def test_gemv_small_shapes(Q, fmt, N, K, B):
     w = _weights(N, K, 7 * N + K)
     xbits, xf = _act(B, K, N)
@@ -96,19 +96,20 @@ def test_gemv_bf16_output(Q, fmt, B):
 
 
 @pytest.mark.parametrize("fmt", [2, 8])
-def test_gemv_subnormal_scales_and_extreme_activations(Q, fmt):
+@pytest.mark.parametrize("B", [1, 4, 9])
+def test_gemv_subnormal_scales_and_extreme_activations(Q, fmt, B):
     """Weights ~1e-4 give f16-subnormal block scales (reference decode: half
     the IEEE value); activations spanning 1e-6..1e5 exercise the per-row
     power-of-two staging."""
-    N, K, B = 64, 512, 4
+    N, K = 64, 512
     w = _weights(N, K, 3, sigma=1e-4)
     blocks = O.quantize_blocks(OFMT[fmt], w.astype(np.float64))
     h = blocks.reshape(-1, 18 if fmt == 2 else 34)[:, :2].copy().view(np.uint16)
     assert np.any((h & 0x7C00) == 0)
     x = np.random.default_rng(4).standard_normal((B, K)).astype(np.float32)
-    x[0] *= 1e5
-    x[1] *= 1e-6
-    x[2, ::2] = 0.0
+    x[0, : K // 2] *= 1e5
+    x[min(1, B - 1), K // 2:] *= 1e-6
+    x[B - 1, ::2] = 0.0
     xbits = O.f32_array_to_bf16_bits(x)
     xf = O.bf16_bits_to_f32_array(xbits).reshape(B, K)
     tw, y = _run(Q, fmt, w, xbits)

@@ -667,16 +667,20 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2)
 }
 
 // ---------------------------------------------------------------------------
-// Batch 1: per-warp streams.
+// Batch 1 (and Q4_0 up to batch 8): per-warp streams.
 //
 // Every warp owns one (16-row tile, k-part) and streams that contiguous run of
 // units through its own ring of shared-memory stages with bulk copies issued
 // by its lane 0; the first stages are requested before the wait for the
 // kernel that produces x, so the weights stream while that kernel finishes.
-// After the wait the warp copies its columns of x into shared memory. Q4_0 codes are decoded to exact bf16 values and multiplied with
-// the bf16 activations as they are (no conversion pass); Q8_0 codes decode to
+// After the wait each warp copies the x columns of its k-part into shared
+// memory (at batch 1 a private copy; for a batch, one copy per k-part shared
+// by the CTA's warps of different tiles). Q4_0 codes are decoded to exact bf16
+// values and multiplied with the bf16 activations as they are (no conversion
+// pass, so a batch up to 8 is one MMA column per row); Q8_0 codes decode to
 // f16 (one PRMT and one HSUB2 per two codes), so the warp converts its x
-// columns to f16 scaled by 2^-e (max|x| * 2^-e in [2^14, 2^15), exact). The
+// columns to f16 scaled by 2^-e (max|x| * 2^-e in [2^14, 2^15), exact) -
+// batch 1 only. The
 // KQ warps of a CTA that share a tile add their partials through shared
 // memory in warp order; with S > 1 the S CTAs of a cluster hold the other
 // k-parts of the same tiles and add through distributed shared memory in CTA
@@ -688,35 +692,39 @@ constexpr int SW_MAX_RING = 4;  // stages per warp ring
 struct StreamArgs {
   const uint8_t *units;  // unit (tile 0, chunk 0)
   const uint32_t *hdr;
-  const uint16_t *x;  // bf16 [K]
+  const uint16_t *x;  // bf16 [B, K]
   void *y;
-  const float *resid;  // optional f32 [N] added in the epilogue
+  const float *resid;  // optional f32 [B, N] added in the epilogue
   int *err;
-  int N, K, n_chunks, y_dtype;
+  int N, K, B, n_chunks, y_dtype;
+  int xs_stride;  // elements per batch row of one k-part's x columns
   int KQ, S;      // warps per tile inside a CTA, CTAs per tile (one cluster)
   int ring;       // stages in each warp's ring
-  int wreg;       // shared-memory bytes of one warp (ring + x columns)
+  int wreg;       // shared-memory bytes of one warp's ring
+  int xoff;       // offset of the x columns (KQ parts x B rows) behind the rings
 };
 
-__device__ __forceinline__ void store_out(const StreamArgs &a, int row, float v) {
-  if (a.resid) v += __ldcg(a.resid + row);
+__device__ __forceinline__ void store_out(const StreamArgs &a, int b, int row, float v) {
+  const size_t o = (size_t)b * a.N + row;
+  if (a.resid) v += __ldcg(a.resid + o);
   if (a.y_dtype == VXB_BF16)
-    ((uint16_t *)a.y)[row] = f32_to_bf16_bits(v);
+    ((uint16_t *)a.y)[o] = f32_to_bf16_bits(v);
   else
-    ((float *)a.y)[row] = v;
+    ((float *)a.y)[o] = v;
 }
 
-// acc[0] = rows g, acc[1] = rows g+8 of the warp's tile (batch column 0 in
-// .x of the lanes with lane % 4 == 0).
-template <int FMT, bool SUBN>
+// acc[0] = rows g, acc[1] = rows g+8 of the warp's tile, batch columns
+// (2q, 2q+1) with q = lane % 4.
+template <int FMT, bool BAT, bool SUBN>
 __device__ __forceinline__ void stream_consume(const StreamArgs &a, const uint8_t *src, uint8_t *ring, uint64_t *full,
                                                const uint16_t *xs, int n_iter, float2 (&acc)[2]) {
   using G = Geo<FMT>;
   constexpr uint32_t STB = CS * G::UNIT;
   const int lane = threadIdx.x & 31;
   acc[0] = acc[1] = make_float2(0.f, 0.f);
-  const bool live = lane < 4;  // the lanes that carry batch column 0 of the B operand
-  const uint16_t *xl = xs + (lane & 3) * 4;
+  const int B = BAT ? a.B : 1;
+  const bool live = (lane >> 2) < B;  // the lanes whose B-operand column is a batch row
+  const uint16_t *xl = xs + (BAT ? (lane >> 2) * a.xs_stride : 0) + (lane & 3) * 4;
   constexpr int BLK = CS * G::BPC;  // blocks per stage
   constexpr int GB = 4;             // blocks per group of independent accumulators
   for (int it = 0; it < n_iter; it++) {
@@ -783,16 +791,21 @@ __device__ __forceinline__ void stream_consume(const StreamArgs &a, const uint8_
   }
 }
 
-template <int FMT>
+// BAT: a batch of 1..8 rows (Q4_0 only) with each k-part's x columns shared
+// by the CTA's warps; otherwise batch 1 with a private copy per warp.
+template <int FMT, bool BAT>
 __global__ void __launch_bounds__(SW_THREADS) gemv_stream_kernel(const StreamArgs a) {
+  static_assert(FMT == 0 || !BAT, "Q8_0 streams batch 1 only");
   using G = Geo<FMT>;
   constexpr uint32_t STB = CS * G::UNIT;  // one stage: CS units of one tile
   constexpr int SPAN = CS * G::CH;        // columns of one stage
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[SW_WARPS][SW_MAX_RING];
-  __shared__ float red[SW_WARPS][16];  // per-warp partials [row]
+  constexpr int RC = BAT ? 8 : 1;           // batch columns kept per row
+  __shared__ float red[SW_WARPS][16][RC];  // per-warp partials [row][batch column]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int RT = SW_WARPS / a.KQ;  // tiles per CTA
+  const int B = BAT ? a.B : 1;
+  const int RT = SW_WARPS / a.KQ;    // tiles per CTA
   const int tile = blockIdx.x * RT + warp / a.KQ;
   const int P = a.KQ * a.S;  // k-parts per tile
   const int part = blockIdx.y * a.KQ + warp % a.KQ;
@@ -800,7 +813,8 @@ __global__ void __launch_bounds__(SW_THREADS) gemv_stream_kernel(const StreamArg
   const int s0 = (int)((long long)part * n_stages / P);
   const int n_iter = (int)((long long)(part + 1) * n_stages / P) - s0;
   uint8_t *ring = smem + (size_t)warp * a.wreg;
-  uint16_t *xs = reinterpret_cast<uint16_t *>(ring + (size_t)a.ring * STB);
+  uint16_t *const xs = BAT ? reinterpret_cast<uint16_t *>(smem + a.xoff) + (size_t)(warp % a.KQ) * B * a.xs_stride
+                           : reinterpret_cast<uint16_t *>(ring + (size_t)a.ring * STB);
   const uint8_t *src = a.units + ((size_t)tile * a.n_chunks + (size_t)s0 * CS) * G::UNIT;
 
   if (lane == 0) {
@@ -818,19 +832,30 @@ __global__ void __launch_bounds__(SW_THREADS) gemv_stream_kernel(const StreamArg
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const bool subnormal = (__ldg(a.hdr + 1) & TILED_FLAG_SUBNORMAL_SCALES) != 0;
 
-  // ---- this warp's x columns [k0, k0 + kr): 16-byte asynchronous copies
-  // through the load/store path and L2 only (the bulk-copy queue is busy with
-  // weights), zeros past K (K and k0 are multiples of 32)
-  const int k0 = s0 * SPAN, kr = n_iter * SPAN;
-  const int kv = max(0, min(kr, a.K - k0));
-  for (int i = lane; i < kr / 8; i += 32) {
-    if (i < kv / 8)
-      cp_async16(xs + i * 8, a.x + k0 + i * 8, 16);
-    else
-      reinterpret_cast<uint4 *>(xs)[i] = make_uint4(0u, 0u, 0u, 0u);
+  // ---- the x columns of this warp's k-part (shared by the RT warps of the
+  // k-part when BAT): 16-byte asynchronous copies through the load/store path
+  // and L2 only (the bulk-copy queue is busy with weights), zeros past K (K
+  // and every part's first column are multiples of 32)
+  {
+    const int k0 = s0 * SPAN, n8 = n_iter * SPAN / 8;
+    const int kv8 = max(0, min(n8, (a.K - k0) / 8));
+    const int i0 = BAT ? (warp / a.KQ) * 32 + lane : lane, di = BAT ? SW_THREADS / a.KQ : 32;
+    for (int b = 0; b < B; b++)
+      for (int i = i0; i < n8; i += di) {
+        uint16_t *dst = xs + (size_t)b * a.xs_stride + i * 8;
+        if (i < kv8)
+          cp_async16(dst, a.x + (size_t)b * a.K + k0 + i * 8, 16);
+        else
+          *reinterpret_cast<uint4 *>(dst) = make_uint4(0u, 0u, 0u, 0u);
+      }
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
-  __syncwarp();
+  // the warps of one k-part share its x columns (KQ is uniform over the CTA)
+  if (!BAT || a.KQ == SW_WARPS)
+    __syncwarp();
+  else
+    __syncthreads();
+  const int kr = n_iter * SPAN;
   int e = 0;
   if (FMT != 0) {
     // f16 operands: e with max|x| * 2^-e in [2^14, 2^15) (0 for all-zero or
@@ -852,29 +877,38 @@ __global__ void __launch_bounds__(SW_THREADS) gemv_stream_kernel(const StreamArg
         w[j] = pack_f16x2(mul_pow2(__uint_as_float(w[j] << 16), -e), mul_pow2(__uint_as_float(w[j] & 0xFFFF0000u), -e));
       *ptr = v;
     }
+    __syncwarp();
   }
-  __syncwarp();
 
   float2 acc[2];
   if (subnormal)
-    stream_consume<FMT, true>(a, src, ring, full[warp], xs, n_iter, acc);
+    stream_consume<FMT, BAT, true>(a, src, ring, full[warp], xs, n_iter, acc);
   else
-    stream_consume<FMT, false>(a, src, ring, full[warp], xs, n_iter, acc);
-  if ((lane & 3) == 0) {
-    red[warp][lane >> 2] = mul_pow2(acc[0].x, e);
-    red[warp][(lane >> 2) + 8] = mul_pow2(acc[1].x, e);
+    stream_consume<FMT, BAT, false>(a, src, ring, full[warp], xs, n_iter, acc);
+  {
+    const int r = lane >> 2, c = (lane & 3) * 2;
+    if (RC > 1) {
+      red[warp][r][c] = acc[0].x;
+      red[warp][r][c + 1] = acc[0].y;
+      red[warp][r + 8][c] = acc[1].x;
+      red[warp][r + 8][c + 1] = acc[1].y;
+    } else if (c == 0) {
+      red[warp][r][0] = mul_pow2(acc[0].x, e);
+      red[warp][r + 8][0] = mul_pow2(acc[1].x, e);
+    }
   }
   __syncthreads();
 
-  // ---- the KQ warps of each tile, in warp order
-  const int nout = RT * 16;  // outputs of this CTA: (tile, row)
+  // ---- the KQ warps of each tile, in warp order; output i = (tile, row, column)
+  const int nout = RT * 16 * B;
   float *cta_sum = reinterpret_cast<float *>(smem);  // the rings are free now
   for (int i = threadIdx.x; i < nout; i += SW_THREADS) {
+    const int rt = i / (16 * B), rr = (i / B) % 16, b = i % B;
     float v = 0.f;
-    for (int q = 0; q < a.KQ; q++) v += red[(i / 16) * a.KQ + q][i % 16];
+    for (int q = 0; q < a.KQ; q++) v += red[rt * a.KQ + q][rr][b];
     if (a.S == 1) {
-      const int row = (blockIdx.x * RT + i / 16) * 16 + i % 16;
-      if (row < a.N) store_out(a, row, v);
+      const int row = (blockIdx.x * RT + rt) * 16 + rr;
+      if (row < a.N) store_out(a, b, row, v);
     } else {
       cta_sum[i] = v;
     }
@@ -890,18 +924,19 @@ __global__ void __launch_bounds__(SW_THREADS) gemv_stream_kernel(const StreamArg
   for (int i = (int)blockIdx.y * per + threadIdx.x; i < i1; i += SW_THREADS) {
     float v = 0.f;
     for (int ss = 0; ss < a.S; ss++) v += *cl.map_shared_rank(cta_sum + i, (unsigned)ss);
-    const int row = (blockIdx.x * RT + i / 16) * 16 + i % 16;
-    if (row < a.N) store_out(a, row, v);
+    const int rt = i / (16 * B), rr = (i / B) % 16, b = i % B;
+    const int row = (blockIdx.x * RT + rt) * 16 + rr;
+    if (row < a.N) store_out(a, b, row, v);
   }
   cluster_sync_all();
 }
 
 struct StreamPlan {
-  int KQ = 0, S = 0, ring = 0, wreg = 0;
+  int KQ = 0, S = 0, ring = 0, wreg = 0, xs_stride = 0;
   size_t smem = 0;
 };
 
-template <int FMT>
+template <int FMT, bool BAT>
 int stream_resident(size_t smem, int cluster, int sms) {
   static std::mutex mu;
   static std::map<std::pair<size_t, int>, int> cache;
@@ -909,7 +944,7 @@ int stream_resident(size_t smem, int cluster, int sms) {
   const auto key = std::make_pair(smem, cluster);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
-  auto kfn = gemv_stream_kernel<FMT>;
+  auto kfn = gemv_stream_kernel<FMT, BAT>;
   int n = 0;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) == cudaSuccess) {
     if (cluster <= 1) {
@@ -944,7 +979,7 @@ int stream_resident(size_t smem, int cluster, int sms) {
 // fewer than 32 warps per SM hide the latency, plus the cost of a cluster
 // reduction (about 1.5 us, some 30 stages of an SM's work) and of each wave
 // beyond the first (its CTAs start streaming only when the first wave ends).
-StreamPlan stream_plan(const vxb_ctx *ctx, const TiledGeom &g) {
+StreamPlan stream_plan(const vxb_ctx *ctx, const TiledGeom &g, int batch) {
   const int sms = ctx->num_sms > 0 ? ctx->num_sms : 148;
   const int n_stages = g.n_chunks / CS;
   const size_t stb = (size_t)CS * (512 + g.sc_per_tile);
@@ -956,15 +991,22 @@ StreamPlan stream_plan(const vxb_ctx *ctx, const TiledGeom &g) {
       const int P = KQ * S;
       if (P > n_stages) continue;
       const int part_max = (n_stages + P - 1) / P;
-      const size_t xbytes = ((size_t)part_max * span * 2 + 127) / 128 * 128;
+      // batch 1: a private x copy behind each warp's ring; a batch: one copy
+      // per k-part behind all rings, rows padded so that stride/2 = 8 (mod
+      // 32) spreads the batch rows over the banks
+      const int xs_stride = batch > 1 ? part_max * span + 16 : 0;
+      const size_t xpriv = batch > 1 ? 0 : ((size_t)part_max * span * 2 + 127) / 128 * 128;
+      const size_t xshared = (size_t)KQ * batch * xs_stride * 2;
       for (int ring = 2; ring <= SW_MAX_RING; ring++) {
         const int rg = std::min(ring, part_max);
         if (rg < ring && ring > 2) break;
-        const size_t wreg = ((size_t)rg * stb + xbytes + 127) / 128 * 128;
-        const size_t cta_sum = (size_t)(SW_WARPS / KQ) * 16 * 4;
-        const size_t smem = std::max((size_t)SW_WARPS * wreg, cta_sum);
+        const size_t wreg = ((size_t)rg * stb + xpriv + 127) / 128 * 128;
+        const size_t cta_sum = (size_t)(SW_WARPS / KQ) * 16 * batch * 4;
+        const size_t smem = std::max((size_t)SW_WARPS * wreg + xshared, cta_sum);
         if (smem > 200 * 1024) continue;
-        const int slots = g.fmt == VXB_Q4_0 ? stream_resident<0>(smem, S, sms) : stream_resident<1>(smem, S, sms);
+        const int slots = g.fmt == VXB_Q8_0 ? stream_resident<1, false>(smem, S, sms)
+                          : batch > 1      ? stream_resident<0, true>(smem, S, sms)
+                                           : stream_resident<0, false>(smem, S, sms);
         if (slots < 1) continue;
         const int ctas = g.n_tiles / (SW_WARPS / KQ) * S;
         const int waves = (ctas + slots - 1) / slots;
@@ -979,6 +1021,7 @@ StreamPlan stream_plan(const vxb_ctx *ctx, const TiledGeom &g) {
           best.S = S;
           best.ring = rg;
           best.wreg = (int)wreg;
+          best.xs_stride = xs_stride;
           best.smem = smem;
         }
       }
@@ -987,9 +1030,9 @@ StreamPlan stream_plan(const vxb_ctx *ctx, const TiledGeom &g) {
   return best;
 }
 
-template <int FMT>
+template <int FMT, bool BAT>
 int stream_launch_t(vxb_ctx *ctx, const StreamArgs &a, dim3 grid, size_t smem, cudaStream_t st, bool pdl) {
-  auto kfn = gemv_stream_kernel<FMT>;
+  auto kfn = gemv_stream_kernel<FMT, BAT>;
   static bool configured[64] = {false};
   const int dev = ctx->device & 63;
   if (!configured[dev]) {
@@ -1021,11 +1064,18 @@ int stream_launch_t(vxb_ctx *ctx, const StreamArgs &a, dim3 grid, size_t smem, c
   return VXB_OK;
 }
 
-// y = W x (+ resid) for one activation row through the per-warp stream kernel.
-int stream_gemv(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const uint16_t *d_x, int y_dtype, void *d_y,
-                const float *d_resid, int *d_err, cudaStream_t st, bool pdl, const char *who) {
+// Batches the per-warp stream kernel takes: Q4_0 multiplies bf16 activations
+// directly, one MMA column per row up to 8 (past batch 4 the group-CTA kernel
+// is faster on 7B shapes); Q8_0 rescales its f16 activations per k-part and
+// runs batch 1 only.
+bool stream_eligible(int fmt, int batch) { return batch == 1 || (fmt == VXB_Q4_0 && batch <= 4); }
+
+// y = W x (+ resid) through the per-warp stream kernel: batch 1, or Q4_0 up
+// to batch 8 (one B-operand column per activation row).
+int stream_gemv(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const uint16_t *d_x, int batch,
+                int y_dtype, void *d_y, const float *d_resid, int *d_err, cudaStream_t st, bool pdl, const char *who) {
   const TiledGeom g = tiled_geom(fmt, N, K);
-  const StreamPlan p = stream_plan(ctx, g);
+  const StreamPlan p = stream_plan(ctx, g, batch);
   if (p.KQ == 0) return set_error(ctx, VXB_EINVAL, "%s: no launch plan fits N=%d K=%d", who, N, K);
   StreamArgs a;
   const uint8_t *base = (const uint8_t *)d_tiled;
@@ -1037,15 +1087,19 @@ int stream_gemv(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const 
   a.err = d_err;
   a.N = N;
   a.K = K;
+  a.B = batch;
   a.n_chunks = g.n_chunks;
   a.y_dtype = y_dtype;
+  a.xs_stride = p.xs_stride;
   a.KQ = p.KQ;
   a.S = p.S;
   a.ring = p.ring;
   a.wreg = p.wreg;
+  a.xoff = SW_WARPS * p.wreg;
   const dim3 grid(g.n_tiles / (SW_WARPS / p.KQ), p.S);
-  return fmt == VXB_Q4_0 ? stream_launch_t<0>(ctx, a, grid, p.smem, st, pdl)
-                         : stream_launch_t<1>(ctx, a, grid, p.smem, st, pdl);
+  if (fmt == VXB_Q8_0) return stream_launch_t<1, false>(ctx, a, grid, p.smem, st, pdl);
+  return batch > 1 ? stream_launch_t<0, true>(ctx, a, grid, p.smem, st, pdl)
+                   : stream_launch_t<0, false>(ctx, a, grid, p.smem, st, pdl);
 }
 
 size_t smem_bytes_t(int fmt, int NT, int batch, int xs_stride) {
@@ -1250,10 +1304,10 @@ int gemv_launch(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const 
   if (((uintptr_t)d_tiled) % 256) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q: tiled weights must be 256-byte aligned");
   if (((uintptr_t)d_x) % 16) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q: activations must be 16-byte aligned");
   if (int rc = use_device(ctx)) return rc;
-  if (batch == 1 && !plan_override) {
+  if (stream_eligible(fmt, batch) && !plan_override) {
     if (int rc = ws_reserve(ctx, 0, 0)) return rc;  // device error word
-    return stream_gemv(ctx, fmt, d_tiled, N, K, d_x, y_dtype, d_y, d_resid, ctx->d_err, (cudaStream_t)stream, true,
-                       "vxb_gemv_q");
+    return stream_gemv(ctx, fmt, d_tiled, N, K, d_x, batch, y_dtype, d_y, d_resid, ctx->d_err, (cudaStream_t)stream,
+                       true, "vxb_gemv_q");
   }
   const TiledGeom g = tiled_geom(fmt, N, K);
   GemvPlan p = plan_override ? *plan_override : gemv_plan(ctx, fmt, N, K, batch);
@@ -1382,8 +1436,8 @@ VXB_API int vxb_gemv_q_static(vxb_ctx *ctx, int fmt, const void *d_tiled, int N,
   if (int rc = use_device(ctx)) return rc;
   uint8_t *base = nullptr;
   if (int rc = static_scratch(ctx, &base)) return rc;
-  if (batch == 1)  // the per-warp stream kernel needs no scratch beyond the error word
-    return stream_gemv(ctx, fmt, d_tiled, N, K, d_x, y_dtype, d_y, nullptr,
+  if (stream_eligible(fmt, batch))  // the per-warp stream kernel needs no scratch beyond the error word
+    return stream_gemv(ctx, fmt, d_tiled, N, K, d_x, batch, y_dtype, d_y, nullptr,
                        (int *)(base + kStaticPartialBytes + (size_t)kStaticCounters * 4), (cudaStream_t)stream, false,
                        "vxb_gemv_q_static");
   GemvPlan p = gemv_plan(ctx, fmt, N, K, batch);
