@@ -1,0 +1,49 @@
+"""K1 batches 9-32 through the tcgen05 kernel (opt-in with VXB_GEMV_TCGEN05=1)
+vs the CPU oracle. The switch is read once per process, so the checks run in
+a child process with it set. Tolerance as for the other GEMV paths: max
+relative error (floored at 1e-3 of max|y|) <= 1e-3 for f32 output.
+"""
+import os
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+CHILD = r'''
+import numpy as np, torch
+from oracle import oracle as O
+from tests.parity import rel_err
+from vortex_b200 import quant as Q
+OFMT = {2: O.GGML_Q4_0, 8: O.GGML_Q8_0}
+fails = []
+for fmt in (2, 8):
+    for (N, K) in ((1000, 160), (300, 4096), (11008, 4096), (4096, 11008)):
+        for B in (9, 17, 32):
+            rng = np.random.default_rng(N + K + B)
+            w = rng.normal(0.0, 0.02, (N, K)).astype(np.float32)
+            x = rng.standard_normal((B, K)).astype(np.float32)
+            xbits = O.f32_array_to_bf16_bits(x)
+            xf = O.bf16_bits_to_f32_array(xbits).reshape(B, K)
+            tw = Q.TiledWeight.from_float(torch.from_numpy(w).cuda(), fmt)
+            xd = torch.from_numpy(xbits.view(np.int16)).cuda().view(torch.bfloat16).reshape(B, K)
+            y = tw.gemv(xd).float().cpu().numpy()
+            blocks = O.quantize_blocks(OFMT[fmt], w.astype(np.float64))
+            ref = O.gemv_blocks(OFMT[fmt], blocks, N, K, xf.astype(np.float64))
+            for b in range(B):
+                e = rel_err(y[b], ref[b])
+                if not e <= 1e-3:
+                    fails.append((fmt, N, K, B, b, float(e)))
+print("FAILS", fails)
+assert not fails
+'''
+
+
+def test_gemv_tcgen05_matches_oracle(cuda_ok):
+    env = dict(os.environ, VXB_GEMV_TCGEN05="1")
+    r = subprocess.run([sys.executable, "-c", CHILD], cwd=ROOT, env=env, capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
