@@ -82,7 +82,6 @@ struct Geo {
   static constexpr int BWP = (BW + 1023) / 1024 * 1024;
   static constexpr int NXB = BCS * CH / XBOX_K;  // x boxes per stage (Q4_0 2, Q8_0 1)
   static constexpr int BSTG = BWP + NXB * XBOX_BYTES;
-  static constexpr int XSTR = CS * CH + 16;  // elements per batch row of a stage's x slice
 };
 
 // Activations: batches up to 8 (XF16) stage the split's x once as f16 scaled
