@@ -37,7 +37,7 @@ extern "C" {
 #define VXB_ETIMEOUT (-4)    /* a bounded device-side wait ran out */
 #define VXB_EFORMAT (-5)     /* malformed GGUF data */
 #define VXB_ENOBLOCKS (-6)   /* KV cache out of blocks */
-#define VXB_EUNSUPPORTED (-7)/* valid request this build does not handle */
+#define VXB_EUNSUPPORTED (-7)/* valid request the library does not handle */
 #define VXB_ENCCL (-8)       /* NCCL error */
 
 /* weight block formats: the GGML type ids of gguf_loader.rs GGMLQuantType

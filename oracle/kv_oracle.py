@@ -4,7 +4,7 @@ Pure-Python restatement of the block allocator of the reference's
 PagedKVCache (src/kv_cache.rs:29-93): a free stack initialised to
 (0..max_blocks).rev(), one block table per (layer, seq_id), a block popped
 when a table is empty or its last block is full, free_seq pushing every block
-of the sequence back. Values are tracked as Python lists for the checker.
+of the sequence back. Values are tracked as Python lists.
 """
 from __future__ import annotations
 

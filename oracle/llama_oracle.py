@@ -7,7 +7,7 @@ driven one token per step with a KV cache (as the .vx kv_cache_* helpers,
 734-846), using the C oracle for the arithmetic. Weights are the dequantized
 GGUF blocks the device holds. Where the device stores a value in bf16 (the
 inputs of every projection, q/k/v after RoPE, the attention output), the
-checker rounds the same value to bf16 (tensor_engine::f32_to_bf16 rule), so
+oracle rounds the same value to bf16 (tensor_engine::f32_to_bf16 rule), so
 both sides see identical operands at those points.
 """
 from __future__ import annotations

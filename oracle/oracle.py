@@ -3,7 +3,8 @@
 numpy wrappers over oracle/_build/libvxo.so, the plain-C restatement of the
 reference's CPU arithmetic (MangoByteLabs/vortex, Rust). Only tests/,
 __graft_entry__.smoke() and bench.py's CPU baseline / reference arm use this
-module, as the checker; the product (vortex_b200) never imports it.
+module, as the reference to compare against; the product (vortex_b200) never
+imports it.
 """
 from __future__ import annotations
 

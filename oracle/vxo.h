@@ -5,7 +5,8 @@
  * arithmetic of the reference (MangoByteLabs/vortex, Rust) for the path that
  * the vortex_b200 CUDA kernels replace. It is used by tests/, by
  * __graft_entry__.smoke() and by bench.py's cpu_baseline / reference arm as
- * the checker and the CPU baseline -- never by the product path.
+ * the reference to compare against and the CPU baseline -- never by the
+ * product path.
  *
  * Every function cites the reference file:line it follows. Loop orders are
  * kept as in the reference so f64 results are reproducible.

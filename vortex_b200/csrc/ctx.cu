@@ -112,7 +112,7 @@ VXB_API int vxb_init(int device, vxb_ctx **out) {
   if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetDeviceProperties");
   if (prop.major != 10)
     return set_error(nullptr, VXB_EUNSUPPORTED,
-                     "vxb_init: device %d is sm_%d%d; this build targets sm_100a (B200)", device,
+                     "vxb_init: device %d is sm_%d%d; the library is compiled for sm_100a (B200)", device,
                      prop.major, prop.minor);
   vxb_ctx *ctx = new vxb_ctx();
   ctx->device = device;
