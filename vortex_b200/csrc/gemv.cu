@@ -6,31 +6,40 @@
 // matmul_f64 890-902) and the matmul of Linear::forward
 // (src/transformer.rs:332-352) at decode batch sizes.
 //
-// Design (HBM-bound streaming):
+// Two kernels (the tcgen05 kernel for batches 9-32 is in gemv_tc.cu, opt-in):
+//  * gemv_stream_kernel - batch 1, and Q4_0 batches 2-4: every warp streams
+//    one (16-row tile, k-part) through its own ring of bulk copies (see the
+//    comment at the kernel).
+//  * gemv_q_kernel - the other batches, the group-CTA design below.
+//
+// Group-CTA design (HBM-bound streaming):
 //  * A CTA owns one 128-row group (8 sixteen-row tiles, one per consumer warp)
-//    and a k-range. The tiled layout stores every (row group, k-chunk) as one
-//    contiguous record of codes and scales, so a producer warp moves a whole
-//    stage (CS records) with a single cp.async.bulk copy into a ring of
-//    shared-memory stages (one mbarrier per stage with a transaction count).
+//    and a k-range. The tiled layout stores every (tile, k-chunk) as one
+//    contiguous unit of codes and scales, and a tile's chunks back to back,
+//    so a producer warp moves a stage (CS units of each of the 8 tiles) with 8
+//    cp.async.bulk copies into a ring of shared-memory stages (one mbarrier
+//    per stage with a transaction count).
 //  * Consumer warps read their tile's codes with one 16-byte LDS per lane per
 //    chunk (the slice is the lane's m16n8k16 A fragments) and turn them into
-//    exact f16 integers: Q4_0 nibbles by LOP3 with the f16 magic 1024 (a nibble
-//    at bits 0-3 gives 1024+n, at bits 4-7 1024+16n) and one HSUB2 per two
-//    codes; Q8_0 bytes (stored as q+128) by one PRMT with the magic byte and one
-//    HSUB2 per two codes.
-//  * The activations of the CTA's k-range are staged in shared memory as f16,
-//    each batch column multiplied by a power of two 2^-e chosen from its largest
-//    magnitude (max |x| * 2^-e in [2^14, 2^15)), so the bf16 -> f16 conversion is
-//    exact for every element within 2^-28 of the column maximum and nothing
-//    overflows; the f32 result is multiplied back by 2^e.
-//  * mma.m16n8k16 (f16 x f16 -> f32) forms the per-block dot products; the
+//    exact integers: for batch <= 8 f16 (Q4_0 nibbles by LOP3 with the f16
+//    magic 1024 and one HSUB2 per two codes; Q8_0 bytes, stored as q+128, by
+//    one PRMT with the magic byte and one HSUB2 per two codes), for larger
+//    batches bf16.
+//  * Batch <= 8: the activations of the CTA's k-range are staged once as f16,
+//    each batch column multiplied by a power of two 2^-e chosen from its
+//    largest magnitude (max |x| * 2^-e in [2^14, 2^15)), so the bf16 -> f16
+//    conversion is exact for every element within 2^-28 of the column maximum
+//    and nothing overflows; the f32 result is multiplied back by 2^e. Larger
+//    batches carry their unchanged bf16 x slice in every stage as 2-D TMA
+//    boxes with a 128-byte swizzle.
+//  * mma.m16n8k16 (f32 accumulate) forms the per-block dot products; the
 //    per-(row, block) f16 scale multiplies that f32 block partial with packed
-//    f32x2 FMAs, so scales never round into the operands (Q4_0 rows decoded as
-//    16q carry 1/16 in their scale, an exact factor).
-//  * Split-K across CTAs with a deterministic reduction: each CTA writes its
-//    f32 partial and the last CTA of a row group (counter in global memory)
-//    sums the partials in split order and applies the epilogue; the counter is
-//    returned to zero.
+//    f32x2 FMAs, so scales never round into the operands.
+//  * Split-K across CTAs with a deterministic reduction: the splits of a row
+//    group form a cluster and add through distributed shared memory in split
+//    order, or (more than 8 splits) each CTA writes its f32 partial and the
+//    last CTA of a row group (counter in global memory) sums the partials in
+//    split order; the counter is returned to zero.
 //  * The producer issues weight copies before any dependency on the kernel
 //    that produces x, so under programmatic dependent launch the weight stream
 //    overlaps the producer kernel's tail. Every mbarrier wait is bounded
@@ -47,6 +56,7 @@
 #include <cuda_fp16.h>
 
 #include "gemv.h"
+#include "gemv_common.h"
 #include "tc_common.h"
 #include "tiled_layout.h"
 #include "vxb_internal.h"
@@ -56,34 +66,6 @@ namespace cg = cooperative_groups;
 
 namespace {
 
-constexpr int CWARPS = 8;                   // consumer warps (one 16-row tile each)
-constexpr int THREADS = (CWARPS + 1) * 32;  // + one producer warp
-constexpr int ROWS_PER_CTA = CWARPS * 16;
-constexpr int STAGES = 3;
-constexpr int CS = 4;  // chunks (units of a tile) per stage
-// batches above 8: stages of 2 chunks in a 6-deep ring (the same shared
-// memory, twice the look-ahead), each stage's activations as 2-D TMA boxes
-// of 64 columns x B rows with 128-byte swizzle
-constexpr int BCS = 2;
-constexpr int BSTAGES = 6;
-constexpr int XBOX_K = 64;              // columns per activation box (128 bytes)
-constexpr int XBOX_BYTES = 32 * 128;    // one box, rows padded to 32 (a 1024-byte multiple)
-constexpr int kMaxClusterSplits = 8;  // portable cluster size
-
-template <int FMT>
-struct Geo {
-  static constexpr int CH = FMT == 0 ? 64 : 32;     // k per chunk
-  static constexpr int BPC = CH / 32;               // 32-element blocks per chunk
-  static constexpr int SCT = 8 * BPC * 4;           // scale bytes of one (tile, chunk) unit
-  static constexpr int UNIT = 512 + SCT;            // bytes of one (tile, chunk) unit
-  static constexpr int STAGE = CWARPS * CS * UNIT;  // a 128-row group's CS chunks
-  // batch path: weights of one stage (1024-byte aligned) + its x boxes
-  static constexpr int BW = CWARPS * BCS * UNIT;
-  static constexpr int BWP = (BW + 1023) / 1024 * 1024;
-  static constexpr int NXB = BCS * CH / XBOX_K;  // x boxes per stage (Q4_0 2, Q8_0 1)
-  static constexpr int BSTG = BWP + NXB * XBOX_BYTES;
-};
-
 // Activations: batches up to 8 (XF16) stage the split's x once as f16 scaled
 // per batch column by 2^-e; larger batches carry an unchanged bf16 x slice in
 // every stage (no prologue, shared memory independent of K).
@@ -91,7 +73,6 @@ template <int NT>
 struct XMode {
   static constexpr bool F16 = NT == 1;
 };
-static_assert(Geo<0>::UNIT == 512 + 64 && Geo<1>::UNIT == 512 + 32, "unit size");
 
 struct GemvArgs {
   const uint8_t *records;
@@ -105,180 +86,6 @@ struct GemvArgs {
   int N, K, B, NP, n_chunks, S, y_dtype, xs_stride;
   int cluster;  // 1: the S splits of a row group are one thread-block cluster
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-
-// raise the transaction count without arriving
-__device__ __forceinline__ void mbar_expect_tx_only(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-// Bounded wait for the phase of the given parity; false after ~2^31 cycles.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-  const uint32_t a = smem_u32(bar);
-  const long long t0 = clock64();
-  while (true) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if (clock64() - t0 > (1ll << 31)) return false;
-  }
-}
-
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t m, uint32_t o) {
-  uint32_t d;
-  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(m), "r"(o));
-  return d;
-}
-
-__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
-// Q4_0 tiled word -> A fragment {a0a1, a2a3, a4a5, a6a7}. Rows g (a0a1, a4a5)
-// come out as the exact codes q, rows g+8 (a2a3, a6a7) as 16q.
-__device__ __forceinline__ void decode_q4(uint32_t w, uint32_t A[4]) {
-  const uint32_t M = 0x64006400u;       // f16 1024.0 x2
-  const uint32_t SUB_LO = 0x64086408u;  // 1024 + 8
-  const uint32_t SUB_HI = 0x64806480u;  // 1024 + 16 * 8
-  const uint32_t w8 = w >> 8;
-  A[0] = hsub2(lop_and_or(w, 0x000F000Fu, M), SUB_LO);
-  A[1] = hsub2(lop_and_or(w, 0x00F000F0u, M), SUB_HI);
-  A[2] = hsub2(lop_and_or(w8, 0x000F000Fu, M), SUB_LO);
-  A[3] = hsub2(lop_and_or(w8, 0x00F000F0u, M), SUB_HI);
-}
-
-// Q8_0 tiled words (bytes q+128) -> A fragment of exact codes: f16 0x64uu is
-// 1024 + u, minus 1152.
-__device__ __forceinline__ void decode_q8(uint32_t w0, uint32_t w1, uint32_t A[4]) {
-  const uint32_t M = 0x64646464u;
-  const uint32_t SUB = 0x64806480u;  // 1024 + 128
-  A[0] = hsub2(__byte_perm(w0, M, 0x4140), SUB);
-  A[1] = hsub2(__byte_perm(w0, M, 0x4342), SUB);
-  A[2] = hsub2(__byte_perm(w1, M, 0x4140), SUB);
-  A[3] = hsub2(__byte_perm(w1, M, 0x4342), SUB);
-}
-
-__device__ __forceinline__ uint32_t bsub2(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  uint32_t d;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-  return d;
-}
-
-// bf16 operands (batches above 8, activations staged unchanged). Q4_0: nibble
-// n at bits 0-3 / 16-19 of (w >> 4i) gives bf16 0x4300|n = 128+n, minus 136:
-// the exact codes of every row.
-__device__ __forceinline__ void decode_q4_bf16(uint32_t w, uint32_t A[4]) {
-  const uint32_t M = 0x43004300u;    // bf16 128.0 x2
-  const uint32_t SUB = 0x43084308u;  // bf16 136.0 x2
-  A[0] = bsub2(lop_and_or(w, 0x000F000Fu, M), SUB);
-  A[1] = bsub2(lop_and_or(w >> 4, 0x000F000Fu, M), SUB);
-  A[2] = bsub2(lop_and_or(w >> 8, 0x000F000Fu, M), SUB);
-  A[3] = bsub2(lop_and_or(w >> 12, 0x000F000Fu, M), SUB);
-}
-
-// Q8_0 bytes u = q+128 -> f32 2^23+u by PRMT, minus 2^23+128, packed to bf16
-// (exact: |q| <= 128)
-__device__ __forceinline__ void q8_word_bf16(uint32_t w, uint32_t &lo, uint32_t &hi) {
-  const float Bm = 8388736.0f;  // 2^23 + 128
-  const float c0 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440)) - Bm;
-  const float c1 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7441)) - Bm;
-  const float c2 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7442)) - Bm;
-  const float c3 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7443)) - Bm;
-  lo = pack_bf16x2(c0, c1);
-  hi = pack_bf16x2(c2, c3);
-}
-
-__device__ __forceinline__ void decode_q8_bf16(uint32_t w0, uint32_t w1, uint32_t A[4]) {
-  q8_word_bf16(w0, A[0], A[1]);
-  q8_word_bf16(w1, A[2], A[3]);
-}
-
-__device__ __forceinline__ void mma_bf16(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ void mma_bf16_z(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
-      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
-}
-
-__device__ __forceinline__ void mma_f16(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// the same with a zero accumulator input
-__device__ __forceinline__ void mma_f16_z(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
-      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
-}
-
-__device__ __forceinline__ float2 decode_scales(uint32_t s, bool subnormal) {
-  if (!subnormal) {
-    __half2 h = *reinterpret_cast<__half2 *>(&s);
-    return __half22float2(h);
-  }
-  return make_float2(ref_f16_to_f32(s & 0xFFFFu), ref_f16_to_f32(s >> 16));
-}
-
-__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
-  uint32_t d;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-  return d;
-}
-
-// v * 2^e for |e| <= 252: two exact power-of-two factors (exact unless the
-// result leaves the f32 range)
-__device__ __forceinline__ float mul_pow2(float v, int e) {
-  const int e1 = e / 2, e2 = e - e1;
-  return v * __int_as_float((127 + e1) << 23) * __int_as_float((127 + e2) << 23);
-}
-
-__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc, int src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc), "r"(src_bytes));
-}
-
-// all threads of every CTA of the cluster (release / acquire)
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
 
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(CWARPS * 32) : "memory"); }
 
@@ -1113,27 +920,6 @@ size_t smem_bytes_t(int fmt, int NT, int batch, int xs_stride) {
 
 // Tensor map of the activations x [B, K] bf16 for the batch path: boxes of
 // 64 columns x B rows, 128-byte swizzle, columns past K read as zero.
-using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_tiled_fn() {
-  static std::mutex mu;
-  static EncodeTiledFn fn = nullptr;
-  std::lock_guard<std::mutex> lk(mu);
-  if (!fn) {
-    void *p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess || !p) {
-      cudaGetLastError();
-      return nullptr;
-    }
-    fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
-  return fn;
-}
-
 int x_tensor_map(vxb_ctx *ctx, const uint16_t *x, int B, int K, CUtensorMap *map) {
   const EncodeTiledFn fn = encode_tiled_fn();
   if (!fn) return set_error(ctx, VXB_ECUDA, "vxb_gemv_q: cuTensorMapEncodeTiled is not available from the driver");
@@ -1254,621 +1040,6 @@ int launch_t(vxb_ctx *ctx, const GemvArgs &a, dim3 grid, size_t smem, cudaStream
 }
 
 
-// ---------------------------------------------------------------------------
-// Batches 9-32: tcgen05 skinny GEMM (opt-in: VXB_GEMV_TCGEN05=1).
-//
-// A CTA owns one 128-row group (8 tiles) and a k-range of whole weight stages
-// (qps quads of 4 chunks of each tile). Per 64-column step the group's codes become the A
-// operand of tcgen05.mma in tensor memory: exact small integers as bf16,
-// written by the decode warp of each TMEM lane quadrant q (tiles 2q, 2q+1)
-// with tcgen05.st.16x256b, whose register layout (thread t: lanes t/4 and
-// t/4+8, columns 2(t%4) and 2(t%4)+1) is the m16n8k16 A fragment the tiled
-// units already hold, with the units' k permutation lining the fragment up
-// with the matrix columns. x is the 128-byte-swizzled K-major B operand [NB
-// rows x 64 columns] (rows past the batch and columns past K zero), copied by
-// one warp with 16-byte cp.async through the load/store path: a TMA load
-// would queue behind the CTA's ~200 KB of weight bulk copies (measured: ~6 us
-// per x stage instead of ~1). Each
-// 32-column block accumulates into its own NB TMEM columns (two M=128 x N=NB
-// x K=16 MMAs), so the epilogue multiplies the block's f32 sums by the f16
-// block scales (acc += d * D, in block order) as the mma.sync kernels do: the
-// scales never round into an operand.
-//
-// The weights of a stage (qps quads of 4 chunks of each of the 8 tiles, 18 or
-// 37 KB) arrive by one 3-D TMA load over the tiled layout viewed as [tiles]
-// [chunks][unit words]: issuing eight bulk copies of 1-2 KB per stage from one
-// thread held a CTA to ~7 GB/s.
-// Warps: 0 weight producer (issued before the wait for the previous kernel),
-// 1 TMEM allocation and MMA issue, 2 x producer,
-// 3-6 decode (lane quadrants 3, 0, 1, 2), 7-10 epilogue (quadrants 3, 0, 1, 2).
-// S > 1 CTAs of a row group form a cluster and add their partial sums through
-// distributed shared memory in CTA order.
-constexpr int TC_THREADS = 352;
-constexpr int TC_AR = 4;   // A slots in TMEM (32 columns = 64 bf16 codes per row each)
-constexpr int TC_DR = 2;   // accumulator slots (2 blocks x NB columns each)
-constexpr int TC_SR = 8;   // scale slots in shared memory (one step each)
-constexpr int TC_XR = 8;   // x stages (one step each)
-constexpr int TC_XLAG = 4;  // x steps in flight (cp.async groups) before the oldest is published
-constexpr int TC_MAX_WR = 24;
-constexpr uint32_t TC_COLS = 256, TC_ACOL = 0, TC_DCOL = 128;
-constexpr int TC_SMEM_MAX = 225 * 1024;  // dynamic shared memory (the barriers are static)
-
-struct TcArgs {
-  const uint8_t *units;  // unit (tile 0, chunk 0)
-  const uint32_t *hdr;
-  const uint16_t *x;  // bf16 [B, K]
-  void *y;
-  const float *resid;  // optional f32 [B, N]
-  int *err;
-  int N, K, B, n_chunks, y_dtype;
-  int wr;     // weight stages in the ring
-  int qps;    // quads (4 chunks) per weight stage
-  int n_wst;  // weight stages over the padded k range (the last may reach past it: zeros)
-  int S;      // CTAs per row group (cluster along y)
-};
-
-template <int FMT>
-struct TcGeo {
-  static constexpr int UNIT = Geo<FMT>::UNIT;
-  static constexpr int SPQ = FMT == 0 ? 4 : 2;  // 64-column steps per quad of 4 chunks
-  __host__ __device__ static constexpr int wsb(int qps) { return 8 * 4 * qps * UNIT; }  // one weight stage
-};
-
-template <int NB>
-struct TcSmem {
-  static constexpr int XB = NB * 128;  // one x stage: NB rows x 64 bf16
-  static constexpr int X_OFF = 0;
-  static constexpr int W_OFF = TC_XR * XB;
-  __host__ __device__ static size_t sc_off(int wsb, int wr) { return (size_t)W_OFF + (size_t)wsb * wr; }
-  __host__ __device__ static size_t red_off(int wsb, int wr) { return sc_off(wsb, wr) + (size_t)TC_SR * 2 * 128 * 4; }
-  __host__ __device__ static size_t bytes(int wsb, int wr, int S) {
-    return red_off(wsb, wr) + (S > 1 ? (size_t)NB * 128 * 4 : 0) + 1024;  // + 1024: base alignment
-  }
-};
-
-__device__ __forceinline__ void tmem_st_16x256b_x4(uint32_t taddr, const uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.16x256b.x4.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-          taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
-}
-
-template <int NB>
-__device__ __forceinline__ void tmem_ld_nb(uint32_t taddr, float (&v)[NB]) {
-  if constexpr (NB == 32)
-    vxb::tc::tmem_ld32(taddr, v);
-  else
-    tmem_ld16(taddr, v);
-}
-
-// bounded wait that records a failure once and then stops waiting
-__device__ __forceinline__ void tc_wait(uint64_t *bar, uint32_t parity, bool &ok, int *err) {
-  if (ok && !mbar_wait(bar, parity)) {
-    ok = false;
-    atomicExch(err, 1);
-  }
-}
-
-// the same for all lanes of a warp, with a warp-uniform outcome (the lanes
-// stay converged for the elected arrivals)
-__device__ __forceinline__ void tc_wait_warp(uint64_t *bar, uint32_t parity, bool &ok, int *err) {
-  bool mine = ok;
-  if (mine && !mbar_wait(bar, parity)) mine = false;
-  const bool all = __all_sync(0xffffffffu, mine);
-  if (ok && !all && (threadIdx.x & 31) == 0) atomicExch(err, 1);
-  ok = all;
-}
-
-// one arrival per warp: the lanes' prior accesses are ordered before it by
-// the warp barrier (32 arrivals on one mbarrier serialize for ~1 us)
-__device__ __forceinline__ void warp_arrive(uint64_t *bar) {
-  __syncwarp();
-  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
-}
-
-// The 16x256b.x4 registers of one tile for one 64-column step: k16 step s
-// holds {row g: k 4q..4q+1, row g: 4q+2..4q+3, row g+8: 4q..4q+1, row g+8:
-// 4q+2..4q+3} = fragment pairs {a0a1, a4a5, a2a3, a6a7}.
-template <int FMT>
-__device__ __forceinline__ void tc_decode_tile(const uint8_t *u0, const uint8_t *u1, int lane, uint32_t (&r)[16]) {
-  const uint4 c0 = *reinterpret_cast<const uint4 *>(u0 + lane * 16);
-  if (FMT == 0) {
-    const uint32_t w[4] = {c0.x, c0.y, c0.z, c0.w};
-#pragma unroll
-    for (int s = 0; s < 4; s++) {
-      uint32_t A[4];
-      decode_q4_bf16(w[s], A);
-      r[4 * s + 0] = A[0];
-      r[4 * s + 1] = A[2];
-      r[4 * s + 2] = A[1];
-      r[4 * s + 3] = A[3];
-    }
-  } else {
-    const uint4 c1 = *reinterpret_cast<const uint4 *>(u1 + lane * 16);
-    const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-    for (int s = 0; s < 4; s++) {
-      uint32_t A[4];
-      decode_q8_bf16(w[2 * s], w[2 * s + 1], A);
-      r[4 * s + 0] = A[0];
-      r[4 * s + 1] = A[2];
-      r[4 * s + 2] = A[1];
-      r[4 * s + 3] = A[3];
-    }
-  }
-}
-
-// one x step [NB rows x 64 columns] into a 128-byte-swizzled stage: 16-byte
-// chunk c of row r at r * 128 + ((c ^ (r % 8)) * 16); zeros past B and K
-template <int NB>
-__device__ __forceinline__ void tc_x_step(const TcArgs &a, uint8_t *dst, int k0, int lane) {
-#pragma unroll
-  for (int i = 0; i < NB * 8 / 32; i++) {
-    const int idx = lane + 32 * i, r = idx >> 3, c = idx & 7;
-    const bool in = r < a.B && k0 + c * 8 < a.K;
-    const uint16_t *src = in ? a.x + (size_t)r * a.K + k0 + c * 8 : a.x;
-    cp_async16(dst + r * 128 + ((c ^ (r & 7)) << 4), src, in ? 16 : 0);
-  }
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-
-template <int FMT, int NB>
-__global__ void __launch_bounds__(TC_THREADS, 1)
-    gemv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const TcArgs a) {
-  using TG = TcGeo<FMT>;
-  using SM = TcSmem<NB>;
-  constexpr int UNIT = TG::UNIT;
-  const int WSTEPS = a.qps * TG::SPQ, WSB = TG::wsb(a.qps), TBYTES = 4 * a.qps * UNIT;  // TBYTES: one tile's part
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint8_t *xring = sm + SM::X_OFF;
-  uint8_t *wring = sm + SM::W_OFF;
-  float *sc = reinterpret_cast<float *>(sm + SM::sc_off(WSB, a.wr));  // [TC_SR][2][128]
-  float *red = reinterpret_cast<float *>(sm + SM::red_off(WSB, a.wr));  // [NB][128] (S > 1)
-  __shared__ __align__(8) uint64_t wfull[TC_MAX_WR], wempty[TC_MAX_WR], xfull[TC_XR], xempty[TC_XR];
-  __shared__ __align__(8) uint64_t afull[TC_AR], aempty[TC_AR], dfull[TC_DR], dempty[TC_DR];
-  __shared__ __align__(8) uint64_t sfull[TC_SR], sempty[TC_SR], mdone;
-  __shared__ uint32_t tmem_base_s;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int grp = blockIdx.x;
-  const int ws0 = (int)((long long)blockIdx.y * a.n_wst / a.S);
-  const int nws = (int)((long long)(blockIdx.y + 1) * a.n_wst / a.S) - ws0;
-  const int nsteps = nws * WSTEPS;
-
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
-                 "r"(TC_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < a.wr; i++) {
-      mbar_init(&wfull[i], 1);
-      mbar_init(&wempty[i], 4);
-    }
-    for (int i = 0; i < TC_XR; i++) {
-      mbar_init(&xfull[i], 1);
-      mbar_init(&xempty[i], 1);
-    }
-    for (int i = 0; i < TC_AR; i++) {
-      mbar_init(&afull[i], 4);
-      mbar_init(&aempty[i], 1);
-    }
-    for (int i = 0; i < TC_DR; i++) {
-      mbar_init(&dfull[i], 1);
-      mbar_init(&dempty[i], 4);
-    }
-    for (int i = 0; i < TC_SR; i++) {
-      mbar_init(&sfull[i], 4);
-      mbar_init(&sempty[i], 4);
-    }
-    mbar_init(&mdone, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  vxb::tc::tc_fence_before();
-  __syncthreads();
-  vxb::tc::tc_fence_after();
-  const uint32_t tmem = tmem_base_s;
-  asm volatile("griddepcontrol.launch_dependents;");
-  bool ok = true;
-
-  if (warp == 0) {
-    // ---------------- weights: one TMA box [8 tiles][4 qps chunks][unit] per
-    // stage. The whole warp waits (a lone spinning lane beside 31 lanes parked
-    // at a warp barrier woke ~1 us after its barrier completed); lane 0 issues.
-    for (int ws = 0; ws < nws; ws++) {
-      const int slot = ws % a.wr;
-      if (ws >= a.wr) tc_wait_warp(&wempty[slot], ((ws / a.wr) - 1) & 1, ok, a.err);
-      if (!ok) break;
-      if (lane == 0) {
-        mbar_expect_tx(&wfull[slot], WSB);
-        vxb::tc::tma_load_3d(wring + (size_t)slot * WSB, &wmap, 0, (ws0 + ws) * 4 * a.qps, grp * 8, &wfull[slot]);
-      }
-      __syncwarp();
-    }
-    // copies still in flight finish before the CTA exits
-    for (int ws = max(0, nws - a.wr); ws < nws; ws++) {
-      bool dr = true;
-      tc_wait_warp(&wfull[ws % a.wr], (ws / a.wr) & 1, dr, a.err);
-    }
-  } else if (warp == 2) {
-    // ---------------- x: per step 16-byte cp.async of all 32 lanes (one
-    // commit group); step st - TC_XLAG is published once its group landed
-    // (cp.async.wait_group, then a proxy fence: the MMA reads it through the
-    // async proxy)
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int k0 = ws0 * WSTEPS * 64;
-    int issued = 0;
-    for (int st = 0; st < nsteps; st++) {
-      const int slot = st % TC_XR;
-      if (st >= TC_XR) tc_wait_warp(&xempty[slot], ((st / TC_XR) - 1) & 1, ok, a.err);
-      if (!ok) break;
-      tc_x_step<NB>(a, xring + slot * SM::XB, k0 + st * 64, lane);
-      issued = st + 1;
-      if (st >= TC_XLAG) {
-        asm volatile("cp.async.wait_group %0;" ::"n"(TC_XLAG) : "memory");
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        warp_arrive(&xfull[(st - TC_XLAG) % TC_XR]);
-      }
-    }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    for (int st = max(0, issued - TC_XLAG); st < issued; st++) warp_arrive(&xfull[st % TC_XR]);
-  } else if (warp == 1) {
-    // ---------------- MMA: per step, blocks b = 0, 1 into accumulator slot
-    // columns [b * NB, b * NB + NB), two K=16 MMAs each; the warp waits, lane 0
-    // issues
-    constexpr uint32_t ID = vxb::tc::idesc_bf16(128, NB, false);
-    for (int st = 0; st < nsteps; st++) {
-      const int as = st % TC_AR, xs = st % TC_XR, ds = st % TC_DR;
-      tc_wait_warp(&afull[as], (st / TC_AR) & 1, ok, a.err);
-      tc_wait_warp(&xfull[xs], (st / TC_XR) & 1, ok, a.err);
-      if (st >= TC_DR) tc_wait_warp(&dempty[ds], ((st / TC_DR) - 1) & 1, ok, a.err);
-      if (!ok) break;
-      vxb::tc::tc_fence_after();
-      if (lane == 0) {
-        const uint32_t xa = smem_u32(xring + xs * SM::XB);
-#pragma unroll
-        for (int b = 0; b < 2; b++)
-#pragma unroll
-          for (int k = 0; k < 2; k++)
-            vxb::tc::umma_bf16_ts(tmem + TC_DCOL + ds * 2 * NB + b * NB, tmem + TC_ACOL + as * 32 + (2 * b + k) * 8,
-                                  vxb::tc::sw128_desc(xa + (2 * b + k) * 32, 16, 1024), ID, k);
-        vxb::tc::umma_commit(&aempty[as]);
-        vxb::tc::umma_commit(&xempty[xs]);
-        vxb::tc::umma_commit(&dfull[ds]);
-      }
-      __syncwarp();
-    }
-    if (lane == 0) vxb::tc::umma_commit(&mdone);  // every MMA issued above has completed
-    __syncwarp();
-    bool dr = true;
-    tc_wait_warp(&mdone, 0, dr, a.err);
-  } else if (warp <= 6) {
-    // ---------------- decode: TMEM lane quadrant q = warp % 4, tiles 2q, 2q+1
-    const int q = warp & 3;
-    const bool subn = (__ldg(a.hdr + 1) & TILED_FLAG_SUBNORMAL_SCALES) != 0;
-    // this lane's scales go to the epilogue row 32q + lane: tile 2q + lane/16,
-    // row pair (lane % 16) % 8, half (lane % 16) / 8
-    const int je = 2 * q + (lane >> 4), pi = (lane & 15) & 7, ph = (lane & 15) >> 3;
-    for (int st = 0; st < nsteps; st++) {
-      const int ws = st / WSTEPS, sub = st % WSTEPS, wslot = ws % a.wr;
-      const int as = st % TC_AR, ss = st % TC_SR;
-      if (sub == 0) tc_wait_warp(&wfull[wslot], (ws / a.wr) & 1, ok, a.err);
-      if (st >= TC_AR) tc_wait_warp(&aempty[as], ((st / TC_AR) - 1) & 1, ok, a.err);
-      if (st >= TC_SR) tc_wait_warp(&sempty[ss], ((st / TC_SR) - 1) & 1, ok, a.err);
-      if (!ok) break;
-      vxb::tc::tc_fence_after();
-      const uint8_t *stg = wring + (size_t)wslot * WSB;
-      // Q4_0: unit `sub` of the tile (4 k16 steps); Q8_0: units 2 sub, 2 sub + 1 (2 each)
-      const int u0 = FMT == 0 ? sub : 2 * sub;
-      const uint8_t *t0 = stg + (2 * q) * TBYTES + u0 * UNIT;
-      const uint8_t *t1 = stg + (2 * q + 1) * TBYTES + u0 * UNIT;
-      uint32_t r0[16], r1[16];
-      tc_decode_tile<FMT>(t0, t0 + UNIT, lane, r0);
-      tc_decode_tile<FMT>(t1, t1 + UNIT, lane, r1);
-      float s0, s1;
-      {
-        const uint8_t *ue = stg + je * TBYTES + u0 * UNIT + 512;
-        uint32_t w0, w1;
-        if (FMT == 0) {
-          const uint2 t = *reinterpret_cast<const uint2 *>(ue + pi * 8);
-          w0 = t.x;
-          w1 = t.y;
-        } else {
-          w0 = *reinterpret_cast<const uint32_t *>(ue + pi * 4);
-          w1 = *reinterpret_cast<const uint32_t *>(ue + UNIT + pi * 4);
-        }
-        const float2 d0 = decode_scales(w0, subn), d1 = decode_scales(w1, subn);
-        s0 = ph ? d0.y : d0.x;
-        s1 = ph ? d1.y : d1.x;
-      }
-      if (sub == WSTEPS - 1) warp_arrive(&wempty[wslot]);  // the warp's reads of the stage are done
-      const uint32_t ta = tmem + TC_ACOL + as * 32 + ((uint32_t)(32 * q) << 16);
-      tmem_st_16x256b_x4(ta, r0);
-      tmem_st_16x256b_x4(ta + (16u << 16), r1);
-      sc[(ss * 2 + 0) * 128 + 32 * q + lane] = s0;
-      sc[(ss * 2 + 1) * 128 + 32 * q + lane] = s1;
-      vxb::tc::tmem_wait_st();
-      vxb::tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&afull[as]);
-        mbar_arrive(&sfull[ss]);
-      }
-    }
-  } else {
-    // ---------------- epilogue: row 32q + lane of the group, all NB columns
-    const int q = warp & 3;
-    const int row = grp * 128 + 32 * q + lane;
-    float acc[NB];
-#pragma unroll
-    for (int n = 0; n < NB; n++) acc[n] = 0.f;
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    for (int st = 0; st < nsteps; st++) {
-      const int ds = st % TC_DR, ss = st % TC_SR;
-      tc_wait_warp(&dfull[ds], (st / TC_DR) & 1, ok, a.err);
-      tc_wait_warp(&sfull[ss], (st / TC_SR) & 1, ok, a.err);
-      if (!ok) break;
-      vxb::tc::tc_fence_after();
-      float v0[NB], v1[NB];
-      const uint32_t td = tmem + TC_DCOL + ds * 2 * NB + ((uint32_t)(32 * q) << 16);
-      tmem_ld_nb<NB>(td, v0);
-      tmem_ld_nb<NB>(td + NB, v1);
-      vxb::tc::tmem_wait_ld();
-      vxb::tc::tc_fence_before();
-      const float s0 = sc[(ss * 2 + 0) * 128 + 32 * q + lane];
-      const float s1 = sc[(ss * 2 + 1) * 128 + 32 * q + lane];
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&dempty[ds]);
-        mbar_arrive(&sempty[ss]);
-      }
-#pragma unroll
-      for (int n = 0; n < NB; n++) acc[n] = fmaf(s1, v1[n], fmaf(s0, v0[n], acc[n]));
-    }
-    if (a.S == 1) {
-      if (row < a.N)
-#pragma unroll
-        for (int n = 0; n < NB; n++) {
-          if (n >= a.B) break;
-          const size_t o = (size_t)n * a.N + row;
-          float v = acc[n];
-          if (a.resid) v += __ldcg(a.resid + o);
-          if (a.y_dtype == VXB_BF16)
-            ((uint16_t *)a.y)[o] = f32_to_bf16_bits(v);
-          else
-            ((float *)a.y)[o] = v;
-        }
-    } else {
-#pragma unroll
-      for (int n = 0; n < NB; n++) red[n * 128 + 32 * q + lane] = acc[n];
-    }
-  }
-
-  if (a.S > 1) {
-    // ---- the S CTAs of the row group: CTA c sums a slice of the outputs over
-    // the peers in CTA order; nobody exits before all reads are done
-    cluster_sync_all();
-    cg::cluster_group cl = cg::this_cluster();
-    const int nout = a.B * 128;
-    const int per = (nout + a.S - 1) / a.S;
-    const int i1 = min(nout, ((int)blockIdx.y + 1) * per);
-    asm volatile("griddepcontrol.wait;" ::: "memory");  // before the first global write of this thread
-    for (int i = (int)blockIdx.y * per + threadIdx.x; i < i1; i += TC_THREADS) {
-      const int n = i >> 7, rr = i & 127;
-      float v = 0.f;
-      for (int s = 0; s < a.S; s++) v += *cl.map_shared_rank(red + n * 128 + rr, (unsigned)s);
-      const int row = grp * 128 + rr;
-      if (row < a.N) {
-        const size_t o = (size_t)n * a.N + row;
-        if (a.resid) v += __ldcg(a.resid + o);
-        if (a.y_dtype == VXB_BF16)
-          ((uint16_t *)a.y)[o] = f32_to_bf16_bits(v);
-        else
-          ((float *)a.y)[o] = v;
-      }
-    }
-    cluster_sync_all();
-  }
-  vxb::tc::tc_fence_before();
-  __syncthreads();
-  vxb::tc::tc_fence_after();
-  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_COLS));
-}
-
-struct TcPlan {
-  int S = 0, wr = 0, qps = 0, n_wst = 0;
-  size_t smem = 0;
-};
-
-template <int FMT, int NB>
-int tc_resident(size_t smem, int cluster, int sms) {
-  static std::mutex mu;
-  static std::map<std::pair<size_t, int>, int> cache;
-  std::lock_guard<std::mutex> lk(mu);
-  const auto key = std::make_pair(smem, cluster);
-  auto it = cache.find(key);
-  if (it != cache.end()) return it->second;
-  auto kfn = gemv_tc_kernel<FMT, NB>;
-  int n = 0;
-  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_MAX) == cudaSuccess) {
-    if (cluster <= 1) {
-      int per_sm = 0;
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, TC_THREADS, smem) == cudaSuccess)
-        n = per_sm * sms;
-    } else {
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(1, cluster);
-      cfg.blockDim = dim3(TC_THREADS);
-      cfg.dynamicSmemBytes = smem;
-      cudaLaunchAttribute attr;
-      attr.id = cudaLaunchAttributeClusterDimension;
-      attr.val.clusterDim.x = 1;
-      attr.val.clusterDim.y = cluster;
-      attr.val.clusterDim.z = 1;
-      cfg.attrs = &attr;
-      cfg.numAttrs = 1;
-      int clusters = 0;
-      if (cudaOccupancyMaxActiveClusters(&clusters, kfn, &cfg) == cudaSuccess) n = clusters * cluster;
-    }
-  }
-  if (n < 1) {
-    cudaGetLastError();
-    n = 0;
-  }
-  cache[key] = n;
-  return n;
-}
-
-// k-splits S and ring depth: the time is the larger of the whole weight
-// stream at the HBM rate and the busiest SM's share at a per-SM rate of about
-// 120 GB/s, plus about 0.5 us for a cluster reduction and 1 us per extra
-// wave. When the CTAs need two per SM, each ring is sized so that two fit.
-template <int FMT, int NB>
-TcPlan tc_plan_t(const vxb_ctx *ctx, const TiledGeom &g) {
-  const int sms = ctx->num_sms > 0 ? ctx->num_sms : 148;
-  const int n_quads = g.n_chunks / 4;
-  TcPlan best;
-  double best_cost = 1e30;
-  for (int qps : {2, 1})
-  for (int S : {1, 2, 4, 8}) {
-    const int wsb = TcGeo<FMT>::wsb(qps);
-    const int n_wst = (n_quads + qps - 1) / qps;
-    if (S > n_wst) break;
-    const int ctas = g.n_groups * S;
-    const int per_cta = (n_wst + S - 1) / S;
-    const int per_sm = std::min(2, (ctas + sms - 1) / sms);
-    const size_t budget = per_sm == 1 ? TC_SMEM_MAX : 112 * 1024;
-    const size_t fixed = TcSmem<NB>::bytes(wsb, 0, S);
-    if (fixed + 2 * (size_t)wsb > budget) continue;
-    const int wr = std::min({TC_MAX_WR, per_cta, (int)((budget - fixed) / wsb)});
-    if (wr < 1) continue;
-    const size_t smem = TcSmem<NB>::bytes(wsb, wr, S);
-    const int slots = tc_resident<FMT, NB>(smem, S, sms);
-    if (slots < 1) continue;
-    const int waves = (ctas + slots - 1) / slots;
-    const double t_hbm = (double)ctas * per_cta * wsb / 6.5e6;
-    const double t_sm = (double)((ctas + sms - 1) / sms) * per_cta * wsb / 1.2e5;
-    const double cost = std::max(t_hbm, t_sm) + (S > 1 ? 0.5 : 0.0) + 1.0 * (waves - 1);
-    if (cost < best_cost - 1e-9) {
-      best_cost = cost;
-      best.S = S;
-      best.wr = wr;
-      best.qps = qps;
-      best.n_wst = n_wst;
-      best.smem = smem;
-    }
-  }
-  return best;
-}
-
-// The tiled units as a 3-D u32 tensor [tiles][chunks][unit words]: boxes of
-// 8 tiles x 4 qps chunks x one unit (chunks past the padded k range read as
-// zero bytes: codes with scale 0).
-int weights_tensor_map(vxb_ctx *ctx, const uint8_t *units, const TiledGeom &g, int qps, CUtensorMap *map) {
-  const EncodeTiledFn fn = encode_tiled_fn();
-  if (!fn) return set_error(ctx, VXB_ECUDA, "vxb_gemv_q: cuTensorMapEncodeTiled is not available from the driver");
-  cuuint64_t dims[3] = {(cuuint64_t)(g.unit / 4), (cuuint64_t)g.n_chunks, (cuuint64_t)g.n_tiles};
-  cuuint64_t strides[2] = {(cuuint64_t)g.unit, (cuuint64_t)g.n_chunks * g.unit};
-  cuuint32_t box[3] = {(cuuint32_t)(g.unit / 4), (cuuint32_t)(4 * qps), 8};
-  cuuint32_t estr[3] = {1, 1, 1};
-  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint8_t *>(units), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q: weight tensor map failed (%d)", (int)r);
-  return VXB_OK;
-}
-
-template <int FMT, int NB>
-int tc_launch_t(vxb_ctx *ctx, const TcArgs &a0, const TiledGeom &g, cudaStream_t st, bool pdl) {
-  auto kfn = gemv_tc_kernel<FMT, NB>;
-  const TcPlan p = tc_plan_t<FMT, NB>(ctx, g);
-  if (p.S == 0) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q: no tensor-core launch plan fits N=%d K=%d", a0.N, a0.K);
-  CUtensorMap wmap;
-  if (int rc = weights_tensor_map(ctx, a0.units, g, p.qps, &wmap)) return rc;
-  static bool configured[64] = {false};
-  const int dev = ctx->device & 63;
-  if (!configured[dev]) {
-    VXB_CUDA_TRY(ctx, cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_MAX));
-    configured[dev] = true;
-  }
-  TcArgs a = a0;
-  a.wr = p.wr;
-  a.qps = p.qps;
-  a.n_wst = p.n_wst;
-  a.S = p.S;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(g.n_groups, p.S);
-  cfg.blockDim = dim3(TC_THREADS);
-  cfg.dynamicSmemBytes = p.smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[2];
-  int na = 0;
-  if (pdl) {
-    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[na].val.programmaticStreamSerializationAllowed = 1;
-    na++;
-  }
-  if (p.S > 1) {
-    attr[na].id = cudaLaunchAttributeClusterDimension;
-    attr[na].val.clusterDim.x = 1;
-    attr[na].val.clusterDim.y = p.S;
-    attr[na].val.clusterDim.z = 1;
-    na++;
-  }
-  cfg.attrs = attr;
-  cfg.numAttrs = na;
-  VXB_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, kfn, wmap, a));
-  return VXB_OK;
-}
-
-// y = W x (+ resid) for batches 9..32 through the tcgen05 kernel.
-int tc_gemv(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const uint16_t *d_x, int batch, int y_dtype,
-            void *d_y, const float *d_resid, int *d_err, cudaStream_t st, bool pdl) {
-  const TiledGeom g = tiled_geom(fmt, N, K);
-  TcArgs a = {};
-  const uint8_t *base = (const uint8_t *)d_tiled;
-  a.units = base + g.codes_off;
-  a.hdr = (const uint32_t *)base;
-  a.x = d_x;
-  a.y = d_y;
-  a.resid = d_resid;
-  a.err = d_err;
-  a.N = N;
-  a.K = K;
-  a.B = batch;
-  a.n_chunks = g.n_chunks;
-  a.y_dtype = y_dtype;
-  if (fmt == VXB_Q4_0)
-    return batch <= 16 ? tc_launch_t<0, 16>(ctx, a, g, st, pdl) : tc_launch_t<0, 32>(ctx, a, g, st, pdl);
-  return batch <= 16 ? tc_launch_t<1, 16>(ctx, a, g, st, pdl) : tc_launch_t<1, 32>(ctx, a, g, st, pdl);
-}
-
-// The tensor-core kernel is exact and parity-tested but not yet faster than
-// the group-CTA kernel (a fixed ~0.8 us per 64-column step), so batches 9-32
-// take it only when the process sets VXB_GEMV_TCGEN05=1.
-bool tc_enabled() {
-  static const bool on = [] {
-    const char *v = getenv("VXB_GEMV_TCGEN05");
-    return v && v[0] == '1';
-  }();
-  return on;
-}
-
-bool tc_eligible(int batch) { return tc_enabled() && batch >= 9 && batch <= 32; }
 
 }  // namespace
 
@@ -1925,9 +1096,9 @@ int gemv_launch(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const 
   if (((uintptr_t)d_tiled) % 256) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q: tiled weights must be 256-byte aligned");
   if (((uintptr_t)d_x) % 16) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q: activations must be 16-byte aligned");
   if (int rc = use_device(ctx)) return rc;
-  if (tc_eligible(batch) && !plan_override) {
+  if (gemv_tc_eligible(batch) && !plan_override) {
     if (int rc = ws_reserve(ctx, 0, 0)) return rc;  // device error word
-    return tc_gemv(ctx, fmt, d_tiled, N, K, d_x, batch, y_dtype, d_y, d_resid, ctx->d_err, (cudaStream_t)stream, true);
+    return gemv_tc(ctx, fmt, d_tiled, N, K, d_x, batch, y_dtype, d_y, d_resid, ctx->d_err, (cudaStream_t)stream, true);
   }
   if (stream_eligible(fmt, batch) && !plan_override) {
     if (int rc = ws_reserve(ctx, 0, 0)) return rc;  // device error word
@@ -2061,8 +1232,8 @@ VXB_API int vxb_gemv_q_static(vxb_ctx *ctx, int fmt, const void *d_tiled, int N,
   if (int rc = use_device(ctx)) return rc;
   uint8_t *base = nullptr;
   if (int rc = static_scratch(ctx, &base)) return rc;
-  if (tc_eligible(batch))  // the tensor-core kernel needs no scratch beyond the error word
-    return tc_gemv(ctx, fmt, d_tiled, N, K, d_x, batch, y_dtype, d_y, nullptr,
+  if (gemv_tc_eligible(batch))  // the tensor-core kernel needs no scratch beyond the error word
+    return gemv_tc(ctx, fmt, d_tiled, N, K, d_x, batch, y_dtype, d_y, nullptr,
                    (int *)(base + kStaticPartialBytes + (size_t)kStaticCounters * 4), (cudaStream_t)stream, false);
   if (stream_eligible(fmt, batch))  // the per-warp stream kernel needs no scratch beyond the error word
     return stream_gemv(ctx, fmt, d_tiled, N, K, d_x, batch, y_dtype, d_y, nullptr,
