@@ -918,21 +918,6 @@ size_t smem_bytes_t(int fmt, int NT, int batch, int xs_stride) {
   return std::max((size_t)STAGES * stage, red) + (size_t)std::min(batch, 8 * NT) * xs_stride * 2;
 }
 
-// Tensor map of the activations x [B, K] bf16 for the batch path: boxes of
-// 64 columns x B rows, 128-byte swizzle, columns past K read as zero.
-int x_tensor_map(vxb_ctx *ctx, const uint16_t *x, int B, int K, CUtensorMap *map) {
-  const EncodeTiledFn fn = encode_tiled_fn();
-  if (!fn) return set_error(ctx, VXB_ECUDA, "vxb_gemv_q: cuTensorMapEncodeTiled is not available from the driver");
-  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)B};
-  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  cuuint32_t box[2] = {(cuuint32_t)XBOX_K, (cuuint32_t)B};
-  cuuint32_t estr[2] = {1, 1};
-  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t *>(x), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q: cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return VXB_OK;
-}
 
 int xs_stride_for(int kc_max) { return kc_max + 16; }  // stride/2 = 8 (mod 32): conflict-free 8-byte loads
 
