@@ -23,7 +23,8 @@ def _ptr(t):
 
 
 @pytest.mark.parametrize("fmt_name,N,K,B", [("Q4_0", 4096, 4096, 1), ("Q8_0", 11008, 4096, 4),
-                                            ("Q4_0", 4096, 11008, 32), ("Q8_0", 1000, 160, 3)])
+                                            ("Q4_0", 4096, 11008, 32), ("Q8_0", 1000, 160, 3),
+                                            ("Q4_0", 11008, 4096, 3)])
 def test_static_scratch_gemv_matches_allocating_gemv(cuda_ok, fmt_name, N, K, B):
     from vortex_b200 import _native as NAT
     from vortex_b200 import quant as Q
