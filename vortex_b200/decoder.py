@@ -26,6 +26,72 @@ LLAMA_7B = dict(vocab_size=32000, dim=4096, n_layers=32, n_heads=32, n_kv_heads=
 WQ, WK, WV, WO, W1, W2, W3, LN1_W, LN1_B, LN2_W, LN2_B = range(11)
 EMBED, FINAL_W, FINAL_B, OUTPUT = range(4)
 
+# Llama-style GGUF tensor names (llama.cpp convention) of the linear slots
+GGUF_LINEARS = {"attn_q": WQ, "attn_k": WK, "attn_v": WV, "attn_output": WO, "ffn_gate": W1, "ffn_down": W2,
+                "ffn_up": W3}
+
+
+def _bf16_bits(x: np.ndarray) -> np.ndarray:
+    """f32 -> bf16 bit patterns, round to nearest even by adding 0x7FFF plus
+    the kept lowest bit (the tensor_engine::f32_to_bf16 rule)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    return (((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFFFFFF) >> 16).astype(np.uint16)
+
+
+def gguf_decoder_weights(f, cfg: dict) -> list:
+    """(layer, slot, host array) for every weight of a decoder with config cfg
+    (vocab_size, dim, n_layers, n_heads, n_kv_heads, ffn_dim, weight_fmt) from
+    an open GGUFFile with llama.cpp tensor names: blk.{i}.attn_q/attn_k/attn_v/
+    attn_output/ffn_gate/ffn_down/ffn_up.weight as blocks of the decoder's
+    weight format (dims [in, out]), blk.{i}.attn_norm/ffn_norm.weight (+
+    optional .bias) and output_norm.weight (+ .bias) as F32 or F16 (a missing
+    bias is zero), token_embd.weight F32/F16 [vocab, dim] (stored as bf16) and
+    output.weight blocks [vocab, dim]. Raises ValueError naming the tensor on a
+    missing tensor, a wrong type or wrong dims."""
+    from . import gguf as G
+    d, ffn, V, L = cfg["dim"], cfg["ffn_dim"], cfg["vocab_size"], cfg["n_layers"]
+    kvd = cfg["n_kv_heads"] * (d // cfg["n_heads"])
+    fmt = cfg["weight_fmt"]
+    have = {t["name"]: t for t in f.tensors()}
+
+    def info(name, dims, types):
+        t = have.get(name)
+        if t is None:
+            raise ValueError(f"GGUF tensor '{name}' is missing")
+        if t["type"] not in types:
+            raise ValueError(f"GGUF tensor '{name}' has ggml type {t['type']}, expected one of {sorted(types)}")
+        if t["dims"] != dims:
+            raise ValueError(f"GGUF tensor '{name}' has dims {t['dims']}, expected {dims}")
+        return t
+
+    def floats(name, n, optional=False):
+        if optional and name not in have:
+            return np.zeros(n, dtype=np.float32)
+        t = info(name, [n], (G.GGML_F32, G.GGML_F16))
+        raw = f.tensor_bytes(name)
+        return (raw.view(np.float32) if t["type"] == G.GGML_F32 else raw.view(np.float16).astype(np.float32)).copy()
+
+    out = []
+    shapes = {WQ: [d, d], WK: [d, kvd], WV: [d, kvd], WO: [d, d], W1: [d, ffn], W2: [ffn, d], W3: [d, ffn]}
+    for i in range(L):
+        for stem, slot in GGUF_LINEARS.items():
+            name = f"blk.{i}.{stem}.weight"
+            info(name, shapes[slot], (fmt,))
+            out.append((i, slot, f.tensor_bytes(name)))
+        out.append((i, LN1_W, floats(f"blk.{i}.attn_norm.weight", d)))
+        out.append((i, LN1_B, floats(f"blk.{i}.attn_norm.bias", d, optional=True)))
+        out.append((i, LN2_W, floats(f"blk.{i}.ffn_norm.weight", d)))
+        out.append((i, LN2_B, floats(f"blk.{i}.ffn_norm.bias", d, optional=True)))
+    t = info("token_embd.weight", [d, V], (G.GGML_F32, G.GGML_F16))
+    raw = f.tensor_bytes("token_embd.weight")
+    emb = raw.view(np.float32) if t["type"] == G.GGML_F32 else raw.view(np.float16).astype(np.float32)
+    out.append((-1, EMBED, _bf16_bits(emb.reshape(V, d))))
+    out.append((-1, FINAL_W, floats("output_norm.weight", d)))
+    out.append((-1, FINAL_B, floats("output_norm.bias", d, optional=True)))
+    info("output.weight", [d, V], (fmt,))
+    out.append((-1, OUTPUT, f.tensor_bytes("output.weight")))
+    return out
+
 
 class Decoder:
     """comm (optional): a vortex_b200.comm.Comm; the decoder is then this
@@ -70,6 +136,17 @@ class Decoder:
         a = np.ascontiguousarray(data)
         self._check(N.lib().vxb_decoder_set_weight(self.ptr, layer, which, a.ctypes.data_as(ctypes.c_void_p),
                                                    a.nbytes))
+
+    def load_gguf(self, source):
+        """Load every weight from a Llama-style GGUF (a path, bytes or an open
+        gguf.GGUFFile; tensor names and formats as gguf_decoder_weights)."""
+        from . import gguf as G
+        f = source if isinstance(source, G.GGUFFile) else G.GGUFFile(source)
+        c = self.cfg
+        cfg = dict(vocab_size=c.vocab_size, dim=c.dim, n_layers=c.n_layers, n_heads=c.n_heads,
+                   n_kv_heads=c.n_kv_heads, ffn_dim=c.ffn_dim, weight_fmt=c.weight_fmt)
+        for layer, which, a in gguf_decoder_weights(f, cfg):
+            self.set_weight(layer, which, a)
 
     def step(self, seq_ids, tokens, want_logits: bool = False):
         ids = np.ascontiguousarray(seq_ids, dtype=np.int64)
