@@ -12,7 +12,6 @@ both sides see identical operands at those points.
 """
 from __future__ import annotations
 
-import math
 
 import numpy as np
 
