@@ -12,7 +12,6 @@ both sides see identical operands at those points.
 """
 from __future__ import annotations
 
-
 import numpy as np
 
 from . import oracle as O
