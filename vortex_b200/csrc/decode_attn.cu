@@ -18,6 +18,7 @@
 // last-arriving CTA of each (sequence, kv head) (counter in global memory).
 // int8 caches stage int8 pages and one f32 scale per (token, head); the K
 // scale multiplies the scores and the V scale is folded into P.
+#include <atomic>
 #include <cuda_bf16.h>
 
 #include "decode_attn.h"
@@ -411,7 +412,7 @@ int launch_t(vxb_ctx *ctx, const DecodeArgs &a, cudaStream_t st) {
   using SM = Smem<D, INT8>;
   const size_t merge = (size_t)WARPS * 16 * D * 4 + 2 * WARPS * 16 * 4;
   const size_t smem = SM::TOTAL > merge ? SM::TOTAL : merge;
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // kernel attributes set on this device (zero-initialized)
   if (!configured[ctx->device & 63]) {
     VXB_CUDA_TRY(ctx, cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     configured[ctx->device & 63] = true;

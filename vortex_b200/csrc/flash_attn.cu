@@ -30,6 +30,7 @@
 //    read the current S, so it overlaps their exponentials.
 // Every mbarrier wait is bounded (clock64); a timeout sets the context's
 // device error word and the kernel runs to completion. No multicast.
+#include <atomic>
 #include <cuda.h>
 #include <cuda_bf16.h>
 
@@ -351,7 +352,7 @@ int make_map(vxb_ctx *ctx, EncodeTiledFn fn, CUtensorMap *map, const void *base,
 template <bool CAUSAL>
 int launch(vxb_ctx *ctx, const CUtensorMap &q, const CUtensorMap &k, const CUtensorMap &v, const FlashArgs &a,
            cudaStream_t st) {
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // kernel attributes set on this device (zero-initialized)
   const int dev = ctx->device & 63;
   if (!configured[dev]) {
     VXB_CUDA_TRY(ctx, cudaFuncSetAttribute(flash_fwd_kernel<CAUSAL>, cudaFuncAttributeMaxDynamicSharedMemorySize,

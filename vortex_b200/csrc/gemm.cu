@@ -25,6 +25,7 @@
 //    residual.
 // Every mbarrier wait is bounded; a timeout sets the context's device error
 // word and the kernel runs to completion.
+#include <atomic>
 #include <cuda.h>
 #include <cuda_fp16.h>
 
@@ -326,7 +327,7 @@ int gemm_q_launch(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, cons
   CUtensorMap mx, mw;
   if (int rc = make_map(ctx, fn, &mx, d_x, M, K, BM)) return rc;
   if (int rc = make_map(ctx, fn, &mw, wt, terms * N, K, BN)) return rc;
-  static bool configured[64][2] = {{false}};
+  static std::atomic<bool> configured[64][2];  // kernel attributes set on this device (zero-initialized)
   if (!configured[ctx->device & 63][terms - 2]) {
     if (terms == 2)
       VXB_CUDA_TRY(ctx, cudaFuncSetAttribute(gemm_terms_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -46,6 +46,7 @@
 //    (clock64); a timeout sets the context's device error word and the kernel
 //    runs to completion.
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -840,7 +841,7 @@ StreamPlan stream_plan(const vxb_ctx *ctx, const TiledGeom &g, int batch) {
 template <int FMT, bool BAT>
 int stream_launch_t(vxb_ctx *ctx, const StreamArgs &a, dim3 grid, size_t smem, cudaStream_t st, bool pdl) {
   auto kfn = gemv_stream_kernel<FMT, BAT>;
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // kernel attributes set on this device (zero-initialized)
   const int dev = ctx->device & 63;
   if (!configured[dev]) {
     VXB_CUDA_TRY(ctx, cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
@@ -993,7 +994,7 @@ int launch_t(vxb_ctx *ctx, const GemvArgs &a, dim3 grid, size_t smem, cudaStream
   memset(&xmap, 0, sizeof(xmap));
   if (NT > 1)
     if (int rc = x_tensor_map(ctx, a.x, a.B, a.K, &xmap)) return rc;
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // kernel attributes set on this device (zero-initialized)
   const int dev = ctx->device & 63;
   if (!configured[dev]) {
     VXB_CUDA_TRY(ctx, cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));

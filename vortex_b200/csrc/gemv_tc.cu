@@ -3,6 +3,7 @@
 // into tensor memory as the MMA's A operand. Opt-in (VXB_GEMV_TCGEN05=1)
 // until it is faster than the group-CTA kernel of gemv.cu.
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -556,7 +557,7 @@ int tc_launch_t(vxb_ctx *ctx, const TcArgs &a0, const TiledGeom &g, cudaStream_t
   if (p.S == 0) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q: no tensor-core launch plan fits N=%d K=%d", a0.N, a0.K);
   CUtensorMap wmap;
   if (int rc = weights_tensor_map(ctx, a0.units, g, p.qps, &wmap)) return rc;
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // kernel attributes set on this device (zero-initialized)
   const int dev = ctx->device & 63;
   if (!configured[dev]) {
     VXB_CUDA_TRY(ctx, cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_MAX));
