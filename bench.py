@@ -382,9 +382,10 @@ def main():
     barrier(ws)
 
     # dequant-GEMV sweep (weights 4096x4096, 11008x4096, 4096x11008; Q4_0 and
-    # Q8_0; batch 1, 4, 16), each over rotating weight copies > 2x L2
+    # Q8_0; batch 1, 4, 16), each over rotating weight copies > 2x L2; one GPU
+    # (with N > 1 the other ranks would idle at the barrier meanwhile)
     gemv = None
-    if rank == 0 and not args.no_gemv_sweep:
+    if rank == 0 and ws == 1 and not args.no_gemv_sweep:
         from vortex_b200 import kernel_bench as KB
         rows = KB.gemv_sweep()
         gemv = {"unit": "GB/s", "peak": hbm, "peak_source": peak_src,
@@ -393,8 +394,8 @@ def main():
                            "achieved": round(r["GBps"], 1), "frac": round(r["GBps"] / hbm, 3)} for r in rows]}
         gemv["best_frac"] = max(c["frac"] for c in gemv["cases"])
 
-    cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    cpu = None  # the CPU baseline runs at N = 1 only
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         per_step, desc = cpu_layer_sample(1, B)
         cpu = {"value": B / per_step, "unit": "tokens/s", "cores": 1, "kind": "port", "sample": desc}
 
