@@ -475,7 +475,8 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2)
 }
 
 // ---------------------------------------------------------------------------
-// Batch 1 (and Q4_0 up to batch 8): per-warp streams.
+// Batch 1, and Q4_0 batches 2-4 (routing: stream_eligible): per-warp streams.
+// The kernel handles Q4_0 batches up to 8; past 4 the group kernel is faster.
 //
 // Every warp owns one (16-row tile, k-part) and streams that contiguous run of
 // units through its own ring of shared-memory stages with bulk copies issued
@@ -488,9 +489,8 @@ __global__ void __launch_bounds__(THREADS, NT <= 2 ? 3 : 2)
 // pass, so a batch up to 8 is one MMA column per row); Q8_0 codes decode to
 // f16 (one PRMT and one HSUB2 per two codes), so the warp converts its x
 // columns to f16 scaled by 2^-e (max|x| * 2^-e in [2^14, 2^15), exact) -
-// batch 1 only. The
-// KQ warps of a CTA that share a tile add their partials through shared
-// memory in warp order; with S > 1 the S CTAs of a cluster hold the other
+// batch 1 only. The KQ warps of a CTA that share a tile add their partials
+// through shared memory in warp order; with S > 1 the S CTAs of a cluster hold the other
 // k-parts of the same tiles and add through distributed shared memory in CTA
 // order. No global scratch, deterministic sums.
 constexpr int SW_WARPS = 8;
