@@ -10,10 +10,18 @@ prefilled in one pass per sequence (prefill GEMM + flash attention).
 
 Prints one JSON line (rank 0). With torchrun (N > 1) the ranks run one
 tensor-parallel decoder (heads, FFN rows and vocabulary split over the N GPUs,
-NCCL all-reduce of the residual stream twice per layer): the batch is the same
+all-reduce of the residual stream twice per layer): the batch is the same
 at every N, value = tokens/s of the job, timed as the max over ranks (strong
-scaling). --impl reference times the CPU oracle port of the reference path
-(rank 0 only).
+scaling). Besides the headline the line carries:
+  tp_parity    logits of a small tensor-parallel-splittable decoder on the N
+               ranks against oracle logits stored in tests/golden (any N);
+  decode_attn  the decode-attention configuration (32 sequences, 32 query /
+               8 KV heads, ctx 1k/8k/32k, bf16 and int8 KV), heads split over
+               the N ranks, GB/s against the HBM peak;
+  flash        the causal flash-attention prefill configuration (B=4, H=32,
+               S=4096, d=128), TFLOP/s against the bf16 peak (N = 1);
+  gemv         the dequant-GEMV sweep (N = 1).
+--impl reference times the CPU oracle port of the reference path (rank 0).
 """
 from __future__ import annotations
 
@@ -31,10 +39,12 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tokens/s (7B-shape 4-bit) at 1/2/4/8 B200; dequant-GEMV HBM GB/s vs peak"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 # DRAM bytes / algorithmic bytes of decode_attn_kernel, from an ncu capture of
 # the same kernel on batch 32, ctx 8192 (1.07446 GB read + 7.79 MB written for
 # 1.07427 GB of K/V/q/out): applied to the bench's launch to give its traffic
 ATTN_TRAFFIC_RATIO = (1.074456e9 + 7.78624e6) / 1.074266112e9
+ATTN_TRAFFIC_SOURCE = "ncu dram bytes / algorithmic bytes of decode_attn_kernel at batch 32, ctx 8192, 32q/8kv"
 CFG_7B = dict(vocab_size=32000, dim=4096, n_layers=32, n_heads=32, n_kv_heads=32, ffn_dim=11008)
 
 
@@ -49,8 +59,9 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=16)
     ap.add_argument("--no-batch1", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-sample-layers", type=int, default=1)
+    ap.add_argument("--cpu-sample-layers", type=int, default=1, help="layer-steps in the CPU baseline sample")
     ap.add_argument("--no-gemv-sweep", action="store_true")
+    ap.add_argument("--no-flash", action="store_true")
     return ap.parse_args()
 
 
@@ -64,6 +75,16 @@ def measured_peaks():
         return float(d["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_tflops():
+    """Dense bf16 peak: the burst figure (kernels timed alone)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_BF16_TFLOPS, "fallback"
 
 
 class ClockSampler:
@@ -174,17 +195,17 @@ def _cpu_weights(seed: int):
     return _CPU_WEIGHTS[seed]
 
 
-def cpu_layer_sample(n_threads: int, batch: int = 1, seed: int = 7):
-    """Time one Llama-style layer of a decode step for `batch` sequences at
-    context 2048 on the CPU oracle (f64, dequantize-then-matvec per reference
-    order) plus the LM head, split across n_threads by output rows. Returns
-    (seconds for one decode step of the full 32-layer model, description)."""
-    import concurrent.futures as cf
-
+def cpu_layer_step(pool, n_threads: int, batch: int, part: int, seed: int = 7):
+    """One layer-step of a decode step for `batch` sequences at context 2048
+    on the CPU oracle (f64, dequantize-then-matvec per reference order): one
+    Llama-style layer's four fused Q4_0 GEMVs and its 32-head attention, plus
+    part `part` (of 32) of the LM head's rows. All 32 layers of the model have
+    the same shapes, so 32 layer-steps (parts 0..31) are exactly the work of
+    one full decode step. Rows are split across n_threads. Returns seconds."""
     import numpy as np
 
     from oracle import oracle as O
-    rng = np.random.default_rng(seed + 1)
+    rng = np.random.default_rng(seed + 1 + part)
     mats, lm = _cpu_weights(seed)
     bpr = lambda k: k // 32 * 18
 
@@ -192,55 +213,116 @@ def cpu_layer_sample(n_threads: int, batch: int = 1, seed: int = 7):
         blocks, n, k, x, r0, r1 = args
         O.gemv_blocks(O.GGML_Q4_0, blocks[r0 * bpr(k):r1 * bpr(k)], r1 - r0, k, x)
 
-    def gemv(pool, blocks, n, k):
+    def gemv(blocks, n, k, r_lo=0, r_hi=None):
+        r_hi = n if r_hi is None else r_hi
         x = rng.standard_normal((batch, k))
-        step = (n + n_threads - 1) // n_threads
-        list(pool.map(gemv_rows, [(blocks, n, k, x, r, min(n, r + step)) for r in range(0, n, step)]))
+        step = (r_hi - r_lo + n_threads - 1) // n_threads
+        list(pool.map(gemv_rows, [(blocks, n, k, x, r, min(r_hi, r + step)) for r in range(r_lo, r_hi, step)]))
 
     ctx, hd, H = 2048, 128, 32
     K = rng.standard_normal((ctx, hd))
     Vv = rng.standard_normal((ctx, hd))
     q = rng.standard_normal(hd)
+    t0 = time.perf_counter()
+    for blocks, n, k in mats:
+        gemv(blocks, n, k)
+    list(pool.map(lambda h: O.paged_attention(q, K, Vv, hd), range(batch * H)))
+    V = lm[1]
+    gemv(*lm, r_lo=part * V // 32, r_hi=(part + 1) * V // 32)
+    return time.perf_counter() - t0
+
+
+def cpu_decode_sample(n_threads: int, batch: int, layer_steps: int = 1):
+    """Tokens/s of the CPU oracle on `layer_steps` consecutive layer-steps
+    (each 1/32 of a decode step, see cpu_layer_step)."""
+    import concurrent.futures as cf
     with cf.ThreadPoolExecutor(max_workers=n_threads) as pool:
-        t0 = time.perf_counter()
-        for blocks, n, k in mats:
-            gemv(pool, blocks, n, k)
-        list(pool.map(lambda h: O.paged_attention(q, K, Vv, hd), range(batch * H)))
-        t_layer = time.perf_counter() - t0
-        t0 = time.perf_counter()
-        gemv(pool, *lm)
-        t_lm = time.perf_counter() - t0
-    per_step = CFG_7B["n_layers"] * t_layer + t_lm
-    return per_step, f"one layer (4 fused Q4_0 GEMVs over {batch} rows + 32-head attention at ctx 2048 for " \
-                     f"{batch} sequences) + LM head, {n_threads} thread(s), extrapolated x32 layers"
+        t = sum(cpu_layer_step(pool, n_threads, batch, i % 32) for i in range(layer_steps))
+    tokens = batch * layer_steps / 32.0
+    return tokens / t, (f"{layer_steps} layer-step(s) of the decode step for {batch} sequences at ctx 2048 "
+                        f"(each: one layer's 4 fused Q4_0 GEMVs + 32-head attention per sequence, and 1/32 of the "
+                        f"LM head rows; 32 layer-steps = one decode step), {n_threads} thread(s)")
+
+
+def cpu_flash_sample():
+    """C3 on the CPU oracle: flash_attention_forward (src/flash_attention.rs:
+    53-159, its auto tile) for one (batch, head) of S=4096, d=128, causal,
+    one thread; the reference runs heads serially, so the configuration's 128
+    heads take 128 times as long. Returns (TFLOP/s, description)."""
+    import numpy as np
+
+    from oracle import oracle as O
+    S, d = 4096, 128
+    rng = np.random.default_rng(3)
+    q, k, v = (rng.standard_normal(S * d) for _ in range(3))
+    t = O.flash_auto_tile(S, d)
+    t0 = time.perf_counter()
+    O.flash_attention_forward(q, k, v, d, t, t, True)
+    dt = time.perf_counter() - t0
+    flops_head = 4 * d * S * (S + 1) // 2
+    return flops_head / dt / 1e12, "one (batch, head) of B=4 H=32 S=4096 d=128 causal, 1 thread " \
+                                   "(the configuration is 128 such heads run serially: time x128)"
+
+
+def cpu_attn_sample(ctx: int = 1024, n: int = 32, Hq: int = 32, Hkv: int = 8, D: int = 128):
+    """C4 at ctx 1024 on the CPU oracle: paged_attention (src/kv_cache.rs:
+    95-112) for every (sequence, query head), one thread, full size. Returns
+    (GB/s on the same algorithmic bytes as the GPU figure, description)."""
+    import numpy as np
+
+    from oracle import oracle as O
+    rng = np.random.default_rng(4)
+    K = rng.standard_normal((n, Hkv, ctx * D))
+    V = rng.standard_normal((n, Hkv, ctx * D))
+    q = rng.standard_normal((n, Hq, D))
+    G = Hq // Hkv
+    t0 = time.perf_counter()
+    for i in range(n):
+        for h in range(Hq):
+            O.paged_attention(q[i, h], K[i, h // G], V[i, h // G], D)
+    dt = time.perf_counter() - t0
+    byts = n * ctx * Hkv * D * 2 * 2 + 2 * 2 * n * Hq * D
+    return byts / dt / 1e9, f"{n} sequences x {Hq} query heads ({Hkv} KV heads) at ctx {ctx}, bf16-sized bytes, " \
+                            "1 thread, full size"
 
 
 def run_reference(args, rank, ws):
+    """The reference path's CPU implementation (the oracle port) with every
+    host thread: a step is one layer-step (1/32 of a decode step for the
+    batch), so value = batch/32 tokens per step over the measured time and
+    steps/warmup are the driver's own."""
     if rank != 0:
         return
+    import concurrent.futures as cf
     n_threads = os.cpu_count() or 1
-    # warmup samples
-    for _ in range(max(0, min(args.warmup, 1))):
-        cpu_layer_sample(n_threads, args.batch)
-    times = []
-    t_all = time.perf_counter()
-    steps = max(1, min(args.steps, 4))
-    for _ in range(steps):
-        per_step, desc = cpu_layer_sample(n_threads, args.batch)
-        times.append(per_step)
-    per_step = statistics.median(times)
-    value = args.batch / per_step
+    B = args.batch
+    with cf.ThreadPoolExecutor(max_workers=n_threads) as pool:
+        for i in range(args.warmup):
+            cpu_layer_step(pool, n_threads, B, i % 32)
+        t_all = time.perf_counter()
+        times = [cpu_layer_step(pool, n_threads, B, i % 32) for i in range(args.steps)]
+        wall = time.perf_counter() - t_all
+    total = sum(times)
+    value = B * args.steps / 32.0 / total
+    desc = (f"{args.steps} layer-steps (each 1/32 of the decode step for {B} sequences at ctx 2048: one layer's "
+            f"4 fused Q4_0 GEMVs + 32-head attention per sequence + 1/32 of the LM head rows), {n_threads} threads")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": "7B-shape Llama decoder decode, Q4_0 linears, CPU oracle port of the reference "
-                                   "path (sampled layer, extrapolated)", "global_batch": args.batch,
-                       "seq_len": args.prompt_len, "parallelism": "cpu threads"},
+            "config": bench_config(args, ws),
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": n_threads, "kind": "port",
                              "sample": desc},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "wall_s": time.perf_counter() - t_all}
+            "wall_s": wall}
     print(json.dumps(line), flush=True)
+
+
+def bench_config(args, ws):
+    return {"workload": "7B-shape Llama decoder decode (32 layers, d4096, 32x128 heads, SwiGLU 11008, "
+                        "vocab 32000, Q4_0 linears, bf16 paged KV), random weights N(0,0.02)",
+            "global_batch": args.batch, "seq_len": args.prompt_len, "prompt_len": args.prompt_len,
+            "parallelism": f"tp{ws}" if ws > 1 else "single",
+            "l2": "inputs larger than L2 (3.7 GB weights + KV per step)"}
 
 
 # ---------------------------------------------------------------- GPU arm
@@ -380,6 +462,21 @@ def main():
         t1, _, _ = run_decode(dec, sid, prompt[:1], args.steps, args.warmup, ws, torch)
         b1 = max_over_ranks(t1, ws)
     barrier(ws)
+    setup_s = time.perf_counter() - t_setup
+    dec.close()  # its CUDA graphs hold NCCL calls: released before any later collective use
+
+    tp = tp_parity(comm, ws)
+    attn = decode_attn_sweep(ws, hbm, peak_src)
+
+    flash = None  # single-GPU configuration
+    if rank == 0 and ws == 1 and not args.no_flash:
+        from vortex_b200 import kernel_bench as KB
+        tfl, tsrc = measured_tflops()
+        r = KB.flash_case(4, 32, 4096, True)
+        flash = {"config": "B=4 H=32 S=4096 d=128 causal, q/k/v bf16 N(0,1), scale 1/sqrt(128)", "unit": "TFLOP/s",
+                 "us": r["us"], "achieved": r["TFLOPs"], "peak": tfl, "peak_source": tsrc + " bf16 burst",
+                 "frac": r["TFLOPs"] / tfl, "flops": r["flops"],
+                 "flops_formula": "4*B*H*d*S(S+1)/2 (visible score pairs only)"}
 
     # dequant-GEMV sweep (weights 4096x4096, 11008x4096, 4096x11008; Q4_0 and
     # Q8_0; batch 1, 4, 16), each over rotating weight copies > 2x L2; one GPU
@@ -394,10 +491,16 @@ def main():
                            "achieved": round(r["GBps"], 1), "frac": round(r["GBps"] / hbm, 3)} for r in rows]}
         gemv["best_frac"] = max(c["frac"] for c in gemv["cases"])
 
-    cpu = None  # the CPU baseline runs at N = 1 only
+    cpu = None  # the CPU baselines run at N = 1 only
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        per_step, desc = cpu_layer_sample(1, B)
-        cpu = {"value": B / per_step, "unit": "tokens/s", "cores": 1, "kind": "port", "sample": desc}
+        v, desc = cpu_decode_sample(1, B, args.cpu_sample_layers)
+        cpu = {"value": v, "unit": "tokens/s", "cores": 1, "kind": "port", "sample": desc}
+        if flash is not None:
+            v, desc = cpu_flash_sample()
+            flash["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": 1, "kind": "port", "sample": desc}
+        if attn is not None:
+            v, desc = cpu_attn_sample()
+            attn["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": 1, "kind": "port", "sample": desc}
 
     # our kernels per step (NCCL's own kernels not counted): embedding; per
     # layer RMSNorm, QKV GEMV, RoPE + KV append, decode attention, O GEMV,
@@ -406,16 +509,12 @@ def main():
     # key -> token with tp > 1)
     launches_per_step = 1 + CFG_7B["n_layers"] * (9 + (2 if ws > 1 else 0)) + (3 if ws == 1 else 5)
     if rank == 0:
+        cfg = bench_config(args, ws)
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_max / args.steps * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "7B-shape Llama decoder decode (32 layers, d4096, 32x128 heads, SwiGLU 11008, "
-                                   "vocab 32000, Q4_0 linears, bf16 paged KV), random weights N(0,0.02)",
-                       "global_batch": B, "seq_len": args.prompt_len,
-                       "prompt_len": args.prompt_len, "decode_steps": args.steps,
-                       "parallelism": f"tp{ws}" if ws > 1 else "single",
-                       "l2": "inputs larger than L2 (3.7 GB weights + KV per step)"},
+            "config": cfg,
             "prefill": {"tokens_per_s": B * args.prompt_len / t_prefill, "seconds": t_prefill,
                         "sequences": B, "prompt_len": args.prompt_len,
                         "note": "host wall time of vxb_decoder_prefill per sequence (K2 GEMM + K3 flash)"},
@@ -424,22 +523,74 @@ def main():
             "roofline": {"kernel": "decode_attn_kernel (layer 0, batch %d)" % B, "bound": "hbm",
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "peak_source": peak_src, "traffic": attn_bytes * ATTN_TRAFFIC_RATIO,
+                         "traffic_source": ATTN_TRAFFIC_SOURCE,
                          "algorithmic_bytes": attn_bytes, "launch_us": t_attn * 1e6},
             "cpu_baseline": cpu,
+            "tp_parity_err": tp["err"] if tp else None,
+            "tp_parity": tp,
+            "decode_attn": attn,
+            "flash": flash,
             "gemv": gemv,
             "clocks": clocks,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches_per_step * args.steps,
-            "setup_s": time.perf_counter() - t_setup,
+            "setup_s": setup_s,
         }
         print(json.dumps(line), flush=True)
     barrier(ws)
-    dec.close()  # its CUDA graphs hold NCCL calls: release them before the communicator
     if comm is not None:
         comm.close()
     if ws > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def tp_parity(comm, ws):
+    """Logits of the small fixture decoder (vocab 1024, d 1024, 2 layers, 8
+    heads x 128, SwiGLU 2048, Q4_0; it splits over 1/2/4/8 ranks) on these
+    ranks, prefill + teacher-forced decode, against the oracle logits stored
+    in tests/golden/tp_decoder_logits.npz (normwise error, max over every
+    position; the gate is 1e-2). Every rank runs it; rank 0 reports."""
+    import numpy as np
+
+    from vortex_b200 import decoder as D
+    fx = np.load(os.path.join(ROOT, "tests", "golden", "tp_decoder_logits.npz"))
+    cfg = json.loads(str(fx["cfg"]))
+    dec = D.Decoder(max_batch=len(fx["seq_ids"]), max_seq=32, comm=comm, **cfg)
+    dec.load_float_weights(D.synthetic_weights(cfg, int(fx["seed"])))
+    ids = [int(s) for s in fx["seq_ids"]]
+    pre, steps = dec.score(ids, fx["prompts"], fx["tokens"])
+    dec.close()
+
+    def nerr(y, r):
+        return float(np.max(np.abs(y.astype(np.float64) - r)) / np.max(np.abs(r)))
+
+    errs = [nerr(pre[i], fx["prefill_logits"][i]) for i in range(len(ids))]
+    errs += [nerr(steps[t, i], fx["logits"][t, i]) for t in range(steps.shape[0]) for i in range(len(ids))]
+    err = max_over_ranks(max(errs), ws)
+    return {"err": err, "gate": 1e-2, "ranks": ws, "positions": len(errs),
+            "model": "vocab 1024, d 1024, 2 layers, 8x128 heads, SwiGLU 2048, Q4_0; 4 sequences, 8-token prompts, "
+                     "4 teacher-forced decode steps; normwise max|y-r|/max|r| against the oracle"}
+
+
+def decode_attn_sweep(ws, hbm, peak_src):
+    """The decode-attention configuration: 32 sequences, 32 query / 8 KV heads,
+    head_dim 128, ctx 1k/8k/32k, bf16 and int8 KV; the heads are split over
+    the ranks (each rank 32/N query and 8/N KV heads), time = max over ranks,
+    GB/s = the whole configuration's algorithmic bytes / that time."""
+    from vortex_b200 import kernel_bench as KB
+    cases = []
+    for dt in ("bf16", "int8"):
+        for ctx in (1024, 8192, 32768):
+            r = KB.attn_case(ctx, dt, n=32, Hq=32 // ws, Hkv=8 // ws)
+            t = max_over_ranks(r["us"], ws)
+            per_tok = 8 * 128 * 2 * 2 if dt == "bf16" else 8 * 128 * 2 + 8 * 2 * 4
+            byts = 32 * ctx * per_tok + 2 * 2 * 32 * 32 * 128
+            cases.append({"dtype": dt, "ctx": ctx, "us": round(t, 2), "achieved": round(byts / t / 1e3, 1),
+                          "frac": round(byts / t / 1e3 / hbm, 3), "bytes": byts})
+    return {"config": "32 sequences x 32 query heads / 8 KV heads (GQA), head_dim 128, one new token each; "
+                      f"heads split over {ws} GPU(s)", "unit": "GB/s", "peak": hbm, "peak_source": peak_src,
+            "bytes": "32*ctx*(8*128*2*2 bf16 | 8*(128+4)*2 int8) + q/out", "cases": cases}
 
 
 if __name__ == "__main__":

@@ -69,11 +69,22 @@ int vxb_memcpy_h2d(vxb_ctx *ctx, void *d_dst, const void *h_src, size_t bytes, v
 int vxb_memcpy_d2h(vxb_ctx *ctx, void *h_dst, const void *d_src, size_t bytes, void *stream);
 int vxb_memset(vxb_ctx *ctx, void *d_dst, int value, size_t bytes, void *stream);
 int vxb_sync(vxb_ctx *ctx, void *stream);
-/* Synchronize the device, read and clear the context's device error word.
- * Kernels bound every wait (clock64 budget); a wait that runs out sets the
- * word and the kernel finishes instead of hanging. Returns VXB_ETIMEOUT
- * (and *out != 0) when that happened since the last call. */
+/* Synchronize the device, read and clear the device error words: the
+ * context's own and the one in vxb_gemv_q_static's fixed array on the
+ * context's device (shared by every context of that device). Kernels bound
+ * every wait (clock64 budget); a wait that runs out sets the word and the
+ * kernel finishes instead of hanging. Returns VXB_ETIMEOUT (and *out != 0)
+ * when that happened since the last call. Allocates nothing. */
 int vxb_device_error(vxb_ctx *ctx, int *out);
+/* Self-test of the bounded waits above (no counterpart in the reference; the
+ * timeout semantics follow the heartbeat timeouts of dist_runtime.rs:426-456):
+ * runs the library's own wait helper - kind 0 the mbarrier wait of the stage
+ * rings, kind 1 the peer-slot poll of the one-shot all-reduce - on a barrier
+ * nobody arrives on / a slot nobody fills, with a budget of budget_cycles SM
+ * clocks (1 .. 2^31). The wait gives up, sets the error word (static_word = 0:
+ * the context's, 1: the one in vxb_gemv_q_static's fixed array) and the
+ * kernel returns, so the next vxb_device_error reports VXB_ETIMEOUT. */
+int vxb_selftest_wait_timeout(vxb_ctx *ctx, int kind, int static_word, long long budget_cycles, void *stream);
 
 /* ------------------------------------------------------------------------ */
 /* Weight blocks (host codec).                                               */
@@ -133,6 +144,14 @@ int vxb_gemv_q(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const u
  * Allocates nothing: no cudaMalloc / cudaFree. */
 int vxb_gemv_q_static(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const uint16_t *d_x,
                       int batch, int y_dtype, void *d_y, void *stream);
+/* What a GEMV of this shape launches (no counterpart in the reference; a
+ * diagnostic of the planner): *kernel 0 = per-warp stream kernel, 1 = group
+ * kernel, 2 = tcgen05 kernel; *splits = k-splits per row group; *cluster = 1
+ * when the splits add through distributed shared memory, 0 when they add
+ * through global partials (splits > 1) or do not split. is_static selects
+ * the plan of vxb_gemv_q_static (its splits are capped by its fixed array). */
+int vxb_gemv_plan_info(vxb_ctx *ctx, int fmt, int N, int K, int batch, int is_static, int *kernel, int *splits,
+                       int *cluster);
 
 /* ------------------------------------------------------------------------ */
 /* Paged KV cache. Replaces PagedKVCache (src/kv_cache.rs:29-93) and the     */

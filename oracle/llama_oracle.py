@@ -12,6 +12,9 @@ both sides see identical operands at those points.
 """
 from __future__ import annotations
 
+import concurrent.futures as cf
+import os
+
 import numpy as np
 
 from . import oracle as O
@@ -33,17 +36,21 @@ class LlamaOracle:
         def deq(blocks, n, k):
             return O.dequantize_blocks(fmt, blocks, n * k).astype(np.float64).reshape(n, k)
 
-        self.L = []
-        for l in layers:
-            self.L.append(dict(
-                wq=deq(l["wq"], d, d), wk=deq(l["wk"], kvd, d), wv=deq(l["wv"], kvd, d), wo=deq(l["wo"], d, d),
-                w1=deq(l["w1"], f, d), w2=deq(l["w2"], d, f), w3=deq(l["w3"], f, d),
-                ln1_w=np.asarray(l["ln1_w"], np.float64), ln1_b=np.asarray(l["ln1_b"], np.float64),
-                ln2_w=np.asarray(l["ln2_w"], np.float64), ln2_b=np.asarray(l["ln2_b"], np.float64)))
+        # one matrix per thread (the C oracle releases the interpreter lock)
+        with cf.ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 1)) as pool:
+            shapes = dict(wq=(d, d), wk=(kvd, d), wv=(kvd, d), wo=(d, d), w1=(f, d), w2=(d, f), w3=(f, d))
+            futs = [{key: pool.submit(deq, l[key], *nk) for key, nk in shapes.items()} for l in layers]
+            fout = pool.submit(deq, out_blocks, V, d)
+            self.L = []
+            for l, fu in zip(layers, futs):
+                m = {key: fu[key].result() for key in shapes}
+                m.update(ln1_w=np.asarray(l["ln1_w"], np.float64), ln1_b=np.asarray(l["ln1_b"], np.float64),
+                         ln2_w=np.asarray(l["ln2_w"], np.float64), ln2_b=np.asarray(l["ln2_b"], np.float64))
+                self.L.append(m)
+            self.wout = fout.result()
         self.emb = np.asarray(emb, np.float64)
         self.fw = np.asarray(final_w, np.float64)
         self.fb = np.asarray(final_b, np.float64)
-        self.wout = deq(out_blocks, V, d)
         self.cache = {}  # seq -> per layer [(k, v)]
         self.eps = cfg.get("norm_eps", 1e-5)
         self.kv_int8 = bool(cfg.get("kv_int8", False))
@@ -60,37 +67,52 @@ class LlamaOracle:
         return out
 
     def step(self, seq: int, token: int) -> np.ndarray:
+        return self.step_batch([seq], [token])[0]
+
+    def step_batch(self, seqs, tokens, logits: bool = True):
+        """One token for each sequence of `seqs` (distinct ids, each at its own
+        position). The projections of all sequences are one f64 matrix
+        product per weight (the same per-column sums as a matvec); norms, RoPE
+        and attention run per sequence. Returns the logits [len(seqs), vocab]
+        (None with logits=False, which skips the output projection)."""
         c = self.cfg
         d, H, Hkv = c["dim"], c["n_heads"], c["n_kv_heads"]
         hd = d // H
         G = H // Hkv
-        kv = self.cache.setdefault(seq, [[] for _ in self.L])
-        pos = len(kv[0])
-        x = self.emb[token].copy()
+        B = len(seqs)
+        kvs = [self.cache.setdefault(s, [[] for _ in self.L]) for s in seqs]
+        pos = [len(kv[0]) for kv in kvs]
+        X = self.emb[np.asarray(tokens, dtype=np.int64)].T.copy()  # [d, B]
+
+        def norm_cols(X, w, b):
+            return bf16(np.stack([O.rmsnorm_bias(X[:, i], w, b, self.eps) for i in range(B)], axis=1))
+
         for li, L in enumerate(self.L):
-            h = bf16(O.rmsnorm_bias(x, L["ln1_w"], L["ln1_b"], self.eps))
-            q = bf16(O.rope_embed(L["wq"] @ h, pos, d))
-            k = bf16(O.rope_embed(L["wk"] @ h, pos, d))
-            v = bf16(L["wv"] @ h)
-            if self.kv_int8:
-                k, v = self._int8(k, Hkv, hd), self._int8(v, Hkv, hd)
-            kv[li].append((k, v))
-            K = np.array([e[0] for e in kv[li]]).reshape(-1, Hkv, hd)
-            Vv = np.array([e[1] for e in kv[li]]).reshape(-1, Hkv, hd)
-            a = np.zeros(d)
-            for j in range(H):
-                kh = j // G
-                a[j * hd:(j + 1) * hd] = O.paged_attention(q[j * hd:(j + 1) * hd], K[:, kh].reshape(-1),
-                                                            Vv[:, kh].reshape(-1), hd)
-            a = bf16(a)
-            x = x + L["wo"] @ a
-            h2 = bf16(O.rmsnorm_bias(x, L["ln2_w"], L["ln2_b"], self.eps))
-            g = L["w1"] @ h2
-            u = L["w3"] @ h2
-            act = bf16(g * (1.0 / (1.0 + np.exp(-g))) * u)
-            x = x + L["w2"] @ act
-        hf = bf16(O.rmsnorm_bias(x, self.fw, self.fb, self.eps))
-        return self.wout @ hf
+            Hn = norm_cols(X, L["ln1_w"], L["ln1_b"])
+            Q, K, V = L["wq"] @ Hn, L["wk"] @ Hn, L["wv"] @ Hn
+            A = np.zeros((d, B))
+            for i in range(B):
+                q = bf16(O.rope_embed(Q[:, i], pos[i], d))
+                k = bf16(O.rope_embed(K[:, i], pos[i], d))
+                v = bf16(V[:, i])
+                if self.kv_int8:
+                    k, v = self._int8(k, Hkv, hd), self._int8(v, Hkv, hd)
+                kvs[i][li].append((k, v))
+                Kc = np.array([e[0] for e in kvs[i][li]]).reshape(-1, Hkv, hd)
+                Vc = np.array([e[1] for e in kvs[i][li]]).reshape(-1, Hkv, hd)
+                for j in range(H):
+                    kh = j // G
+                    A[j * hd:(j + 1) * hd, i] = O.paged_attention(q[j * hd:(j + 1) * hd], Kc[:, kh].reshape(-1),
+                                                                  Vc[:, kh].reshape(-1), hd)
+            X = X + L["wo"] @ bf16(A)
+            H2 = norm_cols(X, L["ln2_w"], L["ln2_b"])
+            Gt = L["w1"] @ H2
+            U = L["w3"] @ H2
+            X = X + L["w2"] @ bf16(Gt * (1.0 / (1.0 + np.exp(-Gt))) * U)
+        if not logits:
+            return None
+        Hf = norm_cols(X, self.fw, self.fb)
+        return (self.wout @ Hf).T
 
 
 def argmax_first(logits: np.ndarray) -> int:

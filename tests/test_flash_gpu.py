@@ -82,6 +82,44 @@ def test_flash_c3_shape_sampled_rows(cuda_ok):
         assert np.max(np.abs(lse[0, h, rows].cpu().numpy() - rl) / np.maximum(1.0, np.abs(rl))) <= 1e-3
 
 
+def test_flash_c3_all_heads_sampled_rows(cuda_ok):
+    """The prefill benchmark configuration itself (B=4, H=32, S=4096, d=128,
+    causal, Q/K/V ~N(0,1) bf16): every one of the 128 (batch, head) pairs is
+    checked on the first and last 64 query rows plus 256 random rows, each
+    against the exact attention over all its visible keys (oracle in f64,
+    heads spread over host threads)."""
+    import concurrent.futures as cf
+    import os
+
+    from oracle import oracle as O
+    from vortex_b200 import attention as A
+    B, S, H = 4, 4096, 32
+    q, k, v = _inputs(B, S, H, H, seed=4096)
+    o, lse = A.flash_attention(q, k, v, causal=True)
+    torch.cuda.synchronize()
+    qn, kn, vn = (t.float().cpu().numpy() for t in (q, k, v))
+    on, ln = o.float().cpu().numpy(), lse.cpu().numpy()
+    rng = np.random.default_rng(128)
+    picks = [np.unique(np.concatenate([np.arange(64), np.arange(S - 64, S), rng.integers(64, S - 64, 256)]))
+             for _ in range(B * H)]
+
+    def check(bh):
+        b, h = divmod(bh, H)
+        rows = picks[bh]
+        ro, rl = O.attention_rows(qn[b, :, h].astype(np.float64), kn[b, :, h].astype(np.float64),
+                                  vn[b, :, h].astype(np.float64), 128, True, rows)
+        e = rel_err(on[b, rows, h], ro)
+        le = float(np.max(np.abs(ln[b, h, rows] - rl) / np.maximum(1.0, np.abs(rl))))
+        return bh, e, le
+
+    with cf.ThreadPoolExecutor(max_workers=min(32, os.cpu_count() or 1)) as pool:
+        results = list(pool.map(check, range(B * H)))
+    assert len(results) == 128
+    worst = max(results, key=lambda r: r[1])
+    assert worst[1] <= 1e-2, worst
+    assert max(r[2] for r in results) <= 1e-3
+
+
 def test_flash_multi_head_layout(cuda_ok):
     """multi_head_flash_attention's [N, H*d] interleaved-head layout."""
     from oracle import oracle as O

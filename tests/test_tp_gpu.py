@@ -177,3 +177,77 @@ def test_allreduce_sum_peer_memory_and_nccl_paths(cuda_ok):
             else:
                 np.testing.assert_allclose(got[0][k], want, rtol=1e-6, atol=1e-6)
             k += 1
+
+
+def _fixture():
+    from tests.golden import make_tp_fixture as M
+    return M, np.load(M.PATH)
+
+
+def _fixture_err(dec, fx):
+    """Largest normwise logits error of a decoder against the oracle fixture
+    (prefill logits and every teacher-forced decode step)."""
+    from tests.parity import norm_err
+    ids = [int(s) for s in fx["seq_ids"]]
+    pre, steps = dec.score(ids, fx["prompts"], fx["tokens"])
+    errs = [norm_err(pre[i], fx["prefill_logits"][i]) for i in range(len(ids))]
+    errs += [norm_err(steps[t, i], fx["logits"][t, i]) for t in range(steps.shape[0]) for i in range(len(ids))]
+    return max(errs)
+
+
+def test_fixture_decoder_matches_oracle_single_gpu(cuda_ok):
+    """The tensor-parallel fixture model on one GPU (prefill + teacher-forced
+    decode) against the oracle's logits: normwise <= 1e-2."""
+    from vortex_b200 import decoder as D
+    from vortex_b200.decoder import synthetic_weights
+    M, fx = _fixture()
+    dec = D.Decoder(max_batch=4, max_seq=32, **M.CFG)
+    dec.load_float_weights(synthetic_weights(M.CFG, M.SEED))
+    err = _fixture_err(dec, fx)
+    dec.close()
+    assert err <= 1e-2, err
+
+
+def _fixture_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    from vortex_b200 import comm as C
+    from vortex_b200 import decoder as D
+    from vortex_b200.decoder import synthetic_weights
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        M, fx = _fixture()
+        comm = C.Comm(world, rank, C.share_unique_id(rank), device=rank)
+        dec = D.Decoder(max_batch=4, max_seq=32, comm=comm, **M.CFG)
+        dec.load_float_weights(synthetic_weights(M.CFG, M.SEED))
+        err = _fixture_err(dec, fx)
+        dec.close()
+        comm.close()
+        q.put((rank, err))
+    except Exception as e:
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_fixture_decoder_matches_oracle_tp2(cuda_ok):
+    """The same model split over 2 GPUs (heads, FFN rows, vocabulary) against
+    the oracle's logits on every rank."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fixture_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=600) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(2):
+        assert not isinstance(got[r], str), got[r]
+        assert got[r] <= 1e-2, (r, got[r])

@@ -56,6 +56,7 @@ SIGNATURES = {
     "vxb_memset": (_I, [_P, _P, _I, _SZ, _P]),
     "vxb_sync": (_I, [_P, _P]),
     "vxb_device_error": (_I, [_P, ctypes.POINTER(_I)]),
+    "vxb_selftest_wait_timeout": (_I, [_P, _I, _I, ctypes.c_longlong, _P]),
     "vxb_block_bytes": (_SZ, [_I, _SZ]),
     "vxb_pack_blocks_f64": (_I, [_I, _P, _SZ, _P]),
     "vxb_pack_blocks_f32": (_I, [_I, _P, _SZ, _P]),
@@ -67,6 +68,7 @@ SIGNATURES = {
     "vxb_untile_weights": (_I, [_P, _I, _P, _I, _I, _P, _P]),
     "vxb_gemv_q": (_I, [_P, _I, _P, _I, _I, _P, _I, _I, _P, _P]),
     "vxb_gemv_q_static": (_I, [_P, _I, _P, _I, _I, _P, _I, _I, _P, _P]),
+    "vxb_gemv_plan_info": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P]),
     "vxb_kv_create": (_I, [_P, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_P)]),
     "vxb_kv_destroy": (_I, [_P]),
     "vxb_kv_append": (_I, [_P, _I, _I, _P, _P, _P, _P]),

@@ -13,6 +13,7 @@
 #include <vector>
 
 #include "comm.h"
+#include "tc_common.h"
 
 using namespace vxb;
 
@@ -86,15 +87,6 @@ __device__ __forceinline__ void st_relaxed_sys_v4(void *p, uint4 v) {
                : "memory");
 }
 
-__device__ __forceinline__ uint4 ld_relaxed_sys_v4(const void *p) {
-  uint4 v;
-  asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p)
-               : "memory");
-  return v;
-}
-
 __device__ __forceinline__ uint32_t canon_bits(float f) { return f != f ? 0x7FC00000u : __float_as_uint(f); }
 
 __global__ void __launch_bounds__(512) oneshot_allreduce_kernel(const ArArgs a) {
@@ -132,15 +124,8 @@ __global__ void __launch_bounds__(512) oneshot_allreduce_kernel(const ArArgs a) 
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int q = 0; q < a.nranks; q++) {
       uint8_t *slot = mine + gbase + (size_t)q * kArSlotBytes + i * 16;
-      uint4 v = ld_relaxed_sys_v4(slot);
-      const long long t0 = clock64();
-      while (v.x == kArEmpty || v.y == kArEmpty || v.z == kArEmpty || v.w == kArEmpty) {
-        if (clock64() - t0 > (1ll << 31)) {
-          atomicExch(a.err, 1);
-          break;
-        }
-        v = ld_relaxed_sys_v4(slot);
-      }
+      uint4 v;
+      if (!wait_slot_filled(slot, &v, vxb::tc::kWaitBudget)) atomicExch(a.err, 1);
       acc.x += __uint_as_float(v.x);
       acc.y += __uint_as_float(v.y);
       acc.z += __uint_as_float(v.z);

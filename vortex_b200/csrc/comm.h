@@ -29,6 +29,34 @@ struct vxb_comm {
 
 namespace vxb {
 
+#ifdef __CUDACC__
+__device__ __forceinline__ uint4 ld_relaxed_sys_v4(const void *p) {
+  uint4 v;
+  asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+// Poll a 16-byte peer slot until none of its words holds the empty marker;
+// false (with whatever the slot held last in *out) once `budget` SM clock
+// cycles have passed.
+__device__ __forceinline__ bool wait_slot_filled(const void *slot, uint4 *out, long long budget) {
+  uint4 v = ld_relaxed_sys_v4(slot);
+  const long long t0 = clock64();
+  while (v.x == kArEmpty || v.y == kArEmpty || v.z == kArEmpty || v.w == kArEmpty) {
+    if (clock64() - t0 > budget) {
+      *out = v;
+      return false;
+    }
+    v = ld_relaxed_sys_v4(slot);
+  }
+  *out = v;
+  return true;
+}
+#endif
+
 // op 0 = sum, 1 = max; dtype VXB_F32, VXB_BF16 or -1 for u64 (max of packed keys)
 int comm_allreduce(vxb_comm *c, void *buf, size_t count, int dtype, int op, cudaStream_t st);
 int comm_allgather_f32(vxb_comm *c, const float *send, float *recv, size_t count, cudaStream_t st);

@@ -1,5 +1,6 @@
 // Context, errors and memory entry points of the C ABI.
 // Replaces gpu_runtime::CpuRuntime allocation/copy (src/gpu_runtime.rs:297-348).
+#include "gemv.h"
 #include "vxb_internal.h"
 
 namespace vxb {
@@ -190,14 +191,24 @@ VXB_API int vxb_memset(vxb_ctx *ctx, void *d_dst, int value, size_t bytes, void 
   return VXB_OK;
 }
 
+// Two words can hold a timeout: the context's own (allocated with its
+// workspace) and the one in vxb_gemv_q_static's fixed array on this device
+// (shared by every context of the device, so reading it here clears it for
+// all of them). Neither read nor clear allocates.
 VXB_API int vxb_device_error(vxb_ctx *ctx, int *out) {
   if (!ctx || !out) return set_error(ctx, VXB_EINVAL, "vxb_device_error: null argument");
   *out = 0;
-  if (!ctx->d_err) return VXB_OK;
+  int *words[2] = {ctx->d_err, static_error_word(ctx->device)};
+  if (!words[0] && !words[1]) return VXB_OK;
   if (int rc = use_device(ctx)) return rc;
   VXB_CUDA_TRY(ctx, cudaDeviceSynchronize());
-  VXB_CUDA_TRY(ctx, cudaMemcpy(out, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
-  VXB_CUDA_TRY(ctx, cudaMemset(ctx->d_err, 0, sizeof(int)));
+  for (int *w : words) {
+    if (!w) continue;
+    int v = 0;
+    VXB_CUDA_TRY(ctx, cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost));
+    if (v) VXB_CUDA_TRY(ctx, cudaMemset(w, 0, sizeof(int)));
+    if (v && !*out) *out = v;
+  }
   if (*out) return set_error(ctx, VXB_ETIMEOUT, "a bounded device wait timed out (error word %d)", *out);
   return VXB_OK;
 }

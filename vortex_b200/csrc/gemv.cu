@@ -1176,6 +1176,8 @@ __device__ __align__(256) uint8_t g_static_scratch[kStaticBytes];
 std::mutex g_static_mu;
 uint8_t *g_static_addr[64] = {nullptr};
 
+constexpr size_t kStaticErrOff = kStaticPartialBytes + (size_t)kStaticCounters * 4;  // the error word
+
 // Device address of g_static_scratch on the context's device (resolved once
 // per device with that device current; the symbol's name in host code is a
 // host-side stand-in, not a device address).
@@ -1192,7 +1194,33 @@ int static_scratch(vxb_ctx *ctx, uint8_t **out) {
   return VXB_OK;
 }
 
+// Split count of the group kernel inside vxb_gemv_q_static: the array holds
+// at most kStaticPartialBytes / per_split partial sets.
+int static_splits(int planned, size_t per_split) {
+  return std::max(1, std::min<int>(planned, (int)(kStaticPartialBytes / per_split)));
+}
+
 }  // namespace
+
+namespace vxb {
+
+// The error word of vxb_gemv_q_static's array on `device`, or null while no
+// static call has resolved the array there (then nothing can have set it).
+int *static_error_word(int device) {
+  if (device < 0 || device >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  return g_static_addr[device] ? (int *)(g_static_addr[device] + kStaticErrOff) : nullptr;
+}
+
+// The same word, resolving the array's address first (device made current by the caller).
+int static_error_word_resolve(vxb_ctx *ctx, int **out) {
+  uint8_t *base = nullptr;
+  if (int rc = static_scratch(ctx, &base)) return rc;
+  *out = (int *)(base + kStaticErrOff);
+  return VXB_OK;
+}
+
+}  // namespace vxb
 
 VXB_API int vxb_gemv_q_static(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const uint16_t *d_x,
                               int batch, int y_dtype, void *d_y, void *stream) {
@@ -1220,13 +1248,12 @@ VXB_API int vxb_gemv_q_static(vxb_ctx *ctx, int fmt, const void *d_tiled, int N,
   if (int rc = static_scratch(ctx, &base)) return rc;
   if (gemv_tc_eligible(batch))  // the tensor-core kernel needs no scratch beyond the error word
     return gemv_tc(ctx, fmt, d_tiled, N, K, d_x, batch, y_dtype, d_y, nullptr,
-                   (int *)(base + kStaticPartialBytes + (size_t)kStaticCounters * 4), (cudaStream_t)stream, false);
+                   (int *)(base + kStaticErrOff), (cudaStream_t)stream, false);
   if (stream_eligible(fmt, batch))  // the per-warp stream kernel needs no scratch beyond the error word
     return stream_gemv(ctx, fmt, d_tiled, N, K, d_x, batch, y_dtype, d_y, nullptr,
-                       (int *)(base + kStaticPartialBytes + (size_t)kStaticCounters * 4), (cudaStream_t)stream, false,
-                       "vxb_gemv_q_static");
+                       (int *)(base + kStaticErrOff), (cudaStream_t)stream, false, "vxb_gemv_q_static");
   GemvPlan p = gemv_plan(ctx, fmt, N, K, batch);
-  p.S = std::max(1, std::min<int>(p.S, (int)(kStaticPartialBytes / per_split)));
+  p.S = static_splits(p.S, per_split);
   GemvArgs a;
   const uint8_t *wb = (const uint8_t *)d_tiled;
   a.records = wb + g.codes_off;
@@ -1236,7 +1263,7 @@ VXB_API int vxb_gemv_q_static(vxb_ctx *ctx, int fmt, const void *d_tiled, int N,
   a.resid = nullptr;
   a.ws = (float *)base;
   a.counters = (unsigned *)(base + kStaticPartialBytes);
-  a.err = (int *)(base + kStaticPartialBytes + (size_t)kStaticCounters * 4);
+  a.err = (int *)(base + kStaticErrOff);
   a.N = N;
   a.K = K;
   a.B = batch;
@@ -1268,4 +1295,33 @@ VXB_API int vxb_gemv_q_static(vxb_ctx *ctx, int fmt, const void *d_tiled, int N,
     case 3: return launch_t<1, 3>(ctx, a, grid, smem, st, false);
     default: return launch_t<1, 4>(ctx, a, grid, smem, st, false);
   }
+}
+
+VXB_API int vxb_gemv_plan_info(vxb_ctx *ctx, int fmt, int N, int K, int batch, int is_static, int *kernel,
+                               int *splits, int *cluster) {
+  if (!ctx || !kernel || !splits || !cluster) return set_error(ctx, VXB_EINVAL, "vxb_gemv_plan_info: null argument");
+  if (fmt != VXB_Q4_0 && fmt != VXB_Q8_0) return set_error(ctx, VXB_EINVAL, "vxb_gemv_plan_info: unknown format %d", fmt);
+  if (N <= 0 || K <= 0 || K % 32 || batch < 1 || batch > 32)
+    return set_error(ctx, VXB_EINVAL, "vxb_gemv_plan_info: bad shape N=%d K=%d batch=%d", N, K, batch);
+  if (int rc = use_device(ctx)) return rc;
+  const TiledGeom g = tiled_geom(fmt, N, K);
+  if (gemv_tc_eligible(batch)) {
+    *kernel = 2;
+    *splits = 0;
+    *cluster = 0;
+    return VXB_OK;
+  }
+  if (stream_eligible(fmt, batch)) {
+    const StreamPlan p = stream_plan(ctx, g, batch);
+    *kernel = 0;
+    *splits = p.S;
+    *cluster = p.S > 1;
+    return VXB_OK;
+  }
+  GemvPlan p = gemv_plan(ctx, fmt, N, K, batch);
+  if (is_static) p.S = static_splits(p.S, (size_t)batch * ((N + 15) / 16 * 16) * sizeof(float));
+  *kernel = 1;
+  *splits = p.S;
+  *cluster = p.cluster && p.S > 1 && p.S <= kMaxClusterSplits;
+  return VXB_OK;
 }

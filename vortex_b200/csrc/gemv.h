@@ -24,4 +24,9 @@ bool gemv_tc_eligible(int batch);
 int gemv_tc(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const uint16_t *d_x, int batch, int y_dtype,
             void *d_y, const float *d_resid, int *d_err, cudaStream_t st, bool pdl);
 
+// Error word of vxb_gemv_q_static's fixed array on a device: null while the
+// array has not been resolved there; the _resolve form resolves it.
+int *static_error_word(int device);
+int static_error_word_resolve(vxb_ctx *ctx, int **out);
+
 }  // namespace vxb

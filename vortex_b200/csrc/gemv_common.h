@@ -14,6 +14,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "tc_common.h"
 #include "tiled_layout.h"
 #include "vxb_internal.h"
 
@@ -70,20 +71,10 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Bounded wait for the phase of the given parity; false after ~2^31 cycles.
+// Bounded wait for the phase of the given parity (the shared helper of every
+// kernel's stage rings): false after vxb::tc::kWaitBudget cycles.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-  const uint32_t a = smem_u32(bar);
-  const long long t0 = clock64();
-  while (true) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if (clock64() - t0 > (1ll << 31)) return false;
-  }
+  return vxb::tc::mbar_wait(bar, parity);
 }
 
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {

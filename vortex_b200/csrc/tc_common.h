@@ -11,6 +11,10 @@
 namespace vxb {
 namespace tc {
 
+// Cycle budget of every bounded device-side wait (mbarrier phases, peer
+// slots): 2^31 SM clocks, about 1.1 s at 1.965 GHz.
+constexpr long long kWaitBudget = 1ll << 31;
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
@@ -25,8 +29,9 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Bounded wait for the phase of the given parity; false after ~2^31 cycles.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+// Bounded wait for the phase of the given parity; false once `budget` SM
+// clock cycles have passed (kWaitBudget by default, about one second).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, long long budget = kWaitBudget) {
   const uint32_t a = smem_u32(bar);
   const long long t0 = clock64();
   while (true) {
@@ -37,12 +42,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
         : "r"(a), "r"(parity)
         : "memory");
     if (done) return true;
-    if (clock64() - t0 > (1ll << 31)) return false;
+    if (clock64() - t0 > budget) return false;
   }
 }
 
-__device__ __forceinline__ void wait_or_flag(uint64_t *bar, uint32_t parity, int *err) {
-  if (!mbar_wait(bar, parity)) atomicExch(err, 1);
+__device__ __forceinline__ void wait_or_flag(uint64_t *bar, uint32_t parity, int *err,
+                                             long long budget = kWaitBudget) {
+  if (!mbar_wait(bar, parity, budget)) atomicExch(err, 1);
 }
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {

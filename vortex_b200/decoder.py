@@ -93,6 +93,37 @@ def gguf_decoder_weights(f, cfg: dict) -> list:
     return out
 
 
+LINEAR_KEYS = ("wq", "wk", "wv", "wo", "w1", "w2", "w3")
+SLOT_OF = dict(wq=WQ, wk=WK, wv=WV, wo=WO, w1=W1, w2=W2, w3=W3, ln1_w=LN1_W, ln1_b=LN1_B, ln2_w=LN2_W,
+               ln2_b=LN2_B)
+
+
+def synthetic_weights(cfg: dict, seed: int, sigma: float = 0.02) -> dict:
+    """Host weights of a random Llama-style decoder from one seeded numpy
+    generator: every linear f32 [out, in] ~N(0, sigma) (wq wk wv wo w1 w2 w3
+    per layer, then the output projection [vocab, dim]), norm weights
+    1 + N(0, 0.1) and biases N(0, 0.1) (f32), the embedding as bf16 bit
+    patterns of N(0, 1) values. Returns {"layers": [dict], "emb_bits",
+    "final_w", "final_b", "out"}; the same seed gives the same arrays on any
+    machine (numpy's PCG64 stream)."""
+    rng = np.random.default_rng(seed)
+    d, f, V = cfg["dim"], cfg["ffn_dim"], cfg["vocab_size"]
+    kvd = cfg["n_kv_heads"] * (d // cfg["n_heads"])
+    lin = lambda n, k: (rng.standard_normal((n, k), dtype=np.float32) * np.float32(sigma))
+    shapes = dict(wq=(d, d), wk=(kvd, d), wv=(kvd, d), wo=(d, d), w1=(f, d), w2=(d, f), w3=(f, d))
+    layers = []
+    for _ in range(cfg["n_layers"]):
+        l = {key: lin(*shapes[key]) for key in LINEAR_KEYS}
+        for key in ("ln1", "ln2"):
+            l[key + "_w"] = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+            l[key + "_b"] = (0.1 * rng.standard_normal(d)).astype(np.float32)
+        layers.append(l)
+    emb_bits = _bf16_bits(rng.standard_normal((V, d), dtype=np.float32))
+    fw = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    fb = (0.1 * rng.standard_normal(d)).astype(np.float32)
+    return {"layers": layers, "emb_bits": emb_bits, "final_w": fw, "final_b": fb, "out": lin(V, d)}
+
+
 class Decoder:
     """comm (optional): a vortex_b200.comm.Comm; the decoder is then this
     rank's tensor-parallel part, and every rank makes the same calls."""
@@ -137,6 +168,21 @@ class Decoder:
         self._check(N.lib().vxb_decoder_set_weight(self.ptr, layer, which, a.ctypes.data_as(ctypes.c_void_p),
                                                    a.nbytes))
 
+    def load_float_weights(self, w: dict):
+        """Quantize host f32 weights (synthetic_weights layout) into the
+        decoder's block format with the host packer (the reference's
+        quantize rules) and load them; norms and the embedding as given."""
+        from . import quant as Q
+        fmt = self.cfg.weight_fmt
+        for li, l in enumerate(w["layers"]):
+            for key, slot in SLOT_OF.items():
+                a = l[key]
+                self.set_weight(li, slot, Q.pack_blocks(fmt, a) if key in LINEAR_KEYS else a)
+        self.set_weight(-1, EMBED, w["emb_bits"])
+        self.set_weight(-1, FINAL_W, w["final_w"])
+        self.set_weight(-1, FINAL_B, w["final_b"])
+        self.set_weight(-1, OUTPUT, Q.pack_blocks(fmt, w["out"]))
+
     def load_gguf(self, source):
         """Load every weight from a Llama-style GGUF (a path, bytes or an open
         gguf.GGUFFile; tensor names and formats as gguf_decoder_weights)."""
@@ -168,6 +214,15 @@ class Decoder:
                                                 nxt.ctypes.data_as(ctypes.c_void_p),
                                                 logits.ctypes.data_as(ctypes.c_void_p) if want_logits else None))
         return (int(nxt[0]), logits) if want_logits else int(nxt[0])
+
+    def score(self, seq_ids, prompts, tokens):
+        """Teacher-forced scoring: prefill prompts[i] into the new sequence
+        seq_ids[i], then feed tokens[s, i] for every step s. Returns the
+        logits after each prompt [n, vocab] and after each fed token
+        [steps, n, vocab] (f32)."""
+        pre = np.stack([self.prefill(s, prompts[i], want_logits=True)[1] for i, s in enumerate(seq_ids)])
+        steps = [self.step(seq_ids, tokens[t], want_logits=True)[1] for t in range(len(tokens))]
+        return pre, np.stack(steps) if steps else np.zeros((0, len(seq_ids), self.vocab), np.float32)
 
     def step_device(self, seq_ids, d_tokens, d_next, stream=None):
         import torch

@@ -1,7 +1,7 @@
 """Kernel-level timing of the decode GEMV and the decode attention.
 
     python -m vortex_b200.kernel_bench gemv [--fmt Q4_0] [--n 11008] [--k 4096] [--batch 1]
-    python -m vortex_b200.kernel_bench attn [--ctx 8192] [--dtype bf16]
+    python -m vortex_b200.kernel_bench attn [--ctx 8192] [--dtype bf16] [--batch 32] [--hq 32] [--hkv 8]
     python -m vortex_b200.kernel_bench flash [--b 4] [--h 32] [--s 4096] [--non-causal]
     python -m vortex_b200.kernel_bench gemm [--m 2048] [--n 12288 ...] [--k 4096 ...]
 
@@ -96,34 +96,41 @@ def gemv_sweep(shapes=((4096, 4096), (11008, 4096), (4096, 11008)), fmts=("Q4_0"
 def attn_case(ctx: int, dtype: str = "bf16", n: int = 32, Hq: int = 32, Hkv: int = 8, D: int = 128, reps: int = 10,
               seed: int = 0):
     """Decode attention over a paged cache: n sequences of ctx tokens, Hq
-    query heads over Hkv KV heads (GQA), head_dim D, one query token each."""
+    query heads over Hkv KV heads (GQA), head_dim D, one query token each.
+    When one cache is smaller than twice the L2, launches rotate over enough
+    distinct caches to exceed it."""
     import torch
 
     from . import kv_cache as KV
     kd = KV.BF16 if dtype == "bf16" else KV.I8
     bs = 16
-    cache = KV.PagedKVCache(1, Hkv, D, bs, max_blocks=n * (-(-ctx // bs)) + 8, max_seqs=n + 1, kv_dtype=kd)
+    per_tok = Hkv * D * 2 * (2 if kd == KV.BF16 else 1) + (Hkv * 2 * 4 if kd == KV.I8 else 0)
+    kv_bytes = n * ctx * per_tok
+    copies = max(1, -(-2 * L2_BYTES // kv_bytes))
     gen = torch.Generator(device="cuda").manual_seed(seed)
-    for i in range(n):
-        k = torch.randn(ctx, Hkv, D, device="cuda", generator=gen).bfloat16()
-        v = torch.randn(ctx, Hkv, D, device="cuda", generator=gen).bfloat16()
-        cache.append_seq(0, i, k, v)
-        del k, v
+    caches = []
+    for _ in range(copies):
+        cache = KV.PagedKVCache(1, Hkv, D, bs, max_blocks=n * (-(-ctx // bs)) + 8, max_seqs=n + 1, kv_dtype=kd)
+        for i in range(n):
+            k = torch.randn(ctx, Hkv, D, device="cuda", generator=gen).bfloat16()
+            v = torch.randn(ctx, Hkv, D, device="cuda", generator=gen).bfloat16()
+            cache.append_seq(0, i, k, v)
+            del k, v
+        caches.append(cache)
     q = torch.randn(n, Hq, D, device="cuda", generator=gen).bfloat16()
     ids = list(range(n))
-    o = cache.attention(0, ids, q)
-    per = 5
+    o = caches[0].attention(0, ids, q)
+    per = max(5, copies)
 
     def run():
-        for _ in range(per):
-            cache.attention(0, ids, q, out=o)
+        for j in range(per):
+            caches[j % copies].attention(0, ids, q, out=o)
 
     t = _graph_time(torch, run, per, reps)
-    per_tok = Hkv * D * 2 * (2 if kd == KV.BF16 else 1) + (Hkv * 2 * 4 if kd == KV.I8 else 0)
-    byts = n * ctx * per_tok + 2 * 2 * n * Hq * D
+    byts = kv_bytes + 2 * 2 * n * Hq * D
     res = {"dtype": dtype, "ctx": ctx, "batch": n, "Hq": Hq, "Hkv": Hkv, "D": D, "us": t * 1e6,
-           "GBps": byts / t / 1e9, "bytes": byts}
-    del cache
+           "GBps": byts / t / 1e9, "bytes": byts, "copies": copies}
+    del caches
     torch.cuda.empty_cache()
     return res
 
@@ -194,6 +201,9 @@ def main():
     a = sub.add_parser("attn")
     a.add_argument("--ctx", type=int, nargs="*", default=[1024, 8192, 32768])
     a.add_argument("--dtype", nargs="*", default=["bf16", "int8"])
+    a.add_argument("--batch", type=int, default=32)
+    a.add_argument("--hq", type=int, default=32)
+    a.add_argument("--hkv", type=int, default=8)
     a.add_argument("--reps", type=int, default=10)
     args = ap.parse_args()
     import torch
@@ -211,7 +221,8 @@ def main():
     else:
         for dt in args.dtype:
             for c in args.ctx:
-                print(json.dumps(attn_case(c, dt, reps=args.reps)), flush=True)
+                print(json.dumps(attn_case(c, dt, n=args.batch, Hq=args.hq, Hkv=args.hkv, reps=args.reps)),
+                      flush=True)
 
 
 if __name__ == "__main__":
