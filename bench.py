@@ -40,11 +40,14 @@ sys.path.insert(0, ROOT)
 METRIC = "decode tokens/s (7B-shape 4-bit) at 1/2/4/8 B200; dequant-GEMV HBM GB/s vs peak"
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
-# DRAM bytes / algorithmic bytes of decode_attn_kernel, from an ncu capture of
-# the same kernel on batch 32, ctx 8192 (1.07446 GB read + 7.79 MB written for
-# 1.07427 GB of K/V/q/out): applied to the bench's launch to give its traffic
-ATTN_TRAFFIC_RATIO = (1.074456e9 + 7.78624e6) / 1.074266112e9
-ATTN_TRAFFIC_SOURCE = "ncu dram bytes / algorithmic bytes of decode_attn_kernel at batch 32, ctx 8192, 32q/8kv"
+# DRAM bytes / algorithmic bytes of decode_attn_kernel on the decode step's
+# own per-layer shape (32 sequences x 32 heads, ctx 2048, bf16): one ncu
+# capture read 1,074,086,144 + wrote 3,865,344 bytes for 1,074,266,112
+# algorithmic bytes; applied to the bench's launch to give its traffic
+ATTN_TRAFFIC_RATIO = (1074086144 + 3865344) / 1074266112
+ATTN_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of decode_attn_kernel at 32 sequences x "
+                       "32 heads, ctx 2048, bf16 (profiles/decode_attn_b32_ctx2048_mha_bf16.md), scaled by "
+                       "algorithmic bytes")
 CFG_7B = dict(vocab_size=32000, dim=4096, n_layers=32, n_heads=32, n_kv_heads=32, ffn_dim=11008)
 
 

@@ -113,6 +113,34 @@ int vxb_dequantize_blocks(vxb_ctx *ctx, int fmt, const uint8_t *d_blocks, size_t
                           void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* QuantTensor codes (the quantize / dequantize / quantized_matmul builtins, */
+/* src/interpreter.rs:7278-7346): INT8 = one two's-complement byte per      */
+/* element, INT4 = two per byte (pack_int4, low nibble = even flat index,   */
+/* src/quantize.rs:664-672). Scales are f64, zero points 0 (symmetric).     */
+/* ------------------------------------------------------------------------ */
+#define VXB_QT_INT8 0
+#define VXB_QT_INT4 1
+size_t vxb_qt_data_bytes(int fmt, size_t n);
+size_t vxb_qt_num_groups(size_t n, size_t group_size); /* group_size 0: PerTensor (1 scale) */
+/* QuantTensor::quantize for INT8 / INT4 (src/quantize.rs:81-163): PerGroup
+ * over the flat buffer when group_size > 0, else PerTensor; scale =
+ * calibrate_minmax / calibrate_minmax_range (585-600); code =
+ * clamp(round(v / scale)). h_scales / h_zero_points hold num_groups entries. */
+int vxb_qt_quantize(int fmt, const double *h_data, size_t n, size_t group_size, uint8_t *h_packed,
+                    double *h_scales, int64_t *h_zero_points);
+/* QuantTensor::get_scale (src/quantize.rs:534-545): the mean of the group
+ * scales, summed in order (1.0 for none). */
+int vxb_qt_mean_scale(const double *h_scales, size_t n_scales, double *out);
+/* QuantTensor::matmul for INT8 x INT8 and INT4 x INT4 (matmul_int8 /
+ * matmul_int4, src/quantize.rs:447-515) on the device: A [M, K] and B [K, N]
+ * code buffers (row-major), out f64 [M, N] = (f64)(i32 wrapping sum of
+ * (a - a_zero_point)(b - b_zero_point)) * a_scale * b_scale. Bit-exact with
+ * the reference. Other format pairs: VXB_EUNSUPPORTED. */
+int vxb_quant_matmul(vxb_ctx *ctx, int fmt, const uint8_t *d_a, const uint8_t *d_b, int M, int K, int N,
+                     double a_scale, double b_scale, int64_t a_zero_point, int64_t b_zero_point, double *d_out,
+                     void *stream);
+
+/* ------------------------------------------------------------------------ */
 /* Tiled weights: the kernels' HBM layout of a weight matrix W [N, K]         */
 /* (row-major, K % 32 == 0). The same codes and f16 scales as the GGUF       */
 /* blocks, regrouped so that each warp reads 512 contiguous bytes per load    */

@@ -41,14 +41,15 @@ def _plan(L, ctx, fmt, N, K, B, static):
     return kern.value, splits.value, cl.value
 
 
-# (format, N, K, batch, expected path): "stream" = per-warp stream kernel,
+# (format, N, K, batch, expected path or None where the occupancy-driven
+# planner may pick either): "stream" = per-warp stream kernel,
 # "single" = group kernel without a split, "cluster" = group kernel whose
 # splits add through distributed shared memory, "global" = group kernel whose
 # splits add through partial sums in the fixed array
 CASES = [("Q4_0", 4096, 4096, 1, "stream"), ("Q4_0", 11008, 4096, 3, "stream"),
-         ("Q8_0", 1000, 160, 3, "single"), ("Q8_0", 11008, 4096, 4, None),
+         ("Q8_0", 1000, 160, 3, None), ("Q8_0", 11008, 4096, 4, None),
          ("Q4_0", 4096, 11008, 32, None), ("Q4_0", 1024, 16384, 16, "global"),
-         ("Q8_0", 512, 8192, 9, "global")]
+         ("Q8_0", 512, 8192, 9, "global"), ("Q8_0", 2048, 128, 9, "single")]
 
 
 def _path(kern, splits, cl):

@@ -63,6 +63,11 @@ SIGNATURES = {
     "vxb_unpack_blocks": (_I, [_I, _P, _SZ, _P]),
     "vxb_quantize_blocks": (_I, [_P, _I, _P, _SZ, _P, _P]),
     "vxb_dequantize_blocks": (_I, [_P, _I, _P, _SZ, _P, _P]),
+    "vxb_qt_data_bytes": (_SZ, [_I, _SZ]),
+    "vxb_qt_num_groups": (_SZ, [_SZ, _SZ]),
+    "vxb_qt_quantize": (_I, [_I, _P, _SZ, _SZ, _P, _P, _P]),
+    "vxb_qt_mean_scale": (_I, [_P, _SZ, _P]),
+    "vxb_quant_matmul": (_I, [_P, _I, _P, _P, _I, _I, _I, ctypes.c_double, ctypes.c_double, _I64, _I64, _P, _P]),
     "vxb_tiled_bytes": (_SZ, [_I, _I, _I]),
     "vxb_tile_weights": (_I, [_P, _I, _P, _I, _I, _P, _P]),
     "vxb_untile_weights": (_I, [_P, _I, _P, _I, _I, _P, _P]),

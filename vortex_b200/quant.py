@@ -201,3 +201,100 @@ def weight_only_matmul(w: TiledWeight, activations):
     out = torch.empty((M, w.N), dtype=torch.float32, device=x.device)
     w.gemv(x, out=out)
     return out
+
+
+# ---------------------------------------------------------------- QuantTensor (mean-scale int matmul)
+
+QT_INT8 = 0
+QT_INT4 = 1
+_QT_FORMATS = {"INT8": QT_INT8, "INT4": QT_INT4}
+
+
+class QuantTensor:
+    """Mirror of QuantTensor (src/quantize.rs:70-94) for the INT8 and INT4
+    formats: codes (`data`), shape, and a PerTensor (group_size None) or
+    PerGroup scheme with f64 scales and zero points. quantize / dequantize run
+    on the host (the reference's rules); matmul runs on the device
+    (vxb_quant_matmul, bit-exact with QuantTensor::matmul)."""
+
+    def __init__(self, data, shape, fmt, scales, zero_points, group_size=None):
+        self.data = np.ascontiguousarray(data, dtype=np.uint8)
+        self.shape = tuple(int(s) for s in shape)
+        self.fmt = _QT_FORMATS[fmt.upper()] if isinstance(fmt, str) else int(fmt)
+        if self.fmt not in (QT_INT8, QT_INT4):
+            raise N.VxbError(N.VXB_EINVAL, f"QuantTensor: format {fmt} (INT8 or INT4)")
+        self.scales = np.ascontiguousarray(scales, dtype=np.float64)
+        self.zero_points = np.ascontiguousarray(zero_points, dtype=np.int64)
+        self.group_size = group_size
+
+    @property
+    def numel(self) -> int:
+        return int(np.prod(self.shape)) if self.shape else 1
+
+    @classmethod
+    def quantize(cls, data, shape, fmt, group_size=None):
+        """QuantTensor::quantize (src/quantize.rs:81-163) for INT8 / INT4."""
+        f = _QT_FORMATS[fmt.upper()] if isinstance(fmt, str) else int(fmt)
+        a = np.ascontiguousarray(data, dtype=np.float64).ravel()
+        if a.size != int(np.prod(shape)):
+            raise N.VxbError(N.VXB_EINVAL, "quantize: data length must match shape product")
+        gs = int(group_size) if group_size else 0
+        L = N.lib()
+        packed = np.zeros(max(L.vxb_qt_data_bytes(f, a.size), 1), dtype=np.uint8)
+        ng = max(L.vxb_qt_num_groups(a.size, gs), 1)
+        scales = np.zeros(ng, dtype=np.float64)
+        zps = np.zeros(ng, dtype=np.int64)
+        N.check(L.vxb_qt_quantize(f, _ptr(a), a.size, gs, _ptr(packed), _ptr(scales), _ptr(zps)))
+        nb = L.vxb_qt_data_bytes(f, a.size)
+        ng = L.vxb_qt_num_groups(a.size, gs)
+        return cls(packed[:nb], shape, f, scales[:max(ng, 1)], zps[:max(ng, 1)], gs or None)
+
+    def codes(self) -> np.ndarray:
+        """The signed codes (unpack_int4 for INT4, src/quantize.rs:675-687)."""
+        if self.fmt == QT_INT8:
+            return self.data.view(np.int8).astype(np.int64)
+        lo = (self.data & 0xF).astype(np.int64)
+        hi = (self.data >> 4).astype(np.int64)
+        q = np.stack([lo, hi], axis=1).ravel()
+        return (q ^ 8) - 8
+
+    def dequantize(self) -> np.ndarray:
+        """QuantTensor::dequantize for INT8 / INT4 (src/quantize.rs:325-370):
+        (q - zp) as f64 * scale per element of its group."""
+        q = self.codes()[:self.numel]
+        if self.group_size is None:
+            return (q - int(self.zero_points[0])).astype(np.float64) * float(self.scales[0])
+        g = np.arange(q.size) // self.group_size
+        return (q - self.zero_points[g]).astype(np.float64) * self.scales[g]
+
+    def get_scale(self) -> float:
+        """get_scale (src/quantize.rs:534-545): the scale, or the mean of the
+        group scales."""
+        if self.group_size is None:
+            return float(self.scales[0])
+        out = ctypes.c_double()
+        s = self.scales
+        N.check(N.lib().vxb_qt_mean_scale(_ptr(s), s.size, ctypes.byref(out)))
+        return out.value
+
+    def get_zero_point(self) -> int:
+        return int(self.zero_points[0]) if self.group_size is None else 0
+
+    def matmul(self, other: "QuantTensor", device=None) -> np.ndarray:
+        """QuantTensor::matmul for INT8 x INT8 / INT4 x INT4 (src/quantize.rs:
+        447-515) on the device: f64 [m * n]."""
+        torch = _torch()
+        if len(self.shape) != 2 or len(other.shape) != 2 or self.shape[1] != other.shape[0]:
+            raise N.VxbError(N.VXB_EINVAL, "matmul: shapes must be [m, k] x [k, n]")
+        if self.fmt != other.fmt:
+            raise N.VxbError(N.VXB_EUNSUPPORTED, "matmul: mixed formats take the dequantize fallback")
+        m, k = self.shape
+        n = other.shape[1]
+        dev = torch.device("cuda", torch.cuda.current_device() if device is None else int(device))
+        a = torch.from_numpy(self.data).to(dev)
+        b = torch.from_numpy(other.data).to(dev)
+        out = torch.empty(m * n, dtype=torch.float64, device=dev)
+        context(dev.index).call("vxb_quant_matmul", self.fmt, _dptr(a), _dptr(b), m, k, n,
+                                ctypes.c_double(self.get_scale()), ctypes.c_double(other.get_scale()),
+                                self.get_zero_point(), other.get_zero_point(), _dptr(out), _stream_ptr())
+        return out.cpu().numpy()
