@@ -263,6 +263,33 @@ int vxb_swiglu(vxb_ctx *ctx, const float *d_gu, int rows, int ffn, uint16_t *d_a
 /* argmax, stdlib/ai/transformer.vx:1163-1177 (first index of the maximum). */
 int vxb_argmax(vxb_ctx *ctx, const float *d_logits, int rows, int vocab, int32_t *d_out, void *stream);
 
+/* sample_top_p, stdlib/ai/transformer.vx:1179-1260 (with the file's series
+ * _exp, 36-80), for each of `rows` rows of f32 logits [rows, vocab]:
+ * probabilities of logit / temperature in f64, the exchange-sort order by
+ * descending probability, the cutoff where the cumulative sum reaches top_p,
+ * and the draw u = ((1664525 * h_seeds[r] + 1013904223) mod 2^31) / 2^31 over
+ * the renormalised prefix; d_out[r] gets the token. Bit-matched to the
+ * reference (ties included). vocab <= 131072. Synchronous on `stream`. */
+int vxb_sample_top_p(vxb_ctx *ctx, const float *d_logits, int rows, int vocab, double temperature, double top_p,
+                     const int64_t *h_seeds, int32_t *d_out, void *stream);
+
+/* ContinuousBatcher (src/kv_cache.rs:117-154) and the batcher_* builtins
+ * (188-290): max_batch_size slots; add takes the lowest free slot and the
+ * next sequence id (ids are never reused) and fails with VXB_ENOBLOCKS
+ * "batcher full" when every slot is taken; remove frees a slot (a bad slot is
+ * ignored, as the reference); num_active counts the taken slots. */
+typedef struct vxb_batcher vxb_batcher;
+int vxb_batcher_create(int max_batch_size, vxb_batcher **out);
+int vxb_batcher_destroy(vxb_batcher *b);
+int vxb_batcher_add(vxb_batcher *b, const uint64_t *h_tokens, size_t n_tokens, int *slot_out);
+int vxb_batcher_remove(vxb_batcher *b, int slot);
+int vxb_batcher_num_active(const vxb_batcher *b, int *out);
+/* the BatchSlot fields of a taken slot (any output may be NULL) */
+int vxb_batcher_slot(const vxb_batcher *b, int slot, int64_t *seq_id, int64_t *position, int *is_prefill,
+                     int *is_done, size_t *n_tokens);
+/* after a step: position += n, is_prefill cleared, is_done set when done != 0 */
+int vxb_batcher_advance(vxb_batcher *b, int slot, int64_t n, int done);
+
 /* ------------------------------------------------------------------------ */
 /* Tensor-parallel communicator. Replaces the nccl_ffi.rs externs            */
 /* (src/nccl_ffi.rs:12-72): NCCL (opened at run time) over NVLink/NVSwitch. */

@@ -72,6 +72,10 @@ def lib():
             "vxo_rmsnorm_bias": (None, [_P, _P, _P, _SZ, ctypes.c_double, _P]),
             "vxo_rope_embed": (None, [_P, _SZ, ctypes.c_int64, ctypes.c_int64, _P]),
             "vxo_silu": (ctypes.c_double, [ctypes.c_double]),
+            "vxo_vx_exp": (ctypes.c_double, [ctypes.c_double]),
+            "vxo_argmax": (ctypes.c_int64, [_P, _SZ]),
+            "vxo_lcg_uniform": (ctypes.c_double, [ctypes.c_int64]),
+            "vxo_sample_top_p": (ctypes.c_int64, [_P, _SZ, ctypes.c_double, ctypes.c_double, ctypes.c_int64]),
             "vxo_matvec": (None, [_P, _P, _SZ, _SZ, _P]),
             "vxo_tf_param_count": (_SZ, [_P]),
             "vxo_tf_init": (None, [_P, ctypes.c_uint64, _P]),
@@ -434,3 +438,22 @@ def tf_forward(cfg: TFConfig, params, tokens, mask=None) -> np.ndarray:
     m = _f32(mask) if mask is not None else None
     lib().vxo_tf_forward(ctypes.byref(cfg), _p(p), _p(t), S, _p(m) if m is not None else None, _p(out))
     return out
+
+
+# ---- sampling (stdlib/ai/transformer.vx:36-80, 1163-1260) ----
+def vx_exp(x: float) -> float:
+    return lib().vxo_vx_exp(float(x))
+
+
+def argmax(logits) -> int:
+    a = _f64(logits)
+    return int(lib().vxo_argmax(_p(a), a.size))
+
+
+def lcg_uniform(seed: int) -> float:
+    return lib().vxo_lcg_uniform(int(seed))
+
+
+def sample_top_p(logits, temperature: float, top_p: float, seed: int) -> int:
+    a = _f64(logits)
+    return int(lib().vxo_sample_top_p(_p(a), a.size, float(temperature), float(top_p), int(seed)))

@@ -117,6 +117,12 @@ void vxo_tf_softmax_rows(const float *x, size_t rows, size_t cols, float *y);
 void vxo_tf_forward(const vxo_tf_config *c, const float *params, const int64_t *tokens, size_t S, const float *mask,
                     float *logits);
 
+/* ---- sampling (stdlib/ai/transformer.vx:36-80, 1163-1260), oracle/vxo_sample.c ---- */
+double vxo_vx_exp(double x);
+int64_t vxo_argmax(const double *logits, size_t n);
+double vxo_lcg_uniform(int64_t seed);
+int64_t vxo_sample_top_p(const double *logits, size_t n, double temperature, double top_p, int64_t seed);
+
 /* ---- int dot primitives (src/bytecarry.rs:491-513) ---- */
 int32_t vxo_int8_dot(const int8_t *a, const int8_t *b, size_t n);
 int32_t vxo_int4_dot(const uint8_t *a, const uint8_t *b, size_t nbytes);

@@ -89,6 +89,14 @@ SIGNATURES = {
     "vxb_rmsnorm": (_I, [_P, _P, _P, _P, _I, _I, ctypes.c_float, _P, _P]),
     "vxb_swiglu": (_I, [_P, _P, _I, _I, _P, _P]),
     "vxb_argmax": (_I, [_P, _P, _I, _I, _P, _P]),
+    "vxb_sample_top_p": (_I, [_P, _P, _I, _I, ctypes.c_double, ctypes.c_double, _P, _P, _P]),
+    "vxb_batcher_create": (_I, [_I, ctypes.POINTER(_P)]),
+    "vxb_batcher_destroy": (_I, [_P]),
+    "vxb_batcher_add": (_I, [_P, _P, _SZ, ctypes.POINTER(_I)]),
+    "vxb_batcher_remove": (_I, [_P, _I]),
+    "vxb_batcher_num_active": (_I, [_P, ctypes.POINTER(_I)]),
+    "vxb_batcher_slot": (_I, [_P, _I, _P, _P, _P, _P, _P]),
+    "vxb_batcher_advance": (_I, [_P, _I, _I64, _I]),
     "vxb_nccl_unique_id": (_I, [_P]),
     "vxb_comm_init": (_I, [_P, _I, _I, _P, ctypes.POINTER(_P)]),
     "vxb_comm_destroy": (_I, [_P]),
