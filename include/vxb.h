@@ -44,6 +44,11 @@ extern "C" {
  * (src/gguf_loader.rs:61-75) */
 #define VXB_Q4_0 2
 #define VXB_Q8_0 8
+/* further GGUF tensor types (dequantize, upload and GEMV over their raw
+ * rows; the tiled kernels take Q4_0 / Q8_0) */
+#define VXB_GGML_F32 0
+#define VXB_GGML_F16 1
+#define VXB_Q4_1 3
 
 /* element types */
 #define VXB_F32 0
@@ -100,7 +105,9 @@ size_t vxb_block_bytes(int fmt, size_t n_elements);
 /* Replaces QuantTensor::quantize (src/quantize.rs:81-163) + pack_int4 (664). */
 int vxb_pack_blocks_f64(int fmt, const double *h_w, size_t n, uint8_t *h_blocks);
 int vxb_pack_blocks_f32(int fmt, const float *h_w, size_t n, uint8_t *h_blocks);
-/* Replaces dequantize_q4_0 / dequantize_q8_0 (src/gguf_loader.rs:413-498). */
+/* Replaces dequantize_q4_0 / dequantize_q4_1 / dequantize_q8_0 /
+ * dequantize_f16 / copy_f32 (src/gguf_loader.rs:413-531): fmt any of the
+ * GGUF types above (vxb_block_bytes gives their sizes). */
 int vxb_unpack_blocks(int fmt, const uint8_t *h_blocks, size_t n, float *h_out);
 
 /* Device quantizer: f32 weights on the device -> GGUF blocks on the device,
@@ -108,7 +115,8 @@ int vxb_unpack_blocks(int fmt, const uint8_t *h_blocks, size_t n, float *h_out);
  * weights that already live in HBM. */
 int vxb_quantize_blocks(vxb_ctx *ctx, int fmt, const float *d_w, size_t n, uint8_t *d_blocks,
                         void *stream);
-/* Device dequantizer (gguf_loader.rs dequantize_q*_0 on the device). */
+/* Device dequantizer (the gguf_loader.rs dequantizers on the device, every
+ * GGUF type above; bit-identical with vxb_unpack_blocks). */
 int vxb_dequantize_blocks(vxb_ctx *ctx, int fmt, const uint8_t *d_blocks, size_t n, float *d_out,
                           void *stream);
 
@@ -162,6 +170,13 @@ int vxb_untile_weights(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K,
 /* ------------------------------------------------------------------------ */
 int vxb_gemv_q(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const uint16_t *d_x,
                int batch, int y_dtype, void *d_y, void *stream);
+/* The same product over a tensor kept as its GGUF rows (row n = the blocks
+ * of W[n, :], vxb_block_bytes(type, K) bytes), for every GGUF type above
+ * (F32, F16, Q4_0, Q4_1, Q8_0; K % 32 == 0 for the block types): the weights
+ * are the reference's dequantized f32 values (src/gguf_loader.rs:413-531),
+ * accumulated in f32. Any batch >= 1. */
+int vxb_gemv_blocks(vxb_ctx *ctx, int type, const void *d_rows, int N, int K, const uint16_t *d_x, int batch,
+                    int y_dtype, void *d_y, void *stream);
 /* The same GEMV for callers that cannot allocate device memory (no
  * counterpart in the reference: it exists for embedders whose runtime owns
  * all device memory, or that must not add allocations mid-run). Scratch lives
@@ -386,6 +401,10 @@ int vxb_gguf_meta_float(const vxb_gguf *g, const char *key, double *value);
 int vxb_gguf_meta_string(const vxb_gguf *g, const char *key, char *out, size_t cap, size_t *len);
 int vxb_gguf_upload_tiled(vxb_ctx *ctx, const vxb_gguf *g, int64_t index, void *d_tiled, size_t tiled_bytes,
                           void *stream);
+/* Any tensor's bytes as stored in the file (F32, F16, Q4_0, Q4_1, Q8_0 rows
+ * of blocks, no conversion) into a device buffer of at least its size;
+ * synchronous. For vxb_gemv_blocks and vxb_dequantize_blocks. */
+int vxb_gguf_upload(vxb_ctx *ctx, const vxb_gguf *g, int64_t index, void *d_dst, size_t dst_bytes, void *stream);
 
 /* ------------------------------------------------------------------------ */
 /* f32 GPT-style model of src/transformer.rs:15-841 (TransformerModel):      */

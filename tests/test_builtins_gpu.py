@@ -58,6 +58,13 @@ def test_kv_cache_builtin_errors(cuda_ok):
         B.kv_cache_append(cid, 0, 0, [0.5] * 64, [1.0] * 64)
     with pytest.raises(B.BuiltinError, match="KV cache out of blocks"):
         B.kv_cache_append(cid, 0, 0, [0.5] * 64, [1.0] * 64)
+    with pytest.raises(B.BuiltinError, match="KV cache out of blocks"):
+        B.kv_cache_append(cid, 0, 7, [0.5] * 64, [1.0] * 64)
+    # the failed append of a new sequence leaves its (empty) table, as the reference
+    assert B.kv_cache_stats(cid) == {"used_blocks": 2, "free_blocks": 0, "block_size": 2, "num_seqs": 2}
+    B.kv_cache_free_seq(cid, 0)
+    assert B.kv_cache_stats(cid)["used_blocks"] == 0
+    assert B.kv_cache_append(cid, 0, 7, [0.5] * 64, [1.0] * 64) is True
     with pytest.raises(B.BuiltinError, match="invalid cache"):
         B.kv_cache_stats(cid + 1000)
     with pytest.raises(B.BuiltinError, match="need cache_id"):

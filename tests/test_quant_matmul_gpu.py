@@ -35,14 +35,14 @@ def test_quant_matmul_bit_exact(cuda_ok, fmt, m, k, n, gs):
 @pytest.mark.parametrize("fmt", ["INT8", "INT4"])
 def test_quant_matmul_zero_points_and_wrapping(cuda_ok, fmt):
     """PerTensor zero points (the quantized_matmul builtin's tensors carry the
-    _zero_point field) and sums far past the i32 range, which wrap."""
+    _zero_point field) and sums far outside the i32 range, which wrap."""
     from vortex_b200.quant import QuantTensor
     m, k, n = 3, 40000, 5
     hi = 127 if fmt == "INT8" else 7
     lo = -128 if fmt == "INT8" else -8
     rng = np.random.default_rng(9)
-    qa = np.where(rng.random(m * k) < 0.9, lo, hi).astype(np.int64)
-    qb = np.where(rng.random(k * n) < 0.9, lo, hi).astype(np.int64)
+    qa = np.where(rng.random(m * k) < 0.95, hi, lo).astype(np.int64)
+    qb = np.where(rng.random(k * n) < 0.95, lo, hi).astype(np.int64)
 
     def pack(q):
         if fmt == "INT8":
@@ -52,16 +52,16 @@ def test_quant_matmul_zero_points_and_wrapping(cuda_ok, fmt):
             q = np.append(q, 0)
         return (q[0::2] | (q[1::2] << 4)).astype(np.uint8)
 
-    for za, zb in ((0, 0), (3, -2), (-100, 7)):
+    zps = ((0, 0), (3, -2), (-128, 127)) if fmt == "INT8" else ((0, 0), (3, -2), (-1000, 1000))
+    for za, zb in zps:
         a = QuantTensor(pack(qa), (m, k), fmt, [0.5], [za])
         b = QuantTensor(pack(qb), (k, n), fmt, [0.25], [zb])
         got = a.matmul(b)
         want = O.matmul_int(a.data, b.data, OF[fmt], m, k, n, 0.5, 0.25, za, zb)
         assert np.array_equal(got, want), (za, zb)
-    # the sums do leave the i32 range (with za = -100 for INT8: ~ 40000 * 227 * 130)
-    exact = ((qa.reshape(m, k) + 100) @ (qb.reshape(k, n) - 7)).astype(np.float64) * 0.125
-    if fmt == "INT8":
-        assert not np.array_equal(got.reshape(m, n), exact)
+    # with the last zero points the exact sums leave the i32 range
+    exact = (qa.reshape(m, k) - zps[-1][0]) @ (qb.reshape(k, n) - zps[-1][1])
+    assert np.all(np.abs(exact) > 2 ** 31)
 
 
 def test_quant_matmul_reference_kat(cuda_ok):

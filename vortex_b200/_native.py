@@ -25,6 +25,8 @@ VXB_ENCCL = -8
 
 Q4_0 = 2
 Q8_0 = 8
+Q4_1 = 3
+GGML_F32, GGML_F16 = 0, 1
 F32, BF16, F16, I8 = 0, 1, 2, 3
 
 _STATUS_NAMES = {0: "VXB_OK", -1: "VXB_EINVAL", -2: "VXB_ECUDA", -3: "VXB_ENOMEM", -4: "VXB_ETIMEOUT",
@@ -72,6 +74,7 @@ SIGNATURES = {
     "vxb_tile_weights": (_I, [_P, _I, _P, _I, _I, _P, _P]),
     "vxb_untile_weights": (_I, [_P, _I, _P, _I, _I, _P, _P]),
     "vxb_gemv_q": (_I, [_P, _I, _P, _I, _I, _P, _I, _I, _P, _P]),
+    "vxb_gemv_blocks": (_I, [_P, _I, _P, _I, _I, _P, _I, _I, _P, _P]),
     "vxb_gemv_q_static": (_I, [_P, _I, _P, _I, _I, _P, _I, _I, _P, _P]),
     "vxb_gemv_plan_info": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P]),
     "vxb_kv_create": (_I, [_P, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_P)]),
@@ -123,6 +126,7 @@ SIGNATURES = {
     "vxb_gguf_meta_float": (_I, [_P, ctypes.c_char_p, _P]),
     "vxb_gguf_meta_string": (_I, [_P, ctypes.c_char_p, _P, _SZ, _P]),
     "vxb_gguf_upload_tiled": (_I, [_P, _P, _I64, _P, _SZ, _P]),
+    "vxb_gguf_upload": (_I, [_P, _P, _I64, _P, _SZ, _P]),
     "vxb_tmodel_create": (_I, [_P, _P, ctypes.POINTER(_P)]),
     "vxb_tmodel_destroy": (_I, [_P]),
     "vxb_tmodel_param_count": (_I, [_P, ctypes.POINTER(_SZ)]),

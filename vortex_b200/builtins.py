@@ -145,14 +145,28 @@ _BATCHERS: list = []
 
 
 class _OneHeadCache:
-    """A kv_cache_new cache: the reference's cache is head-agnostic (each
+    """A kv_cache_new cache. The reference's cache is head-agnostic (each
     appended key / value is one head_dim vector), so the device cache holds
-    one KV head; num_heads is kept for the record as the reference does."""
+    one KV head (num_heads is kept for the record, as the reference does).
+    The block accounting the builtins report (stats, memory, the out-of-blocks
+    error) is the reference's own, kept here per (layer, seq_id) table:
+    a table takes ceil(len / block_size) of max_blocks blocks, a table entry
+    exists from its first append attempt on (src/kv_cache.rs:54-67). The
+    device pages hold 16 tokens (a multiple of 16 at least block_size), so
+    max_blocks device pages always suffice."""
 
     def __init__(self, nl, nh, hd, bs, mb):
         from . import kv_cache as KV
-        self.num_heads, self.head_dim, self.block_size, self.max_blocks = nh, hd, bs, mb
-        self.cache = KV.PagedKVCache(nl, 1, hd, bs, max_blocks=mb, max_seqs=max(64, mb), max_blocks_per_seq=mb)
+        if nl < 1 or bs < 1 or mb < 0:
+            raise BuiltinError("kv_cache_new: num_layers, block_size and max_blocks must be positive")
+        self.num_layers, self.num_heads, self.head_dim, self.block_size, self.max_blocks = nl, nh, hd, bs, mb
+        self.tables = {}  # (layer, seq) -> tokens
+        dev_bs = 16 * -(-bs // 16)
+        self.cache = KV.PagedKVCache(nl, 1, hd, dev_bs, max_blocks=max(mb, 1), max_seqs=max(64, mb),
+                                     max_blocks_per_seq=max(mb, 1))
+
+    def used_blocks(self):
+        return sum(-(-n // self.block_size) for n in self.tables.values())
 
 
 def _int_arg(args, i, default=None, err=None):
@@ -201,15 +215,15 @@ def kv_cache_append(*args):
     c = _cache(cid)
     if key.size != c.head_dim or value.size != c.head_dim:
         raise BuiltinError(f"kv_cache_append: key and value must hold head_dim = {c.head_dim} values")
+    if not 0 <= layer < c.num_layers:
+        raise BuiltinError(f"kv_cache_append: layer {layer} out of range")
+    n = c.tables.setdefault((layer, seq), 0)
+    if n % c.block_size == 0 and c.used_blocks() >= c.max_blocks:
+        raise BuiltinError("KV cache out of blocks")
     k = torch.from_numpy(key.astype(np.float32)).cuda().to(torch.bfloat16).reshape(1, 1, -1)
     v = torch.from_numpy(value.astype(np.float32)).cuda().to(torch.bfloat16).reshape(1, 1, -1)
-    from . import _native as N
-    try:
-        c.cache.append_kv(layer, [seq], k, v)
-    except N.VxbError as e:
-        if e.code == N.VXB_ENOBLOCKS:
-            raise BuiltinError("KV cache out of blocks") from None
-        raise
+    c.cache.append_kv(layer, [seq], k, v)
+    c.tables[(layer, seq)] = n + 1
     return True
 
 
@@ -234,15 +248,18 @@ def kv_cache_stats(*args):
     """kv_cache_stats(cache_id) -> KVCacheStats {used_blocks, free_blocks,
     block_size, num_seqs} (num_seqs = block tables, one per (layer, seq))."""
     cid = _int_arg(args, 0, err="need cache_id")
-    s = _cache(cid).cache.stats()
-    return {"used_blocks": s["used_blocks"], "free_blocks": s["free_blocks"], "block_size": s["block_size"],
-            "num_seqs": s["num_seqs"]}
+    c = _cache(cid)
+    used = c.used_blocks()
+    return {"used_blocks": used, "free_blocks": c.max_blocks - used, "block_size": c.block_size,
+            "num_seqs": len(c.tables)}
 
 
 def kv_cache_free_seq(*args):
     cid = _int_arg(args, 0, err="need cache_id")
     seq = _int_arg(args, 1, err="need seq_id")
-    _cache(cid).cache.free_seq(seq)
+    c = _cache(cid)
+    c.tables = {key: n for key, n in c.tables.items() if key[1] != seq}
+    c.cache.free_seq(seq)
     return True
 
 
@@ -251,7 +268,7 @@ def kv_cache_memory(*args):
     hold: used_blocks * block_size * head_dim * 2 * 8."""
     cid = _int_arg(args, 0, err="need cache_id")
     c = _cache(cid)
-    return c.cache.stats()["used_blocks"] * c.block_size * c.head_dim * 2 * 8
+    return c.used_blocks() * c.block_size * c.head_dim * 2 * 8
 
 
 def batcher_new(*args):

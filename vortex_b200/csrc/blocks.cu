@@ -161,6 +161,28 @@ __global__ void dequantize_blocks_kernel(const uint8_t *__restrict__ blocks, siz
   }
 }
 
+// GGUF types beyond the kernels' storage formats (src/gguf_loader.rs:443-531):
+// Q4_1 (20 bytes: f16 d, f16 m, 16 nibble bytes; x = nibble * d + m with the
+// multiply and the add rounded separately), F16 (the reference's f16_to_f32,
+// subnormals included) and F32 (the bytes as they are).
+__global__ void dequantize_ggml_kernel(const uint8_t *__restrict__ data, size_t n, float *__restrict__ out, int type) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  if (type == VXB_Q4_1) {
+    const uint8_t *blk = data + (i / 32) * 20;
+    const float d = ref_f16_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8));
+    const float m = ref_f16_to_f32((uint32_t)blk[2] | ((uint32_t)blk[3] << 8));
+    const uint8_t byte = blk[4 + (i % 32) / 2];
+    const int nib = (i & 1) ? (byte >> 4) : (byte & 0xF);
+    out[i] = __fadd_rn(__fmul_rn((float)nib, d), m);
+  } else if (type == VXB_GGML_F16) {
+    out[i] = ref_f16_to_f32((uint32_t)data[2 * i] | ((uint32_t)data[2 * i + 1] << 8));
+  } else {
+    out[i] = __uint_as_float((uint32_t)data[4 * i] | ((uint32_t)data[4 * i + 1] << 8) |
+                             ((uint32_t)data[4 * i + 2] << 16) | ((uint32_t)data[4 * i + 3] << 24));
+  }
+}
+
 // ---------------- tiled layout ----------------
 
 __global__ void tile_header_kernel(uint32_t *hdr, int fmt, int N, int K) {
@@ -292,6 +314,10 @@ __global__ void untile_kernel(const uint8_t *__restrict__ tiled, int fmt, int N,
   }
 }
 
+bool ggml_fmt(int fmt) {
+  return fmt == VXB_Q4_0 || fmt == VXB_Q8_0 || fmt == VXB_Q4_1 || fmt == VXB_GGML_F16 || fmt == VXB_GGML_F32;
+}
+
 int check_fmt(vxb_ctx *ctx, int fmt, const char *who) {
   if (fmt != VXB_Q4_0 && fmt != VXB_Q8_0) return set_error(ctx, VXB_EINVAL, "%s: unknown block format %d", who, fmt);
   return VXB_OK;
@@ -302,6 +328,9 @@ int check_fmt(vxb_ctx *ctx, int fmt, const char *who) {
 VXB_API size_t vxb_block_bytes(int fmt, size_t n) {
   if (fmt == VXB_Q4_0) return (n + 31) / 32 * 18;
   if (fmt == VXB_Q8_0) return (n + 31) / 32 * 34;
+  if (fmt == VXB_Q4_1) return (n + 31) / 32 * 20;
+  if (fmt == VXB_GGML_F16) return n * 2;
+  if (fmt == VXB_GGML_F32) return n * 4;
   return 0;
 }
 
@@ -318,8 +347,25 @@ VXB_API int vxb_pack_blocks_f32(int fmt, const float *w, size_t n, uint8_t *out)
 }
 
 VXB_API int vxb_unpack_blocks(int fmt, const uint8_t *blocks, size_t n, float *out) {
-  if (check_fmt(nullptr, fmt, "vxb_unpack_blocks")) return VXB_EINVAL;
+  if (!ggml_fmt(fmt)) return set_error(nullptr, VXB_EINVAL, "vxb_unpack_blocks: unknown block format %d", fmt);
   if (n && (!blocks || !out)) return set_error(nullptr, VXB_EINVAL, "vxb_unpack_blocks: null argument");
+  if (fmt == VXB_Q4_1 || fmt == VXB_GGML_F16 || fmt == VXB_GGML_F32) {
+    for (size_t i = 0; i < n; i++) {
+      if (fmt == VXB_Q4_1) {
+        const uint8_t *blk = blocks + (i / 32) * 20;
+        const float d = host_ref_f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+        const float m = host_ref_f16_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
+        const uint8_t byte = blk[4 + (i % 32) / 2];
+        volatile float prod = (float)((i & 1) ? (byte >> 4) : (byte & 0xF)) * d;  // rounded before the add
+        out[i] = prod + m;
+      } else if (fmt == VXB_GGML_F16) {
+        out[i] = host_ref_f16_to_f32((uint16_t)(blocks[2 * i] | (blocks[2 * i + 1] << 8)));
+      } else {
+        std::memcpy(out + i, blocks + 4 * i, 4);
+      }
+    }
+    return VXB_OK;
+  }
   for (size_t i = 0; i < n; i++) {
     size_t b = i / 32, e = i % 32;
     if (fmt == VXB_Q4_0) {
@@ -354,10 +400,14 @@ VXB_API int vxb_quantize_blocks(vxb_ctx *ctx, int fmt, const float *d_w, size_t 
 VXB_API int vxb_dequantize_blocks(vxb_ctx *ctx, int fmt, const uint8_t *d_blocks, size_t n, float *d_out,
                                   void *stream) {
   if (!ctx) return set_error(nullptr, VXB_EINVAL, "vxb_dequantize_blocks: null context");
-  if (int rc = check_fmt(ctx, fmt, "vxb_dequantize_blocks")) return rc;
+  if (!ggml_fmt(fmt)) return set_error(ctx, VXB_EINVAL, "vxb_dequantize_blocks: unknown block format %d", fmt);
   if (n == 0) return VXB_OK;
   if (!d_blocks || !d_out) return set_error(ctx, VXB_EINVAL, "vxb_dequantize_blocks: null pointer");
   if (int rc = use_device(ctx)) return rc;
+  if (fmt != VXB_Q4_0 && fmt != VXB_Q8_0) {
+    dequantize_ggml_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(d_blocks, n, d_out, fmt);
+    return launch_check(ctx, "dequantize_ggml_kernel");
+  }
   dequantize_blocks_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(d_blocks, n, d_out,
                                                                                           fmt == VXB_Q4_0);
   return launch_check(ctx, "dequantize_blocks_kernel");

@@ -428,3 +428,21 @@ VXB_API int vxb_gguf_upload_tiled(vxb_ctx *ctx, const vxb_gguf *g, int64_t i, vo
   cudaFree(d_blocks);
   return rc;
 }
+
+VXB_API int vxb_gguf_upload(vxb_ctx *ctx, const vxb_gguf *g, int64_t i, void *d_dst, size_t dst_bytes, void *stream) {
+  if (!ctx || !g || !d_dst) return set_error(ctx, VXB_EINVAL, "vxb_gguf_upload: null argument");
+  const void *src = nullptr;
+  uint64_t nbytes = 0;
+  if (int rc = vxb_gguf_tensor(g, i, nullptr, 0, nullptr, nullptr, nullptr, nullptr, &nbytes, &src)) {
+    set_error(ctx, rc, "%s", vxb_last_error(nullptr));
+    return rc;
+  }
+  if (dst_bytes < nbytes)
+    return set_error(ctx, VXB_EINVAL, "vxb_gguf_upload: buffer of %zu bytes, the tensor holds %llu", dst_bytes,
+                     (unsigned long long)nbytes);
+  if (int rc = use_device(ctx)) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  VXB_CUDA_TRY(ctx, cudaMemcpyAsync(d_dst, src, nbytes, cudaMemcpyHostToDevice, st));
+  VXB_CUDA_TRY(ctx, cudaStreamSynchronize(st));  // the mapping may be closed right after
+  return VXB_OK;
+}

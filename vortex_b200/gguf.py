@@ -138,6 +138,25 @@ class GGUFFile:
         ctx.call("vxb_gguf_upload_tiled", self.ptr, i, ctypes.c_void_p(tiled.data_ptr()), nbytes, Q._stream_ptr())
         return Q.TiledWeight.from_tiled(tiled, info["type"], rows, K)
 
+    def upload(self, name: str, device=None):
+        """Any tensor (F32, F16, Q4_0, Q4_1, Q8_0) as its GGUF bytes on the
+        GPU, wrapped as a BlockRows (rows = product of the dimensions after the
+        first, K = the first): dequantize() or gemv() over it on the device."""
+        import torch
+
+        from . import quant as Q
+        i = self.find(name)
+        info = self.tensor_info(i)
+        K = info["dims"][0]
+        rows = int(np.prod(info["dims"][1:])) if len(info["dims"]) > 1 else 1
+        nbytes = N.lib().vxb_block_bytes(info["type"], rows * K)
+        if nbytes == 0:
+            raise GGUFError(N.VXB_EUNSUPPORTED, f"tensor '{name}' has ggml type {info['type']}")
+        ctx = Q.context(device)
+        buf = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{ctx.device}")
+        ctx.call("vxb_gguf_upload", self.ptr, i, ctypes.c_void_p(buf.data_ptr()), nbytes, Q._stream_ptr())
+        return Q.BlockRows(buf, info["type"], rows, K)
+
 
 
 # ---------------------------------------------------------------- writer

@@ -189,6 +189,40 @@ class TiledWeight:
         return out
 
 
+class BlockRows:
+    """A weight matrix W [N, K] kept on the device as its GGUF rows (any of
+    F32, F16, Q4_0, Q4_1, Q8_0: row n = the blocks of W[n, :]), e.g. a Q4_1
+    projection from a GGUF file (gguf_loader.rs:413-531)."""
+
+    def __init__(self, data, ggml_type: int, n_rows: int, k_cols: int):
+        self.data = data
+        self.type = int(ggml_type)
+        self.N, self.K = int(n_rows), int(k_cols)
+        self.device = data.device
+        self.ctx = context(data.device.index)
+        if data.numel() < N.lib().vxb_block_bytes(self.type, self.N * self.K):
+            raise N.VxbError(N.VXB_EINVAL, "BlockRows: buffer too short")
+
+    def dequantize(self):
+        torch = _torch()
+        out = torch.empty(self.N * self.K, dtype=torch.float32, device=self.device)
+        self.ctx.call("vxb_dequantize_blocks", self.type, _dptr(self.data), self.N * self.K, _dptr(out),
+                      _stream_ptr())
+        return out.reshape(self.N, self.K)
+
+    def gemv(self, x, out=None, out_dtype=None):
+        """y = x @ deq(W)^T for bf16 x [B, K]."""
+        torch = _torch()
+        x = x.contiguous()
+        B = x.numel() // self.K
+        dt = out_dtype or (out.dtype if out is not None else torch.float32)
+        if out is None:
+            out = torch.empty((B, self.N), dtype=dt, device=x.device)
+        self.ctx.call("vxb_gemv_blocks", self.type, _dptr(self.data), self.N, self.K, _dptr(x), B,
+                      N.F32 if dt == torch.float32 else N.BF16, _dptr(out), _stream_ptr())
+        return out
+
+
 def weight_only_matmul(w: TiledWeight, activations):
     """Mirror of weight_only_matmul (src/quantize.rs:845-852) for W stored
     [N, K]: returns activations [M, K] @ deq(W)^T as f32 [M, N]: the decode
