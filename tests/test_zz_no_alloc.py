@@ -45,11 +45,13 @@ def _plan(L, ctx, fmt, N, K, B, static):
 # planner may pick either): "stream" = per-warp stream kernel,
 # "single" = group kernel without a split, "cluster" = group kernel whose
 # splits add through distributed shared memory, "global" = group kernel whose
-# splits add through partial sums in the fixed array
+# splits add through partial sums in the fixed array, "tcgen05" = the
+# tensor-core kernel (its splits add through distributed shared memory)
 CASES = [("Q4_0", 4096, 4096, 1, "stream"), ("Q4_0", 11008, 4096, 3, "stream"),
          ("Q8_0", 1000, 160, 3, None), ("Q8_0", 11008, 4096, 4, None),
-         ("Q4_0", 4096, 11008, 32, None), ("Q4_0", 1024, 16384, 16, "global"),
-         ("Q8_0", 512, 8192, 9, "global"), ("Q8_0", 2048, 128, 9, "single")]
+         ("Q4_0", 4096, 11008, 20, None), ("Q4_0", 1024, 16384, 16, "global"),
+         ("Q4_0", 512, 8192, 12, "global"), ("Q8_0", 2048, 128, 5, "single"),
+         ("Q8_0", 512, 8192, 9, "tcgen05"), ("Q4_0", 4096, 4096, 32, "tcgen05")]
 
 
 def _path(kern, splits, cl):

@@ -1082,7 +1082,7 @@ int gemv_launch(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const 
   if (((uintptr_t)d_tiled) % 256) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q: tiled weights must be 256-byte aligned");
   if (((uintptr_t)d_x) % 16) return set_error(ctx, VXB_EINVAL, "vxb_gemv_q: activations must be 16-byte aligned");
   if (int rc = use_device(ctx)) return rc;
-  if (gemv_tc_eligible(batch) && !plan_override) {
+  if (gemv_tc_eligible(fmt, N, batch) && !plan_override) {
     if (int rc = ws_reserve(ctx, 0, 0)) return rc;  // device error word
     return gemv_tc(ctx, fmt, d_tiled, N, K, d_x, batch, y_dtype, d_y, d_resid, ctx->d_err, (cudaStream_t)stream, true);
   }
@@ -1246,7 +1246,7 @@ VXB_API int vxb_gemv_q_static(vxb_ctx *ctx, int fmt, const void *d_tiled, int N,
   if (int rc = use_device(ctx)) return rc;
   uint8_t *base = nullptr;
   if (int rc = static_scratch(ctx, &base)) return rc;
-  if (gemv_tc_eligible(batch))  // the tensor-core kernel needs no scratch beyond the error word
+  if (gemv_tc_eligible(fmt, N, batch))  // the tensor-core kernel needs no scratch beyond the error word
     return gemv_tc(ctx, fmt, d_tiled, N, K, d_x, batch, y_dtype, d_y, nullptr,
                    (int *)(base + kStaticErrOff), (cudaStream_t)stream, false);
   if (stream_eligible(fmt, batch))  // the per-warp stream kernel needs no scratch beyond the error word
@@ -1305,10 +1305,10 @@ VXB_API int vxb_gemv_plan_info(vxb_ctx *ctx, int fmt, int N, int K, int batch, i
     return set_error(ctx, VXB_EINVAL, "vxb_gemv_plan_info: bad shape N=%d K=%d batch=%d", N, K, batch);
   if (int rc = use_device(ctx)) return rc;
   const TiledGeom g = tiled_geom(fmt, N, K);
-  if (gemv_tc_eligible(batch)) {
+  if (gemv_tc_eligible(fmt, N, batch)) {
     *kernel = 2;
-    *splits = 0;
-    *cluster = 0;
+    *splits = gemv_tc_splits(ctx, fmt, N, K, batch);
+    *cluster = *splits > 1;
     return VXB_OK;
   }
   if (stream_eligible(fmt, batch)) {

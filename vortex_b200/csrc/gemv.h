@@ -18,9 +18,11 @@ size_t gemv_smem_bytes(int fmt, int N, int K, int batch, int S);
 int gemv_launch(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const uint16_t *d_x, int batch,
                 int y_dtype, void *d_y, const float *d_resid, void *stream, const GemvPlan *plan_override);
 
-// Batches 9..32 on the tcgen05 kernel (gemv_tc.cu): eligible only when the
-// process sets VXB_GEMV_TCGEN05=1. d_err is the device error word.
-bool gemv_tc_eligible(int batch);
+// Batches 9..32 on the tcgen05 kernel (gemv_tc.cu): by default Q4_0 batches
+// 17-32 and Q8_0 batches 9-32 with up to 11520 rows (VXB_GEMV_TCGEN05=1:
+// every batch 9-32, =0: none). d_err is the device error word.
+bool gemv_tc_eligible(int fmt, int N, int batch);
+int gemv_tc_splits(const vxb_ctx *ctx, int fmt, int N, int K, int batch);
 int gemv_tc(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const uint16_t *d_x, int batch, int y_dtype,
             void *d_y, const float *d_resid, int *d_err, cudaStream_t st, bool pdl);
 

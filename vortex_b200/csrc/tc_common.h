@@ -31,17 +31,22 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
 
 // Bounded wait for the phase of the given parity; false once `budget` SM
 // clock cycles have passed (kWaitBudget by default, about one second).
+__device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(a), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, long long budget = kWaitBudget) {
   const uint32_t a = smem_u32(bar);
+  if (mbar_try(a, parity)) return true;  // the common case: already complete, no clock read
   const long long t0 = clock64();
   while (true) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
+    if (mbar_try(a, parity)) return true;
     if (clock64() - t0 > budget) return false;
   }
 }
