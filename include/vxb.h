@@ -218,8 +218,16 @@ int vxb_kv_append(vxb_kv *kv, int layer, int n, const int64_t *h_seq_ids, const 
 /* n_tokens consecutive tokens of one sequence (prefill), [n_tokens, H, D]. */
 int vxb_kv_append_seq(vxb_kv *kv, int layer, int64_t seq_id, int n_tokens, const uint16_t *d_k,
                       const uint16_t *d_v, void *stream);
-/* PagedKVCache::free_seq (src/kv_cache.rs:82-89): all layers of seq_id. */
+/* PagedKVCache::free_seq (src/kv_cache.rs:82-89): all layers of seq_id. A
+ * block shared with a forked sequence returns to the free stack when the
+ * last sequence holding it is freed. */
 int vxb_kv_free_seq(vxb_kv *kv, int64_t seq_id);
+/* Prefix reuse (the prefix_cache the reference declares but never fills,
+ * src/kv_cache.rs:37, 44): the empty sequence dst_seq starts as the first
+ * n_tokens tokens of src_seq in every layer. Full blocks are shared (counted
+ * once in kv_stats), a partly filled last block is copied; appends to either
+ * sequence never touch a shared block. Synchronous on `stream`. */
+int vxb_kv_fork(vxb_kv *kv, int64_t src_seq, int64_t dst_seq, int64_t n_tokens, void *stream);
 /* kv_cache_stats (src/kv_cache.rs:220-230): out6 = {used_blocks, free_blocks,
  * block_size, num_seqs (tables), device bytes in use, distinct sequences}. */
 int vxb_kv_stats(const vxb_kv *kv, int64_t *out6);
@@ -373,6 +381,11 @@ int vxb_decoder_step_device(vxb_decoder *d, int batch, const int64_t *h_seq_ids,
                             const int32_t *d_tokens, int32_t *d_next, void *stream);
 int vxb_decoder_logits(vxb_decoder *d, int batch, float *d_out, void *stream);
 int vxb_decoder_free_seq(vxb_decoder *d, int64_t seq_id);
+/* A new sequence dst_seq continuing from the first n_tokens tokens of src_seq
+ * (vxb_kv_fork on the decoder's cache: shared prompt prefixes are stored and
+ * attended once per block). The same call on every rank with tensor
+ * parallelism. */
+int vxb_decoder_fork(vxb_decoder *d, int64_t src_seq, int64_t dst_seq, int64_t n_tokens);
 int vxb_decoder_kv(vxb_decoder *d, vxb_kv **out);
 int vxb_decoder_stream(vxb_decoder *d, void **out);
 

@@ -82,6 +82,7 @@ SIGNATURES = {
     "vxb_kv_append": (_I, [_P, _I, _I, _P, _P, _P, _P]),
     "vxb_kv_append_seq": (_I, [_P, _I, _I64, _I, _P, _P, _P]),
     "vxb_kv_free_seq": (_I, [_P, _I64]),
+    "vxb_kv_fork": (_I, [_P, _I64, _I64, _I64, _P]),
     "vxb_kv_stats": (_I, [_P, _P]),
     "vxb_kv_seq_len": (_I, [_P, _I, _I64, _P]),
     "vxb_kv_block_table": (_I, [_P, _I, _I64, _P, _I, _P]),
@@ -114,6 +115,7 @@ SIGNATURES = {
     "vxb_decoder_step_device": (_I, [_P, _I, _P, _P, _P, _P]),
     "vxb_decoder_logits": (_I, [_P, _I, _P, _P]),
     "vxb_decoder_free_seq": (_I, [_P, _I64]),
+    "vxb_decoder_fork": (_I, [_P, _I64, _I64, _I64]),
     "vxb_decoder_kv": (_I, [_P, ctypes.POINTER(_P)]),
     "vxb_decoder_stream": (_I, [_P, ctypes.POINTER(_P)]),
     "vxb_gguf_open": (_I, [ctypes.c_char_p, ctypes.POINTER(_P)]),

@@ -92,6 +92,22 @@ __device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t &hi, uin
   lo = pack_bf16x2(a - ha, b - hb);
 }
 
+// Four int8 codes -> two bf16x2 words, exactly and without the conversion
+// pipe: each byte b (as b ^ 0x80 = b + 128 unsigned) becomes the f32
+// 2^23 + b + 128 by one byte permute, one f32 subtraction leaves b, and as
+// |b| <= 128 the value's bf16 is the upper half of its f32, so one more
+// permute packs two of them.
+__device__ __forceinline__ void i8x4_to_bf16(uint32_t w, uint32_t &lo, uint32_t &hi) {
+  const float B = 8388736.0f;  // 2^23 + 128
+  const uint32_t u = w ^ 0x80808080u;
+  const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)) - B;
+  const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441)) - B;
+  const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)) - B;
+  const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443)) - B;
+  lo = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
+  hi = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
+}
+
 // byte offset of 16-byte chunk c of token row r in a swizzled page tile
 template <int D>
 __device__ __forceinline__ uint32_t swz(int r, int c) {
@@ -235,12 +251,9 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
         const int r = cc_ / CHUNKS, cc = cc_ % CHUNKS;
         const int8_t *src = rk + (isv ? SM::RAW : 0) + r * D + cc * 8;
         const uint2 raw = *reinterpret_cast<const uint2 *>(src);
-        const int8_t *b8 = reinterpret_cast<const int8_t *>(&raw);
         uint4 outv;
-        outv.x = pack_bf16x2((float)b8[0], (float)b8[1]);
-        outv.y = pack_bf16x2((float)b8[2], (float)b8[3]);
-        outv.z = pack_bf16x2((float)b8[4], (float)b8[5]);
-        outv.w = pack_bf16x2((float)b8[6], (float)b8[7]);
+        i8x4_to_bf16(raw.x, outv.x, outv.y);
+        i8x4_to_bf16(raw.y, outv.z, outv.w);
         *reinterpret_cast<uint4 *>(tk + (isv ? SM::TILE : 0) + swz<D>(r, cc)) = outv;
       }
       __syncwarp();

@@ -785,6 +785,14 @@ VXB_API int vxb_decoder_logits(vxb_decoder *d, int batch, float *d_out, void *st
   return VXB_OK;
 }
 
+VXB_API int vxb_decoder_fork(vxb_decoder *d, int64_t src_seq, int64_t dst_seq, int64_t n_tokens) {
+  if (!d) return set_error(nullptr, VXB_EINVAL, "vxb_decoder_fork: null decoder");
+  if (int rc = use_device(d->ctx)) return rc;
+  if (int rc = vxb_kv_fork(d->kv, src_seq, dst_seq, n_tokens, d->stream)) return rc;
+  VXB_CUDA_TRY(d->ctx, cudaStreamSynchronize(d->stream));
+  return VXB_OK;
+}
+
 VXB_API int vxb_decoder_free_seq(vxb_decoder *d, int64_t seq_id) {
   if (!d) return set_error(nullptr, VXB_EINVAL, "vxb_decoder_free_seq: null decoder");
   VXB_CUDA_TRY(d->ctx, cudaStreamSynchronize(d->stream));

@@ -93,6 +93,26 @@ __global__ void kv_gather_kernel(const int32_t *__restrict__ table, int len, int
   }
 }
 
+// The first `rows` token rows of every head of block `src` into block `dst`
+// (keys, values and, for int8, their scales): the private copy of a forked
+// sequence's partly filled last block.
+__global__ void kv_copy_rows_kernel(uint8_t *pool_k, uint8_t *pool_v, float *scale_k, float *scale_v, int src, int dst,
+                                    int H, int bs, int D, int elem, int rows) {
+  const int h = blockIdx.x;
+  const size_t row_bytes = (size_t)D * elem;
+  const size_t so = ((size_t)src * H + h) * bs * row_bytes, d0 = ((size_t)dst * H + h) * bs * row_bytes;
+  const size_t n = (size_t)rows * row_bytes;
+  for (size_t i = threadIdx.x * 4; i < n; i += (size_t)blockDim.x * 4) {
+    *reinterpret_cast<uint32_t *>(pool_k + d0 + i) = *reinterpret_cast<const uint32_t *>(pool_k + so + i);
+    *reinterpret_cast<uint32_t *>(pool_v + d0 + i) = *reinterpret_cast<const uint32_t *>(pool_v + so + i);
+  }
+  if (scale_k)
+    for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+      scale_k[((size_t)dst * H + h) * bs + r] = scale_k[((size_t)src * H + h) * bs + r];
+      scale_v[((size_t)dst * H + h) * bs + r] = scale_v[((size_t)src * H + h) * bs + r];
+    }
+}
+
 int kv_check(vxb_kv *kv, const char *who) {
   if (!kv || !kv->ctx) return set_error(nullptr, VXB_EINVAL, "%s: null cache", who);
   return VXB_OK;
@@ -124,6 +144,7 @@ int kv_place(vxb_kv *kv, int layer, int64_t seq_id, KVPlace *out) {
                        kv->max_blocks_per_seq);
     if (kv->free_blocks.empty()) return set_error(kv->ctx, VXB_ENOBLOCKS, "KV cache out of blocks");
     t.blocks.push_back(kv->free_blocks.back());
+    kv->refs[kv->free_blocks.back()] = 1;
     kv->free_blocks.pop_back();
   }
   out->block = t.blocks.back();
@@ -134,6 +155,13 @@ int kv_place(vxb_kv *kv, int layer, int64_t seq_id, KVPlace *out) {
   return VXB_OK;
 }
 
+void kv_release_block(vxb_kv *kv, int32_t b) {
+  if (--kv->refs[b] <= 0) {
+    kv->refs[b] = 0;
+    kv->free_blocks.push_back(b);
+  }
+}
+
 void kv_unplace(vxb_kv *kv, int layer, int64_t seq_id, int n) {
   auto it = kv->tables.find(std::make_pair(layer, seq_id));
   if (it == kv->tables.end()) return;
@@ -141,7 +169,7 @@ void kv_unplace(vxb_kv *kv, int layer, int64_t seq_id, int n) {
   for (int i = 0; i < n && t.len > 0; i++) {
     t.len--;
     if (t.len % kv->block_size == 0 && !t.blocks.empty()) {
-      kv->free_blocks.push_back(t.blocks.back());
+      kv_release_block(kv, t.blocks.back());
       t.blocks.pop_back();
     }
   }
@@ -199,6 +227,7 @@ VXB_API int vxb_kv_create(vxb_ctx *ctx, int num_layers, int num_kv_heads, int he
   }
   kv->free_blocks.reserve(max_blocks);
   for (int b = max_blocks - 1; b >= 0; b--) kv->free_blocks.push_back(b);
+  kv->refs.assign(max_blocks, 0);
   for (int s = max_seqs - 1; s >= 0; s--) kv->free_slots.push_back(s);
   *out = kv;
   return VXB_OK;
@@ -276,7 +305,7 @@ VXB_API int vxb_kv_free_seq(vxb_kv *kv, int64_t seq_id) {
     auto it = kv->tables.find(std::make_pair(layer, seq_id));
     if (it == kv->tables.end()) continue;
     any = true;
-    for (int32_t b : it->second.blocks) kv->free_blocks.push_back(b);
+    for (int32_t b : it->second.blocks) kv_release_block(kv, b);
     kv->tables.erase(it);
   }
   auto si = kv->slot_of.find(seq_id);
@@ -333,4 +362,73 @@ VXB_API int vxb_kv_gather(vxb_kv *kv, int layer, int64_t seq_id, float *d_k_out,
       table, (int)it->second.len, kv->num_kv_heads, kv->head_dim, kv->block_size, kv->dtype == VXB_I8, kv->pool_k,
       kv->pool_v, kv->scale_k, kv->scale_v, d_k_out, d_v_out);
   return launch_check(kv->ctx, "kv_gather_kernel");
+}
+
+// Prefix reuse: sequence dst_seq starts as the first n_tokens tokens of
+// src_seq in every layer. Full blocks are shared (each block counts the
+// tables holding it; a shared block is never written again: appends go to
+// a sequence's own last block or to a new one), a partly filled last block is
+// copied into a block of dst's own. The reference only declares a
+// prefix_cache map (src/kv_cache.rs:37, 44) and never fills it.
+VXB_API int vxb_kv_fork(vxb_kv *kv, int64_t src_seq, int64_t dst_seq, int64_t n_tokens, void *stream) {
+  if (int rc = kv_check(kv, "vxb_kv_fork")) return rc;
+  if (src_seq == dst_seq) return set_error(kv->ctx, VXB_EINVAL, "vxb_kv_fork: source and target are the same sequence");
+  if (n_tokens < 0) return set_error(kv->ctx, VXB_EINVAL, "vxb_kv_fork: negative token count");
+  for (int l = 0; l < kv->num_layers; l++) {
+    auto d = kv->tables.find(std::make_pair(l, dst_seq));
+    if (d != kv->tables.end() && d->second.len > 0)
+      return set_error(kv->ctx, VXB_EINVAL, "vxb_kv_fork: sequence %lld already holds tokens", (long long)dst_seq);
+    auto sit = kv->tables.find(std::make_pair(l, src_seq));
+    const int64_t have = sit == kv->tables.end() ? 0 : sit->second.len;
+    if (n_tokens > have)
+      return set_error(kv->ctx, VXB_EINVAL, "vxb_kv_fork: sequence %lld holds %lld tokens in layer %d, %lld asked",
+                       (long long)src_seq, (long long)have, l, (long long)n_tokens);
+  }
+  if (n_tokens == 0) return VXB_OK;
+  const int bs = kv->block_size;
+  const int64_t full = n_tokens / bs, rem = n_tokens % bs;
+  if (full + (rem > 0) > kv->max_blocks_per_seq)
+    return set_error(kv->ctx, VXB_ENOBLOCKS, "sequence %lld exceeds max_blocks_per_seq=%d", (long long)dst_seq,
+                     kv->max_blocks_per_seq);
+  if (rem > 0 && (int64_t)kv->free_blocks.size() < kv->num_layers)
+    return set_error(kv->ctx, VXB_ENOBLOCKS, "KV cache out of blocks");
+  int slot;
+  auto si = kv->slot_of.find(dst_seq);
+  if (si == kv->slot_of.end()) {
+    if (kv->free_slots.empty())
+      return set_error(kv->ctx, VXB_ENOBLOCKS, "KV cache has no free sequence slot (max_seqs=%d)", kv->max_seqs);
+    slot = kv->free_slots.back();
+    kv->free_slots.pop_back();
+    kv->slot_of[dst_seq] = slot;
+  } else {
+    slot = si->second;
+  }
+  if (int rc = use_device(kv->ctx)) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  std::vector<int32_t> tab;
+  for (int l = 0; l < kv->num_layers; l++) {
+    const vxb_kv::Table &s = kv->tables.at(std::make_pair(l, src_seq));
+    vxb_kv::Table &t = kv->tables[std::make_pair(l, dst_seq)];
+    t.blocks.assign(s.blocks.begin(), s.blocks.begin() + full);
+    for (int32_t b : t.blocks) kv->refs[b]++;
+    if (rem > 0) {
+      const int32_t b = kv->free_blocks.back();
+      kv->free_blocks.pop_back();
+      kv->refs[b] = 1;
+      kv_copy_rows_kernel<<<kv->num_kv_heads, 256, 0, st>>>(
+          (uint8_t *)kv->pool_k, (uint8_t *)kv->pool_v, kv->scale_k, kv->scale_v, s.blocks[full], b, kv->num_kv_heads,
+          bs, kv->head_dim, (int)kv->elem_bytes, (int)rem);
+      if (int rc = launch_check(kv->ctx, "kv_copy_rows_kernel")) return rc;
+      t.blocks.push_back(b);
+    }
+    t.len = n_tokens;
+    tab = t.blocks;
+    const size_t row = ((size_t)l * kv->max_seqs + slot);
+    VXB_CUDA_TRY(kv->ctx, cudaMemcpyAsync(kv->d_tables + row * kv->max_blocks_per_seq, tab.data(),
+                                          tab.size() * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    const int32_t len = (int32_t)n_tokens;
+    VXB_CUDA_TRY(kv->ctx, cudaMemcpyAsync(kv->d_lens + row, &len, sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    VXB_CUDA_TRY(kv->ctx, cudaStreamSynchronize(st));  // tab and len are host temporaries
+  }
+  return VXB_OK;
 }

@@ -34,6 +34,7 @@ struct vxb_kv {
   };
   std::map<std::pair<int, int64_t>, Table> tables;  // (layer, seq_id) -> table
   std::vector<int32_t> free_blocks;                   // stack; back() is popped next
+  std::vector<int32_t> refs;                          // tables holding each block (a fork shares blocks)
   std::unordered_map<int64_t, int> slot_of;           // seq_id -> slot
   std::vector<int> free_slots;                        // stack of unused slots
 };
@@ -44,6 +45,10 @@ namespace vxb {
 // from the free stack when the sequence's last block is full
 // (PagedKVCache::append_kv, src/kv_cache.rs:54-67).
 int kv_place(vxb_kv *kv, int layer, int64_t seq_id, KVPlace *out);
+
+// Drop one table's hold on a block; the block returns to the free stack when
+// no table holds it.
+void kv_release_block(vxb_kv *kv, int32_t b);
 
 // Roll back the placements of a failed multi-token append.
 void kv_unplace(vxb_kv *kv, int layer, int64_t seq_id, int n);

@@ -236,6 +236,11 @@ class Decoder:
     def free_seq(self, seq_id: int):
         self._check(N.lib().vxb_decoder_free_seq(self.ptr, int(seq_id)))
 
+    def fork(self, src_seq: int, dst_seq: int, n_tokens: int):
+        """A new sequence continuing from the first n_tokens of src_seq
+        (shared prompt prefix: its KV blocks are shared, not recomputed)."""
+        self._check(N.lib().vxb_decoder_fork(self.ptr, int(src_seq), int(dst_seq), int(n_tokens)))
+
     def stream_handle(self) -> int:
         p = ctypes.c_void_p()
         self._check(N.lib().vxb_decoder_stream(self.ptr, ctypes.byref(p)))

@@ -73,6 +73,11 @@ class PagedKVCache:
     def free_seq(self, seq_id: int):
         self._check(N.lib().vxb_kv_free_seq(self.ptr, int(seq_id)))
 
+    def fork(self, src_seq: int, dst_seq: int, n_tokens: int):
+        """Prefix reuse: dst_seq starts as the first n_tokens tokens of
+        src_seq (full blocks shared, a partial last block copied)."""
+        self._check(N.lib().vxb_kv_fork(self.ptr, int(src_seq), int(dst_seq), int(n_tokens), _stream_ptr()))
+
     def stats(self) -> dict:
         out = (ctypes.c_int64 * 6)()
         self._check(N.lib().vxb_kv_stats(self.ptr, out))
