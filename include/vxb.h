@@ -273,6 +273,18 @@ int vxb_gemm_q(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const u
 int vxb_flash_fwd(vxb_ctx *ctx, const uint16_t *d_q, const uint16_t *d_k, const uint16_t *d_v, int B, int H,
                   int Hkv, int S, int d, float scale, int causal, uint16_t *d_o, float *d_lse, void *stream);
 
+/* Flash-attention backward. Replaces flash_attention_backward
+ * (src/flash_attention.rs:227-317): with D_i = dO_i . O_i and P_ij =
+ * exp(scale q_i.k_j - lse_i) (0 for masked keys), dV_j = sum_i P_ij dO_i,
+ * dS_ij = P_ij (dO_i.v_j - D_i) scale, dK_j = sum_i dS_ij q_i, dQ_i = sum_j
+ * dS_ij k_j. Tensors as vxb_flash_fwd (bf16 [B, S, heads, 128], lse f32
+ * [B, H, S] from the forward); d_dq f32 [B, S, H, 128], d_dk / d_dv f32
+ * [B, S, Hkv, 128] (summed over the query heads of each kv head). Tensor
+ * cores (mma.sync, f32 accumulate), deterministic (no atomics). */
+int vxb_flash_bwd(vxb_ctx *ctx, const uint16_t *d_q, const uint16_t *d_k, const uint16_t *d_v, const uint16_t *d_o,
+                  const uint16_t *d_dout, const float *d_lse, int B, int H, int Hkv, int S, int d, float scale,
+                  int causal, float *d_dq, float *d_dk, float *d_dv, void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* K5: single ops of the Llama-style block (stdlib/ai/transformer.vx).       */
 /* ------------------------------------------------------------------------ */

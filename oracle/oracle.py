@@ -66,6 +66,8 @@ def lib():
             "vxo_flash_auto_tile": (ctypes.c_int, [_SZ, _SZ]),
             "vxo_flash_attention_forward": (None, [_P, _P, _P, _SZ, _SZ, _SZ, _SZ, ctypes.c_int, _P, _P, _P]),
             "vxo_standard_attention": (None, [_P, _P, _P, _SZ, _SZ, ctypes.c_int, _P]),
+            "vxo_flash_attention_backward": (None, [_P, _P, _P, _P, _P, _P, _SZ, _SZ, _SZ, _SZ, ctypes.c_int, _P, _P,
+                                                    _P]),
             "vxo_multi_head_flash_attention": (None, [_P, _P, _P, _SZ, _SZ, _SZ, ctypes.c_int, _P]),
             "vxo_attention_rows": (None, [_P, _P, _P, _SZ, _SZ, ctypes.c_int, _P, _SZ, _P, _P]),
             "vxo_paged_attention": (None, [_P, _P, _P, _SZ, _SZ, _P]),
@@ -305,6 +307,17 @@ def multi_head_flash_attention(q, k, v, num_heads: int, head_dim: int, causal: b
     out = np.zeros(n * num_heads * head_dim)
     lib().vxo_multi_head_flash_attention(_p(q), _p(k), _p(v), n, num_heads, head_dim, int(causal), _p(out))
     return out
+
+
+def flash_attention_backward(q, k, v, out, grad_out, lse, d: int, br: int, bc: int, causal: bool):
+    """flash_attention_backward (src/flash_attention.rs:227-317) of one head:
+    inputs [N, d] (flat), lse [N]; returns (grad_q, grad_k, grad_v) flat."""
+    q, k, v, out, grad_out, lse = (_f64(t) for t in (q, k, v, out, grad_out, lse))
+    n = q.size // d
+    gq, gk, gv = (np.zeros(n * d) for _ in range(3))
+    lib().vxo_flash_attention_backward(_p(q), _p(k), _p(v), _p(out), _p(grad_out), _p(lse), n, d, br, bc,
+                                       int(causal), _p(gq), _p(gk), _p(gv))
+    return gq, gk, gv
 
 
 def attention_rows(q, k, v, d: int, causal: bool, rows):

@@ -683,3 +683,43 @@ int32_t vxo_int4_dot(const uint8_t *a, const uint8_t *b, size_t nbytes) {
     }
     return (int32_t)acc;
 }
+
+/* flash_attention_backward (src/flash_attention.rs:227-317): D_i = dO_i . O_i,
+ * then K/V tiles outer, Q tiles inner, the causal skip of whole tiles and of
+ * keys past the query, P = exp(s - lse_i), and the four accumulations in the
+ * reference's order. */
+void vxo_flash_attention_backward(const double *q, const double *k, const double *v, const double *out,
+                                  const double *grad_out, const double *lse, size_t n, size_t d, size_t br,
+                                  size_t bc, int causal, double *grad_q, double *grad_k, double *grad_v) {
+    const double scale = 1.0 / sqrt((double)d);
+    double *di = (double *)calloc(n ? n : 1, sizeof(double));
+    for (size_t i = 0; i < n * d; i++) grad_q[i] = grad_k[i] = grad_v[i] = 0.0;
+    for (size_t i = 0; i < n; i++)
+        for (size_t dd = 0; dd < d; dd++) di[i] += grad_out[i * d + dd] * out[i * d + dd];
+    for (size_t jb = 0; jb < n; jb += bc) {
+        size_t je = jb + bc < n ? jb + bc : n;
+        for (size_t ib = 0; ib < n; ib += br) {
+            size_t ie = ib + br < n ? ib + br : n;
+            if (causal && ie - 1 < jb) continue;
+            for (size_t ii = 0; ii < ie - ib; ii++) {
+                size_t qi = ib + ii, qo = qi * d;
+                for (size_t jj = 0; jj < je - jb; jj++) {
+                    size_t kj = jb + jj;
+                    if (causal && kj > qi) continue;
+                    size_t ko = kj * d;
+                    double dot = 0.0;
+                    for (size_t dd = 0; dd < d; dd++) dot += q[qo + dd] * k[ko + dd];
+                    double s = dot * scale;
+                    double p = exp(s - lse[qi]);
+                    for (size_t dd = 0; dd < d; dd++) grad_v[ko + dd] += p * grad_out[qo + dd];
+                    double dp = 0.0;
+                    for (size_t dd = 0; dd < d; dd++) dp += grad_out[qo + dd] * v[ko + dd];
+                    double ds = p * (dp - di[qi]) * scale;
+                    for (size_t dd = 0; dd < d; dd++) grad_q[qo + dd] += ds * k[ko + dd];
+                    for (size_t dd = 0; dd < d; dd++) grad_k[ko + dd] += ds * q[qo + dd];
+                }
+            }
+        }
+    }
+    free(di);
+}

@@ -82,6 +82,9 @@ int vxo_flash_auto_tile(size_t seq_len, size_t head_dim);
 void vxo_flash_attention_forward(const double *q, const double *k, const double *v,
                                  size_t n, size_t d, size_t br, size_t bc, int causal,
                                  double *out, double *lse, double *row_max);
+void vxo_flash_attention_backward(const double *q, const double *k, const double *v, const double *out,
+                                  const double *grad_out, const double *lse, size_t n, size_t d, size_t br,
+                                  size_t bc, int causal, double *grad_q, double *grad_k, double *grad_v);
 void vxo_standard_attention(const double *q, const double *k, const double *v,
                             size_t n, size_t d, int causal, double *out);
 void vxo_multi_head_flash_attention(const double *q, const double *k, const double *v,

@@ -361,3 +361,24 @@ def test_tf_model_shapes_kat():
     # Xavier bound of the embedding (fan_in 64, fan_out 16) and zero biases
     assert np.max(np.abs(p[:emb])) <= np.sqrt(6 / 80) + 1e-7
     assert np.all(p[emb + 16 * 16:emb + 16 * 16 + 16] == 0)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_flash_backward_numerical_gradient(causal):  # src/flash_attention.rs:783-880
+    """The oracle's flash_attention_backward against central differences of
+    the forward (N=4, d=4, tiles 2, seeds 1/2/3, loss = sum of the outputs,
+    eps 1e-5, |analytical - numerical| < 1e-4), as the reference's own test;
+    the causal case is checked the same way."""
+    n, d, eps = 4, 4, 1e-5
+    q, k, v = (lcg_matrix(n, d, s) for s in (1, 2, 3))
+    out, lse, _ = O.flash_attention_forward(q, k, v, d, 2, 2, causal)
+    gq, gk, gv = O.flash_attention_backward(q, k, v, out, np.ones(n * d), lse, d, 2, 2, causal)
+    for which, g in ((0, gq), (1, gk), (2, gv)):
+        for idx in range(n * d):
+            args_p = [np.array(t, dtype=np.float64) for t in (q, k, v)]
+            args_m = [np.array(t, dtype=np.float64) for t in (q, k, v)]
+            args_p[which][idx] += eps
+            args_m[which][idx] -= eps
+            lp = O.flash_attention_forward(*args_p, d, 2, 2, causal)[0].sum()
+            lm = O.flash_attention_forward(*args_m, d, 2, 2, causal)[0].sum()
+            assert abs(g[idx] - (lp - lm) / (2 * eps)) < 1e-4, (which, idx)

@@ -90,6 +90,7 @@ SIGNATURES = {
     "vxb_decode_attention": (_I, [_P, _I, _I, _P, _P, _I, ctypes.c_float, _P, _P, _P]),
     "vxb_gemm_q": (_I, [_P, _I, _P, _I, _I, _P, _I, _I, _P, _P]),
     "vxb_flash_fwd": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, ctypes.c_float, _I, _P, _P, _P]),
+    "vxb_flash_bwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, ctypes.c_float, _I, _P, _P, _P, _P]),
     "vxb_rmsnorm": (_I, [_P, _P, _P, _P, _I, _I, ctypes.c_float, _P, _P]),
     "vxb_swiglu": (_I, [_P, _P, _I, _I, _P, _P]),
     "vxb_argmax": (_I, [_P, _P, _I, _I, _P, _P]),

@@ -50,3 +50,28 @@ def multi_head_flash_attention(q, k, v, num_heads: int, head_dim: int, causal: b
     o, _ = flash_attention(q.reshape(shp).contiguous(), k.reshape(shp).contiguous(), v.reshape(shp).contiguous(),
                            causal=causal)
     return o.reshape(n, num_heads * head_dim)
+
+
+def flash_attention_backward(q, k, v, out, grad_out, lse, causal: bool = True, softmax_scale: float | None = None,
+                             stream=None):
+    """flash_attention_backward (src/flash_attention.rs:227-317) on the
+    device: q / out / grad_out bf16 [B, S, H, 128], k / v bf16 [B, S, Hkv,
+    128], lse f32 [B, H, S] (the forward's second output). Returns (dq, dk,
+    dv) as f32 tensors of the shapes of q, k, v."""
+    import torch
+    B, S, H, d = q.shape
+    Hkv = k.shape[2]
+    for t in (q, k, v, out, grad_out):
+        if t.dtype != torch.bfloat16 or not t.is_cuda or not t.is_contiguous():
+            raise N.VxbError(N.VXB_EINVAL, "flash_attention_backward: tensors must be contiguous bf16 on the GPU")
+    if out.shape != q.shape or grad_out.shape != q.shape or v.shape != k.shape:
+        raise N.VxbError(N.VXB_EINVAL, "flash_attention_backward: shape mismatch")
+    lse = lse.contiguous().float()
+    scale = 1.0 / math.sqrt(d) if softmax_scale is None else float(softmax_scale)
+    dq = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    dk = torch.empty(k.shape, dtype=torch.float32, device=q.device)
+    dv = torch.empty(v.shape, dtype=torch.float32, device=q.device)
+    ctx = context(q.device.index)
+    ctx.call("vxb_flash_bwd", _dptr(q), _dptr(k), _dptr(v), _dptr(out), _dptr(grad_out), _dptr(lse), B, H, Hkv, S,
+             d, ctypes.c_float(scale), int(causal), _dptr(dq), _dptr(dk), _dptr(dv), _stream_ptr(stream))
+    return dq, dk, dv

@@ -137,6 +137,30 @@ def flash_attention(*args):
     return o.float().cpu().numpy().astype(np.float64).tolist()
 
 
+def flash_attention_backward(*args):
+    """flash_attention_backward(q, k, v, output, grad_output, [num_heads],
+    [causal]) -> (grad_q, grad_k, grad_v) as [N][H*d] (the
+    builtin_flash_attention_backward adapter, src/interpreter.rs:2267-2340:
+    per head, lse from a non-causal forward and a non-causal backward - the
+    adapter reads `causal` but never uses it)."""
+    import torch
+
+    from . import attention as A
+    if len(args) < 5:
+        raise BuiltinError("flash_attention_backward expects (q, k, v, output, grad_output, [num_heads], [causal])")
+    mats = [np.asarray(a, dtype=np.float64) for a in args[:5]]
+    if mats[0].size == 0:
+        return ([], [], [])
+    n, total = mats[0].shape
+    heads = args[5] if len(args) > 5 and isinstance(args[5], (int, np.integer)) else 1
+    hd = total // heads
+    q, k, v, o, do = (torch.from_numpy(m.astype(np.float32)).cuda().to(torch.bfloat16).reshape(1, n, heads, hd)
+                      for m in mats)
+    _, lse = A.flash_attention(q, k, v, causal=False)
+    dq, dk, dv = A.flash_attention_backward(q, k, v, o, do, lse, causal=False)
+    return tuple(t.reshape(n, total).cpu().numpy().astype(np.float64).tolist() for t in (dq, dk, dv))
+
+
 # ---------------------------------------------------------------- KV cache and batcher
 
 _LOCK = threading.Lock()

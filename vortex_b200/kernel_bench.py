@@ -3,6 +3,7 @@
     python -m vortex_b200.kernel_bench gemv [--fmt Q4_0] [--n 11008] [--k 4096] [--batch 1]
     python -m vortex_b200.kernel_bench attn [--ctx 8192] [--dtype bf16] [--batch 32] [--hq 32] [--hkv 8]
     python -m vortex_b200.kernel_bench flash [--b 4] [--h 32] [--s 4096] [--non-causal]
+    python -m vortex_b200.kernel_bench flash_bwd [--b 4] [--h 32] [--s 4096]
     python -m vortex_b200.kernel_bench gemm [--m 2048] [--n 12288 ...] [--k 4096 ...]
 
 Each case streams its operands from HBM: the GEMV rotates over enough distinct
@@ -156,6 +157,28 @@ def flash_case(B: int = 4, H: int = 32, S: int = 4096, causal: bool = True, reps
             "flops": flops}
 
 
+def flash_bwd_case(B: int = 4, H: int = 32, S: int = 4096, causal: bool = True, reps: int = 5, seed: int = 0):
+    """Flash-attention backward on the prefill shape. FLOPs count the
+    algorithmic products over visible pairs: S, dP, dV, dK, dQ = 5 x 2 x d
+    per pair (the recomputation of S and dP in the dQ pass is not counted)."""
+    import torch
+
+    from . import attention as A
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    q, k, v, do = (torch.randn(B, S, H, 128, device="cuda", generator=gen).bfloat16() for _ in range(4))
+    o, lse = A.flash_attention(q, k, v, causal=causal)
+    A.flash_attention_backward(q, k, v, o, do, lse, causal=causal)
+
+    def run():
+        A.flash_attention_backward(q, k, v, o, do, lse, causal=causal)
+
+    t = _graph_time(torch, run, 1, reps)
+    pairs = S * (S + 1) // 2 if causal else S * S
+    flops = 10 * B * H * 128 * pairs
+    return {"B": B, "H": H, "S": S, "d": 128, "causal": causal, "us": t * 1e6, "TFLOPs": flops / t / 1e12,
+            "flops": flops}
+
+
 def gemm_case(fmt="Q4_0", M: int = 2048, N: int = 11008, K: int = 4096, reps: int = 10, seed: int = 0):
     """Prefill GEMM Y[M, N] = X[M, K] deq(W)^T, W ~ N(0, 0.02), X ~ N(0, 1)
     bf16, Y f32. FLOPs = 2 M N K (algorithmic; the kernel runs the hi and lo
@@ -198,6 +221,11 @@ def main():
     f.add_argument("--s", type=int, default=4096)
     f.add_argument("--non-causal", action="store_true")
     f.add_argument("--reps", type=int, default=10)
+    fb = sub.add_parser("flash_bwd")
+    fb.add_argument("--b", type=int, default=4)
+    fb.add_argument("--h", type=int, default=32)
+    fb.add_argument("--s", type=int, default=4096)
+    fb.add_argument("--reps", type=int, default=5)
     a = sub.add_parser("attn")
     a.add_argument("--ctx", type=int, nargs="*", default=[1024, 8192, 32768])
     a.add_argument("--dtype", nargs="*", default=["bf16", "int8"])
@@ -216,6 +244,8 @@ def main():
     elif args.what == "gemm":
         for n, k in zip(args.n, args.k):
             print(json.dumps(gemm_case(args.fmt, args.m, n, k, args.reps)), flush=True)
+    elif args.what == "flash_bwd":
+        print(json.dumps(flash_bwd_case(args.b, args.h, args.s, True, args.reps)), flush=True)
     elif args.what == "flash":
         print(json.dumps(flash_case(args.b, args.h, args.s, not args.non_causal, args.reps)), flush=True)
     else:
