@@ -580,7 +580,8 @@ def decode_attn_sweep(ws, hbm, peak_src):
     """The decode-attention configuration: 32 sequences, 32 query / 8 KV heads,
     head_dim 128, ctx 1k/8k/32k, bf16 and int8 KV; the heads are split over
     the ranks (each rank 32/N query and 8/N KV heads), time = max over ranks,
-    GB/s = the whole configuration's algorithmic bytes / that time."""
+    GB/s = the whole configuration's algorithmic bytes / that time; frac
+    against the N GPUs' combined peak (N x the one-GPU copy bandwidth)."""
     from vortex_b200 import kernel_bench as KB
     cases = []
     for dt in ("bf16", "int8"):
@@ -590,9 +591,10 @@ def decode_attn_sweep(ws, hbm, peak_src):
             per_tok = 8 * 128 * 2 * 2 if dt == "bf16" else 8 * 128 * 2 + 8 * 2 * 4
             byts = 32 * ctx * per_tok + 2 * 2 * 32 * 32 * 128
             cases.append({"dtype": dt, "ctx": ctx, "us": round(t, 2), "achieved": round(byts / t / 1e3, 1),
-                          "frac": round(byts / t / 1e3 / hbm, 3), "bytes": byts})
+                          "frac": round(byts / t / 1e3 / (hbm * ws), 3), "bytes": byts})
     return {"config": "32 sequences x 32 query heads / 8 KV heads (GQA), head_dim 128, one new token each; "
-                      f"heads split over {ws} GPU(s)", "unit": "GB/s", "peak": hbm, "peak_source": peak_src,
+                      f"heads split over {ws} GPU(s)", "unit": "GB/s", "peak": hbm * ws,
+            "peak_source": peak_src + (f" (x{ws} GPUs)" if ws > 1 else ""),
             "bytes": "32*ctx*(8*128*2*2 bf16 | 8*(128+4)*2 int8) + q/out", "cases": cases}
 
 
