@@ -19,6 +19,7 @@
 // int8 caches stage int8 pages and one f32 scale per (token, head); the K
 // scale multiplies the scores and the V scale is folded into P.
 #include <atomic>
+#include <cstdlib>
 #include <cuda_bf16.h>
 
 #include "decode_attn.h"
@@ -448,25 +449,46 @@ int launch_t(vxb_ctx *ctx, const DecodeArgs &a, cudaStream_t st) {
 
 namespace vxb {
 
-// Token splits per (sequence, kv head): a CTA streams its pages at a rate
-// set by its own pipeline, so the CTAs should fill one wave of the resident
-// slots (3 per SM) rather than spill a small second wave; with many pairs one
-// split each. At most 16 splits: the merge in the last-arriving CTA grows with
-// the split count (measured at batch 1: 12 splits 13 us, 34 splits 19 us).
+// Token splits per (sequence, kv head). The run time is about the number of
+// CTA waves (3 resident CTAs per SM) times the time of one CTA, which is a
+// fixed part - pipeline fill and drain, the merge - worth about 300 tokens of
+// streaming plus its share of the tokens. Fitted to measurements on B200 (32
+// sequences x 8 KV heads: ctx 1k best unsplit, 8k and 32k at 5 splits, 0.96
+// and 1.06 of the copy bandwidth; 32 sequences x 32 KV heads at ctx 2k: 2
+// splits). At most 12 splits (the merge in the last-arriving CTA grows with
+// the split count), at least 64 tokens each.
+// VXB_DECODE_SPLITS=n forces n (tuning).
 DecodePlan decode_plan(const vxb_ctx *ctx, int n, int Hkv, int max_len) {
   DecodePlan p;
   const int sms = ctx->num_sms > 0 ? ctx->num_sms : 148;
-  const int pairs = n * Hkv;
-  const int slots = 3 * sms;
-  int splits = pairs >= slots ? 1 : slots / pairs;
-  splits = min(splits, 16);
-  const int max_split = max(1, (max_len + 63) / 64);
-  splits = max(1, min(splits, max_split));
-  int tps = (max_len + splits - 1) / splits;
-  tps = max(64, (tps + 63) / 64 * 64);
-  splits = max(1, (max_len + tps - 1) / tps);
-  p.splits = splits;
-  p.tps = tps;
+  const long long pairs = (long long)n * Hkv;
+  const long long slots = 3LL * sms;
+  static const int forced = [] {
+    const char *e = std::getenv("VXB_DECODE_SPLITS");
+    return e ? std::atoi(e) : 0;
+  }();
+  auto tps_for = [&](int s) {
+    const int t = (max_len + s - 1) / s;
+    return max(64, (t + 63) / 64 * 64);
+  };
+  int best = 1;
+  if (forced > 0) {
+    best = min(forced, 16);
+  } else {
+    double best_cost = 1e300;
+    for (int s = 1; s <= 12; s++) {
+      const int tps = tps_for(s);
+      if ((max_len + tps - 1) / tps != s && s > 1) continue;  // the same split count as a smaller s
+      const double waves = (double)((pairs * s + slots - 1) / slots);
+      const double cost = waves * (300.0 + tps);
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best = s;
+      }
+    }
+  }
+  p.tps = tps_for(best);
+  p.splits = max(1, (max_len + p.tps - 1) / p.tps);
   return p;
 }
 
