@@ -473,10 +473,10 @@ DecodePlan decode_plan(const vxb_ctx *ctx, int n, int Hkv, int max_len) {
   };
   int best = 1;
   if (forced > 0) {
-    best = min(forced, 16);
+    best = min(forced, kMaxDecodeSplits);
   } else {
     double best_cost = 1e300;
-    for (int s = 1; s <= 12; s++) {
+    for (int s = 1; s <= kMaxDecodeSplits; s++) {
       const int tps = tps_for(s);
       if ((max_len + tps - 1) / tps != s && s > 1) continue;  // the same split count as a smaller s
       const double waves = (double)((pairs * s + slots - 1) / slots);

@@ -10,6 +10,9 @@ struct DecodePlan {
   int tps;     // tokens per split (multiple of 64)
 };
 
+// decode_plan never returns more splits than this
+constexpr int kMaxDecodeSplits = 12;
+
 DecodePlan decode_plan(const vxb_ctx *ctx, int n, int Hkv, int max_len);
 size_t decode_ws_bytes(int n, int Hkv, int G, int D, int splits);
 

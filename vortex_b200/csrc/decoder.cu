@@ -261,9 +261,9 @@ int decoder_create(vxb_ctx *ctx, const vxb_decoder_config *cfg, vxb_comm *comm, 
     rc = vxb_kv_create(ctx, L, d->hkv, hd, bs, max_blocks, B, mbps, c.kv_dtype ? c.kv_dtype : VXB_BF16, &d->kv);
   }
   if (!rc) {
-    // attention scratch for the largest batch with the split plan used in graphs
-    const DecodePlan p = decode_plan(ctx, 1, d->hkv, c.max_seq);
-    d->attn_ws_bytes = decode_ws_bytes(B, d->hkv, c.n_heads / c.n_kv_heads, hd, p.splits);
+    // attention scratch for the largest batch at the largest split count any
+    // plan uses, so that every captured step fits
+    d->attn_ws_bytes = decode_ws_bytes(B, d->hkv, c.n_heads / c.n_kv_heads, hd, kMaxDecodeSplits);
     rc = dalloc(d, (void **)&d->attn_ws, d->attn_ws_bytes);
   }
   if (!rc) {
