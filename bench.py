@@ -44,7 +44,7 @@ FALLBACK_BF16_TFLOPS = 1590.0
 # own per-layer shape (32 sequences x 32 heads, ctx 2048, bf16): one ncu
 # capture read 1,074,086,144 + wrote 3,865,344 bytes for 1,074,266,112
 # algorithmic bytes; applied to the bench's launch to give its traffic
-ATTN_TRAFFIC_RATIO = (1074086144 + 3865344) / 1074266112
+ATTN_TRAFFIC_RATIO = (1074920192 + 6536448) / 1074266112
 ATTN_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of decode_attn_kernel at 32 sequences x "
                        "32 heads, ctx 2048, bf16 (profiles/decode_attn_b32_ctx2048_mha_bf16.md), scaled by "
                        "algorithmic bytes")
