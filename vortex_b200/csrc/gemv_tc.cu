@@ -37,24 +37,26 @@ namespace {
 // block's f32 sums by the f16 block scales (acc += d * D): the scales never
 // round into an operand.
 //
-// Eight worker warps run every pair in lockstep; there is no producer or MMA
-// warp. Per pair, warp w decodes tile 2(w%4) + w/4 of both steps (its TMEM
-// lane quadrant is w%4), runs the epilogue of the previous pair (block w/4 of
-// both steps for the 32 rows of its quadrant: one tcgen05.ld per step and
-// packed f32x2 FMAs), stores its codes into the A buffer, and the warps meet
-// on a hardware named barrier (sleeping, no polling). Thread 0 then issues
-// the pair's eight MMAs and commits them to one mbarrier, refilling the ring
-// slot of the stage whose MMAs it has just seen complete. A and the
-// accumulators have one buffer each (192 of 256 TMEM columns, two CTAs per
-// SM): the epilogue of the previous pair waits for its MMAs before the A
-// buffer is rewritten, and the next MMAs are issued only after every warp
-// has read the accumulators. The waits are for TMA data issued stages ahead
-// and for MMAs issued a pair earlier, so they are normally complete when
-// reached. The first stages' weights are requested before the wait for the
-// kernel that produces x.
+// Eight worker warps run every pair in lockstep, and a ninth warp issues the
+// MMAs and the TMA refills. Per pair, worker warp w reads the codes of tile
+// 2(w%4) + w/4 for both steps, runs the epilogue of the previous pair (block
+// w/4 of both steps for the 32 rows of its quadrant: one tcgen05.ld per step
+// and packed f32x2 FMAs), decodes and stores its codes into the A buffer,
+// and the nine warps meet on a hardware named barrier (sleeping, no
+// polling). The MMA warp then refills the ring slot of the previous pair
+// (whose MMAs the workers saw complete in their epilogue) and issues this
+// pair's eight MMAs with one commit, while the workers move on to the next
+// pair - so no worker waits for the MMA issue at the next barrier (with a
+// worker thread issuing them, that wait was the kernel's largest stall). A
+// and the accumulators have one buffer each (192 of 256 TMEM columns, two
+// CTAs per SM): the epilogue of the previous pair waits for its MMAs before
+// the A buffer is rewritten, and the next MMAs are issued only after every
+// worker has read the accumulators. The first stages' weights are requested
+// before the wait for the kernel that produces x.
 // S > 1 CTAs of a row group form a cluster and add their partial sums through
 // distributed shared memory in CTA order.
-constexpr int TC_THREADS = 256;
+constexpr int TC_WORKERS = 256;                 // eight worker warps
+constexpr int TC_THREADS = TC_WORKERS + 32;     // + the MMA / TMA warp
 constexpr int TC_MAX_WR = 8;
 constexpr uint32_t TC_COLS = 256, TC_ACOL = 0, TC_DCOL = 64;
 constexpr size_t TC_SMEM_CAP = 110 * 1024;  // two CTAs per SM
@@ -127,14 +129,16 @@ __device__ __forceinline__ void tc_wait_warp(uint64_t *bar, uint32_t parity, int
   if (!__all_sync(0xffffffffu, mine) && (threadIdx.x & 31) == 0) atomicExch(err, 1);
 }
 
-__device__ __forceinline__ void workers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(TC_THREADS) : "memory"); }
+// the worker warps and the MMA warp, once per pair: the A buffer is written
+__device__ __forceinline__ void pair_sync() { asm volatile("bar.sync 1, %0;" ::"n"(TC_THREADS) : "memory"); }
+// the worker warps only
+__device__ __forceinline__ void workers_sync() { asm volatile("bar.sync 2, %0;" ::"n"(TC_WORKERS) : "memory"); }
 
 // The 16x256b.x4 registers of one tile for one 64-column step: k16 step s
 // holds {row g: k 4q..4q+1, row g: 4q+2..4q+3, row g+8: 4q..4q+1, row g+8:
 // 4q+2..4q+3} = fragment pairs {a0a1, a4a5, a2a3, a6a7}.
 template <int FMT>
-__device__ __forceinline__ void tc_decode_tile(const uint8_t *u0, const uint8_t *u1, int lane, uint32_t (&r)[16]) {
-  const uint4 c0 = *reinterpret_cast<const uint4 *>(u0 + lane * 16);
+__device__ __forceinline__ void tc_decode_words(const uint4 c0, const uint4 c1, uint32_t (&r)[16]) {
   if (FMT == 0) {
     const uint32_t w[4] = {c0.x, c0.y, c0.z, c0.w};
 #pragma unroll
@@ -147,7 +151,6 @@ __device__ __forceinline__ void tc_decode_tile(const uint8_t *u0, const uint8_t 
       r[4 * s + 3] = A[3];
     }
   } else {
-    const uint4 c1 = *reinterpret_cast<const uint4 *>(u1 + lane * 16);
     const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
     for (int s = 0; s < 4; s++) {
@@ -208,18 +211,51 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
     vxb::tc::tma_load_2d(d, &xmap, (ws0 + ws) * 128, 0, &wfull[slot]);
     vxb::tc::tma_load_2d(d + SM::XB, &xmap, (ws0 + ws) * 128 + 64, 0, &wfull[slot]);
   };
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == TC_WORKERS) {
     const int pre = min(a.wr, nws);
     for (int ws = 0; ws < pre; ws++) load_weights(ws, ws);
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x comes from the previous kernel
     for (int ws = 0; ws < pre; ws++) load_x(ws, ws);
   }
+  constexpr uint32_t ID = vxb::tc::idesc_bf16(128, NB, false);
+  if (warp == 8) {
+    // ---- the MMA / TMA warp: once the workers have stored pair ws's codes,
+    // refill the slot of pair ws - 1 (its MMAs are complete: the workers
+    // waited for them before the barrier) and issue pair ws's eight MMAs
+    // (thread TC_WORKERS)
+    int slot = 0;
+    for (int ws = 0; ws < nws; ws++) {
+      pair_sync();
+      if (lane == 0) {
+        if (ws > 0) {
+          vxb::tc::wait_or_flag(&mdone, (ws - 1) & 1, a.err);
+          const int pslot = slot == 0 ? a.wr - 1 : slot - 1;
+          if (ws - 1 + a.wr < nws) {
+            load_weights(ws - 1 + a.wr, pslot);
+            load_x(ws - 1 + a.wr, pslot);
+          }
+        }
+        vxb::tc::tc_fence_after();
+        const uint32_t xa = smem_u32(sm + (size_t)slot * SM::SLOT);
+#pragma unroll
+        for (int j = 0; j < 2; j++)
+#pragma unroll
+          for (int b = 0; b < 2; b++)
+#pragma unroll
+            for (int k = 0; k < 2; k++)
+              vxb::tc::umma_bf16_ts(tmem + TC_DCOL + (2 * j + b) * NB, tmem + TC_ACOL + j * 32 + (2 * b + k) * 8,
+                                    vxb::tc::sw128_desc(xa + j * SM::XB + (2 * b + k) * 32, 16, 1024), ID, k);
+        vxb::tc::umma_commit(&mdone);
+      }
+      __syncwarp();
+      if (++slot == a.wr) slot = 0;
+    }
+  } else {  // ---- the eight worker warps
 
   const bool subn = (__ldg(a.hdr + 1) & TILED_FLAG_SUBNORMAL_SCALES) != 0;
   // epilogue row of this thread: 32q + lane = tile je, row pair pi, half ph
   const int je = 2 * q + (lane >> 4), pi = (lane & 15) & 7, ph = (lane & 15) >> 3;
   const int dtile = 2 * q + half;  // the tile this warp decodes
-  constexpr uint32_t ID = vxb::tc::idesc_bf16(128, NB, false);
   const uint32_t tq = (uint32_t)(32 * q) << 16;  // TMEM lane base of the quadrant
   float2 acc[NB / 2];
 #pragma unroll
@@ -229,16 +265,18 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
   auto epilogue = [&](int t, float s0, float s1) {
     tc_wait_warp(&mdone, t & 1, a.err);
     vxb::tc::tc_fence_after();
-    float v0[NB], v1[NB];
-    tmem_ld_nb<NB>(tmem + TC_DCOL + (0 + half) * NB + tq, v0);
-    tmem_ld_nb<NB>(tmem + TC_DCOL + (2 + half) * NB + tq, v1);
-    vxb::tc::tmem_wait_ld();
-    vxb::tc::tc_fence_before();
+    // one step's block at a time (fewer live registers), in step order,
+    // with packed f32x2 FMAs
 #pragma unroll
-    for (int n = 0; n < NB / 2; n++) {
-      acc[n].x = fmaf(s1, v1[2 * n], fmaf(s0, v0[2 * n], acc[n].x));
-      acc[n].y = fmaf(s1, v1[2 * n + 1], fmaf(s0, v0[2 * n + 1], acc[n].y));
+    for (int j = 0; j < 2; j++) {
+      float v[NB];
+      tmem_ld_nb<NB>(tmem + TC_DCOL + (2 * j + half) * NB + tq, v);
+      vxb::tc::tmem_wait_ld();
+      const float sj = j == 0 ? s0 : s1;
+#pragma unroll
+      for (int n = 0; n < NB / 2; n++) acc[n] = __ffma2_rn(make_float2(v[2 * n], v[2 * n + 1]), make_float2(sj, sj), acc[n]);
     }
+    vxb::tc::tc_fence_before();
   };
 
   float sp0 = 0.f, sp1 = 0.f;  // scales of the previous pair
@@ -247,17 +285,15 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
   for (int ws = 0; ws < nws; ws++) {
     tc_wait_warp(&wfull[slot], par, a.err);
     const uint8_t *wst = sm + (size_t)slot * SM::SLOT + 2 * SM::XB;
-    // step j: Q4_0 unit j of the tile (4 k16 steps); Q8_0 units 2j, 2j + 1
-    uint32_t r0[16], r1[16];
+    // the codes of this warp's tile, raw (decoded after the epilogue, which
+    // keeps the live registers low): step j = Q4_0 unit j (4 k16 steps), Q8_0
+    // units 2j, 2j + 1
+    constexpr int NU = FMT == 0 ? 2 : 4;
+    uint4 cw[NU];
     {
-      const uint8_t *tu = wst + dtile * TBYTES;
-      if (FMT == 0) {
-        tc_decode_tile<FMT>(tu, tu, lane, r0);
-        tc_decode_tile<FMT>(tu + UNIT, tu + UNIT, lane, r1);
-      } else {
-        tc_decode_tile<FMT>(tu, tu + UNIT, lane, r0);
-        tc_decode_tile<FMT>(tu + 2 * UNIT, tu + 3 * UNIT, lane, r1);
-      }
+      const uint8_t *tu = wst + dtile * TBYTES + lane * 16;
+#pragma unroll
+      for (int u = 0; u < NU; u++) cw[u] = *reinterpret_cast<const uint4 *>(tu + u * UNIT);
     }
     float sc0, sc1;
     {
@@ -278,34 +314,21 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
     }
     if (ws > 0) {
       // the previous pair's MMAs are complete after this: its accumulators
-      // are read, the A buffer is free, and its stage's slot can be refilled
+      // are read and the A buffer is free (the MMA warp refills its slot)
       epilogue(ws - 1, sp0, sp1);
-      const int pslot = slot == 0 ? a.wr - 1 : slot - 1;
-      if (threadIdx.x == 0 && ws - 1 + a.wr < nws) {
-        load_weights(ws - 1 + a.wr, pslot);
-        load_x(ws - 1 + a.wr, pslot);
-      }
-      __syncwarp();
     }
-    tmem_st_16x256b_x4(tmem + TC_ACOL + ((uint32_t)(32 * q + 16 * half) << 16), r0);
-    tmem_st_16x256b_x4(tmem + TC_ACOL + 32 + ((uint32_t)(32 * q + 16 * half) << 16), r1);
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      uint32_t r[16];
+      if (FMT == 0)
+        tc_decode_words<FMT>(cw[j], cw[j], r);
+      else
+        tc_decode_words<FMT>(cw[2 * j], cw[2 * j + 1], r);
+      tmem_st_16x256b_x4(tmem + TC_ACOL + 32 * j + ((uint32_t)(32 * q + 16 * half) << 16), r);
+    }
     vxb::tc::tmem_wait_st();
     vxb::tc::tc_fence_before();
-    workers_sync();
-    if (threadIdx.x == 0) {
-      vxb::tc::tc_fence_after();
-      const uint32_t xa = smem_u32(sm + (size_t)slot * SM::SLOT);
-#pragma unroll
-      for (int j = 0; j < 2; j++)
-#pragma unroll
-        for (int b = 0; b < 2; b++)
-#pragma unroll
-          for (int k = 0; k < 2; k++)
-            vxb::tc::umma_bf16_ts(tmem + TC_DCOL + (2 * j + b) * NB, tmem + TC_ACOL + j * 32 + (2 * b + k) * 8,
-                                  vxb::tc::sw128_desc(xa + j * SM::XB + (2 * b + k) * 32, 16, 1024), ID, k);
-      vxb::tc::umma_commit(&mdone);
-    }
-    __syncwarp();
+    pair_sync();
     sp0 = sc0;
     sp1 = sc1;
     if (++slot == a.wr) {
@@ -351,6 +374,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
       for (int n = 0; n < NB; n++) red[n * 128 + rr] = v[n];
     }
   }
+
+  }  // worker warps
 
   if (a.S > 1) {
     // ---- the S CTAs of the row group: CTA c sums a slice of the outputs over
@@ -431,8 +456,9 @@ int tc_resident(size_t smem, int cluster, int sms) {
 // cost that grows when two CTAs share an SM, so the plan spreads the row
 // groups' stages over every SM: the busiest SM's stages (CTAs spread evenly,
 // a second wave counted whole), plus about 0.7 us for a cluster reduction.
-// The co-residency of clusters is taken from the plain per-SM occupancy
-// (clusters of up to 8 CTAs pack into the GPCs at two CTAs per SM).
+// The co-residency of clusters is taken from the plain per-SM occupancy (the
+// cluster occupancy query reports fewer co-resident clusters of 3 than run
+// in one wave in practice: trusting it doubled the 11008x4096 time).
 template <int FMT, int NB>
 TcPlan tc_plan_t(const vxb_ctx *ctx, const TiledGeom &g) {
   using SM = TcSmem<FMT, NB>;
@@ -545,12 +571,16 @@ int tc_launch_t(vxb_ctx *ctx, const TcArgs &a0, const uint16_t *x, const TiledGe
   return VXB_OK;
 }
 
-// Routing by measurement (kernel_bench, 7B shapes, batch 32): the
-// tensor-core kernel is faster than the mma.sync group kernel on up to ~11k
-// rows (4096x4096 10.3 us against 11.8, 4096x11008 19.6 against 21.9,
-// 11008x4096 21.2 against 22.1), for Q4_0 from batch 17 and for Q8_0 from
-// batch 9; with more rows the group kernel wins (a second CTA on an SM adds
-// little throughput to this kernel: 32000x4096 76 us against 50).
+// Routing by measurement (kernel_bench, back-to-back launches over rotating
+// weight copies): the tensor-core kernel is faster than the mma.sync group
+// kernel on up to ~11k rows for Q4_0 from batch 17 and for Q8_0 from batch 9
+// (batch 32, Q4_0: 4096x4096 10.0 us against 11.8, 4096x11008 18.5 against
+// 21.9, 11008x4096 19.6 against 22.0), and on 16k rows and more at batch 28
+// and above (22016x4096 41.2 against 43.8, 32000x4096 41.9 against 50.5);
+// Q8_0 with 28k rows and more takes it at every batch (32000x4096, batch 9:
+// 45.7 against 49.5). Between 11.5k and 16k rows (12288x4096: 32.8 against
+// 31.4) the splits that would fill the SMs come as clusters of 3 that spill
+// into a second wave, and the group kernel stays.
 // VXB_GEMV_TCGEN05=1 sends every batch 9-32 to it, =0 none.
 int tc_mode() {
   static const int mode = [] {
@@ -592,8 +622,9 @@ bool gemv_tc_eligible(int fmt, int N, int batch) {
   const int m = tc_mode();
   if (m >= 0) return m == 1;
   // one wave of two CTAs per SM covers up to ~11.5k rows with a k-split of 3
-  if (N > 11520) return false;
-  return fmt == VXB_Q8_0 || batch >= 17;
+  if (N <= 11520) return fmt == VXB_Q8_0 || batch >= 17;
+  if (fmt == VXB_Q8_0 && N >= 28000) return true;
+  return N >= 16384 && batch >= 28;
 }
 
 int gemv_tc_splits(const vxb_ctx *ctx, int fmt, int N, int K, int batch) {
