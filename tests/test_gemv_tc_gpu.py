@@ -22,7 +22,7 @@ from vortex_b200 import quant as Q
 OFMT = {2: O.GGML_Q4_0, 8: O.GGML_Q8_0}
 fails = []
 for fmt in (2, 8):
-    for (N, K) in ((1000, 160), (300, 4096), (11008, 4096), (4096, 11008), (22016, 4096)):
+    for (N, K) in ((1000, 160), (300, 4096), (11008, 4096), (4096, 11008), (12288, 4096), (22016, 4096)):
         for B in (9, 17, 32):
             rng = np.random.default_rng(N + K + B)
             w = rng.normal(0.0, 0.02, (N, K)).astype(np.float32)
@@ -51,7 +51,7 @@ def test_gemv_tcgen05_matches_oracle(cuda_ok):
 
 
 @pytest.mark.parametrize("fmt_name,N,K,B,kernel", [
-    ("Q4_0", 4096, 4096, 32, 2), ("Q4_0", 11008, 4096, 16, 1), ("Q4_0", 12288, 4096, 32, 1),
+    ("Q4_0", 4096, 4096, 32, 2), ("Q4_0", 11008, 4096, 16, 1), ("Q4_0", 12288, 4096, 32, 2),
     ("Q4_0", 22016, 4096, 32, 2), ("Q4_0", 32000, 4096, 32, 2), ("Q4_0", 32000, 4096, 24, 1),
     ("Q8_0", 4096, 4096, 9, 2), ("Q8_0", 32000, 4096, 9, 2), ("Q8_0", 22016, 4096, 16, 1)])
 def test_gemv_default_routing(cuda_ok, fmt_name, N, K, B, kernel):

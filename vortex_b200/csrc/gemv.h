@@ -19,8 +19,8 @@ int gemv_launch(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, const 
                 int y_dtype, void *d_y, const float *d_resid, void *stream, const GemvPlan *plan_override);
 
 // Batches 9..32 on the tcgen05 kernel (gemv_tc.cu): by default Q4_0 batches
-// 17-32 and Q8_0 batches 9-32 with up to 11520 rows, batches 28-32 with 16384
-// rows or more, and Q8_0 with 28000 rows or more (VXB_GEMV_TCGEN05=1: every
+// 17-32 and Q8_0 batches 9-32 with up to 16384 rows, batches 28-32 with more
+// rows, and Q8_0 with 28000 rows or more (VXB_GEMV_TCGEN05=1: every
 // batch 9-32, =0: none). d_err is the device error word.
 bool gemv_tc_eligible(int fmt, int N, int batch);
 int gemv_tc_splits(const vxb_ctx *ctx, int fmt, int N, int K, int batch);

@@ -481,6 +481,9 @@ TcPlan tc_plan_t(const vxb_ctx *ctx, const TiledGeom &g) {
     const int slots = per_sm * sms;
     const int waves = (ctas + slots - 1) / slots;
     if (waves > 1 && S > 1) continue;  // a split that needs a second wave never pays
+    // clusters pack into the GPCs with some loss: a cluster split must leave a
+    // tenth of the slots free to stay in one wave
+    if (S > 1 && ctas * 10 > slots * 9) continue;
     // stages of the busiest SM: its CTAs (one wave at a time) share it
     const int on_sm = std::min(per_sm, (std::min(ctas, slots) + sms - 1) / sms);
     const double t_stage = on_sm > 1 ? 0.55 : 1.0;  // per CTA and stage, relative: two CTAs overlap
@@ -573,14 +576,12 @@ int tc_launch_t(vxb_ctx *ctx, const TcArgs &a0, const uint16_t *x, const TiledGe
 
 // Routing by measurement (kernel_bench, back-to-back launches over rotating
 // weight copies): the tensor-core kernel is faster than the mma.sync group
-// kernel on up to ~11k rows for Q4_0 from batch 17 and for Q8_0 from batch 9
-// (batch 32, Q4_0: 4096x4096 10.0 us against 11.8, 4096x11008 18.5 against
-// 21.9, 11008x4096 19.6 against 22.0), and on 16k rows and more at batch 28
-// and above (22016x4096 41.2 against 43.8, 32000x4096 41.9 against 50.5);
-// Q8_0 with 28k rows and more takes it at every batch (32000x4096, batch 9:
-// 45.7 against 49.5). Between 11.5k and 16k rows (12288x4096: 32.8 against
-// 31.4) the splits that would fill the SMs come as clusters of 3 that spill
-// into a second wave, and the group kernel stays.
+// kernel on up to 16k rows for Q4_0 from batch 17 and for Q8_0 from batch 9
+// (batch 32, Q4_0: 4096x4096 10.0 us against 11.8, 4096x11008 18.6 against
+// 21.9, 11008x4096 19.6 against 22.0, 12288x4096 25.8 against 31.4), and on
+// more rows at batch 28 and above (22016x4096 41.2 against 43.8, 32000x4096
+// 41.9 against 50.5); Q8_0 with 28k rows and more takes it at every batch
+// (32000x4096, batch 9: 45.7 against 49.5).
 // VXB_GEMV_TCGEN05=1 sends every batch 9-32 to it, =0 none.
 int tc_mode() {
   static const int mode = [] {
@@ -621,8 +622,8 @@ bool gemv_tc_eligible(int fmt, int N, int batch) {
   if (batch < 9 || batch > 32) return false;
   const int m = tc_mode();
   if (m >= 0) return m == 1;
-  // one wave of two CTAs per SM covers up to ~11.5k rows with a k-split of 3
-  if (N <= 11520) return fmt == VXB_Q8_0 || batch >= 17;
+  // up to 16k rows the row groups' k-splits fill one wave of two CTAs per SM
+  if (N <= 16384) return fmt == VXB_Q8_0 || batch >= 17;
   if (fmt == VXB_Q8_0 && N >= 28000) return true;
   return N >= 16384 && batch >= 28;
 }
