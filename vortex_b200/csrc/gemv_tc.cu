@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   float *red = reinterpret_cast<float *>(sm + SM::red_off(a.wr));  // [NB][128]
-  __shared__ __align__(8) uint64_t wfull[TC_MAX_WR], mdone;
+  __shared__ __align__(8) uint64_t wfull[TC_MAX_WR], mdone[2];
   __shared__ uint32_t tmem_base_s;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = warp & 3, half = warp >> 2;
@@ -190,7 +190,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
   }
   if (threadIdx.x == 0) {
     for (int i = 0; i < a.wr; i++) mbar_init(&wfull[i], 1);
-    mbar_init(&mdone, 1);
+    mbar_init(&mdone[0], 1);
+    mbar_init(&mdone[1], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   vxb::tc::tc_fence_before();
@@ -218,36 +219,42 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
     for (int ws = 0; ws < pre; ws++) load_x(ws, ws);
   }
   constexpr uint32_t ID = vxb::tc::idesc_bf16(128, NB, false);
+  const int nsteps = 2 * nws;  // 64-column steps, two per stage
   if (warp == 8) {
-    // ---- the MMA / TMA warp: once the workers have stored pair ws's codes,
-    // refill the slot of pair ws - 1 (its MMAs are complete: the workers
-    // waited for them before the barrier) and issue pair ws's eight MMAs
-    // (thread TC_WORKERS)
+    // ---- the MMA / TMA warp (thread TC_WORKERS): once the workers have stored
+    // step i's codes in A buffer i % 2, issue its four MMAs into accumulator
+    // buffer i % 2 and commit them to mdone[i % 2]; at the first step of a
+    // stage, wait for the previous stage's last MMAs and refill its slot
     int slot = 0;
     for (int ws = 0; ws < nws; ws++) {
-      pair_sync();
-      if (lane == 0) {
-        if (ws > 0) {
-          vxb::tc::wait_or_flag(&mdone, (ws - 1) & 1, a.err);
-          const int pslot = slot == 0 ? a.wr - 1 : slot - 1;
-          if (ws - 1 + a.wr < nws) {
-            load_weights(ws - 1 + a.wr, pslot);
-            load_x(ws - 1 + a.wr, pslot);
-          }
-        }
-        vxb::tc::tc_fence_after();
-        const uint32_t xa = smem_u32(sm + (size_t)slot * SM::SLOT);
 #pragma unroll
-        for (int j = 0; j < 2; j++)
+      for (int j = 0; j < 2; j++) {
+        const int i = 2 * ws + j;
+        pair_sync();
+        if (lane == 0) {
+          vxb::tc::tc_fence_after();
+          const uint32_t xa = smem_u32(sm + (size_t)slot * SM::SLOT);
 #pragma unroll
           for (int b = 0; b < 2; b++)
 #pragma unroll
             for (int k = 0; k < 2; k++)
-              vxb::tc::umma_bf16_ts(tmem + TC_DCOL + (2 * j + b) * NB, tmem + TC_ACOL + j * 32 + (2 * b + k) * 8,
+              vxb::tc::umma_bf16_ts(tmem + TC_DCOL + (uint32_t)(j * 2 + b) * NB,
+                                    tmem + TC_ACOL + j * 32 + (2 * b + k) * 8,
                                     vxb::tc::sw128_desc(xa + j * SM::XB + (2 * b + k) * 32, 16, 1024), ID, k);
-        vxb::tc::umma_commit(&mdone);
+          vxb::tc::umma_commit(&mdone[j]);
+          if (j == 0 && i >= 2) {
+            // step i - 1 (odd: mdone[1], its (i - 1) / 2-th phase) was the
+            // last reader of the previous stage's slot
+            vxb::tc::wait_or_flag(&mdone[1], ((i - 1) >> 1) & 1, a.err);
+            const int pslot = slot == 0 ? a.wr - 1 : slot - 1;
+            if (ws - 1 + a.wr < nws) {
+              load_weights(ws - 1 + a.wr, pslot);
+              load_x(ws - 1 + a.wr, pslot);
+            }
+          }
+        }
+        __syncwarp();
       }
-      __syncwarp();
       if (++slot == a.wr) slot = 0;
     }
   } else {  // ---- the eight worker warps
@@ -261,82 +268,73 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
 #pragma unroll
   for (int n = 0; n < NB / 2; n++) acc[n] = make_float2(0.f, 0.f);
 
-  // epilogue of pair t: block `half` of both steps, rows of quadrant q
-  auto epilogue = [&](int t, float s0, float s1) {
-    tc_wait_warp(&mdone, t & 1, a.err);
+  // epilogue of step i: block `half` of the step, rows of quadrant q, in
+  // accumulator buffer i % 2 (packed f32x2 FMAs; the blocks add in step order)
+  auto epilogue = [&](int i, float sc) {
+    tc_wait_warp(&mdone[i & 1], (i >> 1) & 1, a.err);
     vxb::tc::tc_fence_after();
-    // one step's block at a time (fewer live registers), in step order,
-    // with packed f32x2 FMAs
-#pragma unroll
-    for (int j = 0; j < 2; j++) {
-      float v[NB];
-      tmem_ld_nb<NB>(tmem + TC_DCOL + (2 * j + half) * NB + tq, v);
-      vxb::tc::tmem_wait_ld();
-      const float sj = j == 0 ? s0 : s1;
-#pragma unroll
-      for (int n = 0; n < NB / 2; n++) acc[n] = __ffma2_rn(make_float2(v[2 * n], v[2 * n + 1]), make_float2(sj, sj), acc[n]);
-    }
+    float v[NB];
+    tmem_ld_nb<NB>(tmem + TC_DCOL + (uint32_t)((i & 1) * 2 + half) * NB + tq, v);
+    vxb::tc::tmem_wait_ld();
     vxb::tc::tc_fence_before();
+#pragma unroll
+    for (int n = 0; n < NB / 2; n++) acc[n] = __ffma2_rn(make_float2(v[2 * n], v[2 * n + 1]), make_float2(sc, sc), acc[n]);
   };
 
-  float sp0 = 0.f, sp1 = 0.f;  // scales of the previous pair
+  // Step i writes A buffer i % 2 and accumulator buffer i % 2; the epilogue
+  // of step i - 1 runs after step i's barrier, while the tensor core works
+  // on step i. A buffer i % 2 is free again once step i - 2's MMAs are
+  // complete (the epilogue of step i - 2 waited for them).
+  float s_prev = 0.f;  // scale of the previous step's block for this thread's row
   int slot = 0;
   uint32_t par = 0;
+  constexpr int NU = FMT == 0 ? 2 : 4;
+  uint4 cw[NU];  // this warp's tile codes of the current stage (raw)
   for (int ws = 0; ws < nws; ws++) {
     tc_wait_warp(&wfull[slot], par, a.err);
     const uint8_t *wst = sm + (size_t)slot * SM::SLOT + 2 * SM::XB;
-    // the codes of this warp's tile, raw (decoded after the epilogue, which
-    // keeps the live registers low): step j = Q4_0 unit j (4 k16 steps), Q8_0
-    // units 2j, 2j + 1
-    constexpr int NU = FMT == 0 ? 2 : 4;
-    uint4 cw[NU];
     {
       const uint8_t *tu = wst + dtile * TBYTES + lane * 16;
 #pragma unroll
       for (int u = 0; u < NU; u++) cw[u] = *reinterpret_cast<const uint4 *>(tu + u * UNIT);
     }
-    float sc0, sc1;
-    {
-      const uint8_t *ue = wst + je * TBYTES + 512;
-      uint32_t w0, w1;
-      if (FMT == 0) {
-        const uint2 t0 = *reinterpret_cast<const uint2 *>(ue + pi * 8);
-        const uint2 t1 = *reinterpret_cast<const uint2 *>(ue + UNIT + pi * 8);
-        w0 = half ? t0.y : t0.x;
-        w1 = half ? t1.y : t1.x;
-      } else {
-        w0 = *reinterpret_cast<const uint32_t *>(ue + half * UNIT + pi * 4);
-        w1 = *reinterpret_cast<const uint32_t *>(ue + (2 + half) * UNIT + pi * 4);
-      }
-      const float2 d0 = decode_scales(w0, subn), d1 = decode_scales(w1, subn);
-      sc0 = ph ? d0.y : d0.x;
-      sc1 = ph ? d1.y : d1.x;
-    }
-    if (ws > 0) {
-      // the previous pair's MMAs are complete after this: its accumulators
-      // are read and the A buffer is free (the MMA warp refills its slot)
-      epilogue(ws - 1, sp0, sp1);
-    }
 #pragma unroll
     for (int j = 0; j < 2; j++) {
-      uint32_t r[16];
-      if (FMT == 0)
-        tc_decode_words<FMT>(cw[j], cw[j], r);
-      else
-        tc_decode_words<FMT>(cw[2 * j], cw[2 * j + 1], r);
-      tmem_st_16x256b_x4(tmem + TC_ACOL + 32 * j + ((uint32_t)(32 * q + 16 * half) << 16), r);
+      const int i = 2 * ws + j;
+      float sc;
+      {
+        // the f16 scale of block `half` of step j for this thread's row
+        const uint8_t *ue = wst + je * TBYTES + 512;
+        uint32_t w;
+        if (FMT == 0) {
+          const uint2 t2 = *reinterpret_cast<const uint2 *>(ue + j * UNIT + pi * 8);
+          w = half ? t2.y : t2.x;
+        } else {
+          w = *reinterpret_cast<const uint32_t *>(ue + (2 * j + half) * UNIT + pi * 4);
+        }
+        const float2 d = decode_scales(w, subn);
+        sc = ph ? d.y : d.x;
+      }
+      {
+        uint32_t r[16];
+        if (FMT == 0)
+          tc_decode_words<FMT>(cw[j], cw[j], r);
+        else
+          tc_decode_words<FMT>(cw[2 * j], cw[2 * j + 1], r);
+        tmem_st_16x256b_x4(tmem + TC_ACOL + 32 * j + ((uint32_t)(32 * q + 16 * half) << 16), r);
+      }
+      vxb::tc::tmem_wait_st();
+      vxb::tc::tc_fence_before();
+      pair_sync();
+      if (i > 0) epilogue(i - 1, s_prev);
+      s_prev = sc;
     }
-    vxb::tc::tmem_wait_st();
-    vxb::tc::tc_fence_before();
-    pair_sync();
-    sp0 = sc0;
-    sp1 = sc1;
     if (++slot == a.wr) {
       slot = 0;
       par ^= 1u;
     }
   }
-  if (nws > 0) epilogue(nws - 1, sp0, sp1);
+  if (nsteps > 0) epilogue(nsteps - 1, s_prev);
 
   // rows of quadrant q: block-0 warps (half 0) and block-1 warps (half 1) add
   asm volatile("griddepcontrol.wait;" ::: "memory");  // before any global write of this thread
