@@ -193,3 +193,24 @@ def test_append_one_token_per_sequence_then_attend(KV):
             keys[i] = np.concatenate([keys[i], bf16_values(k[i:i + 1])])
             vals[i] = np.concatenate([vals[i], bf16_values(v[i:i + 1])])
     _check(KV, c, keys, vals, [40] * n, Hq, H, D)
+
+
+def test_decode_attention_int8_scale_range(KV):
+    """int8 pages whose V magnitudes span 1e-4 .. 1e4 from token to token: the
+    kernel scales P times the V scale into the f16 range per page (and
+    rescales O when a page needs a smaller factor), so every page keeps its
+    share of the output."""
+    H, D, Hq = 8, 128, 32
+    lens = [300, 77]
+    c = KV.PagedKVCache(num_layers=1, num_heads=H, head_dim=D, block_size=16, max_blocks=64, max_seqs=4,
+                        kv_dtype=KV.I8)
+    rng = np.random.default_rng(21)
+    keys, vals = {}, {}
+    for i, L in enumerate(lens):
+        mag = 10.0 ** rng.uniform(-4, 4, size=(L, 1, 1))
+        k = (rng.standard_normal((L, H, D)) * 0.1).astype(np.float32)
+        v = (rng.standard_normal((L, H, D)) * mag).astype(np.float32)
+        c.append_seq(0, 100 + i, bf16_tensor(k), bf16_tensor(v))
+        keys[i] = int8_quant_rows_np(bf16_values(k))
+        vals[i] = int8_quant_rows_np(bf16_values(v))
+    _check(KV, c, keys, vals, lens, Hq, H, D)

@@ -16,9 +16,18 @@
 //   O += P V    : A = P re-packed from the S fragments, B = V via ldmatrix.trans
 // Warps merge through shared memory; splits merge deterministically in the
 // last-arriving CTA of each (sequence, kv head) (counter in global memory).
-// int8 caches stage int8 pages and one f32 scale per (token, head); the K
-// scale multiplies the scores and the V scale is folded into P.
+// int8 caches stage the raw int8 pages (16-byte chunks XOR-swizzled) and one
+// f32 scale per (token, head), and build the MMA fragments straight from
+// them: ldmatrix gives each lane 4 bytes of one K row (with the head
+// dimension permuted the same way in q) or, with .trans, 2 tokens x 2
+// columns of V; XOR 0x80, a byte permute with the f16 magic 0x64 and one
+// f16 subtraction turn two codes into exact f16 integers. q is f16 scaled
+// per row by 2^-e (exact for every element within 2^-28 of the row maximum),
+// P times the V scale is split into f16 hi + lo scaled by 2^k, k chosen per
+// page from the page's largest V scale (O is rescaled with the softmax
+// correction when k drops). The K scale multiplies the scores.
 #include <atomic>
+#include <climits>
 #include <cstdlib>
 #include <cuda_bf16.h>
 
@@ -93,20 +102,56 @@ __device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t &hi, uin
   lo = pack_bf16x2(a - ha, b - hb);
 }
 
-// Four int8 codes -> two bf16x2 words, exactly and without the conversion
-// pipe: each byte b (as b ^ 0x80 = b + 128 unsigned) becomes the f32
-// 2^23 + b + 128 by one byte permute, one f32 subtraction leaves b, and as
-// |b| <= 128 the value's bf16 is the upper half of its f32, so one more
-// permute packs two of them.
-__device__ __forceinline__ void i8x4_to_bf16(uint32_t w, uint32_t &lo, uint32_t &hi) {
-  const float B = 8388736.0f;  // 2^23 + 128
-  const uint32_t u = w ^ 0x80808080u;
-  const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)) - B;
-  const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441)) - B;
-  const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)) - B;
-  const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443)) - B;
-  lo = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
-  hi = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
+__device__ __forceinline__ void mma_f16(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+__device__ __forceinline__ float2 f16x2_to_f32(uint32_t v) {
+  return __half22float2(*reinterpret_cast<const __half2 *>(&v));
+}
+
+// (a, b) -> hi = f16x2(a, b) and lo = f16x2(a - hi.a, b - hi.b)
+__device__ __forceinline__ void split_f16x2(float a, float b, uint32_t &hi, uint32_t &lo) {
+  hi = pack_f16x2(a, b);
+  const float2 h = f16x2_to_f32(hi);
+  lo = pack_f16x2(a - h.x, b - h.y);
+}
+
+__device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// Two int8 codes of w (bytes selected by `sel` with the magic byte 0x64 in
+// the high halves) -> f16x2 of the exact codes: (b ^ 0x80) = c + 128 in the
+// low byte of f16 0x64xx is 1024 + c + 128, minus 1152.
+__device__ __forceinline__ uint32_t i8pair_f16(uint32_t w_xor80, uint32_t sel) {
+  return hsub2_u(__byte_perm(w_xor80, 0x64646464u, sel), 0x64806480u);
+}
+
+// v * 2^e for |e| <= 252 (two exact power-of-two factors)
+__device__ __forceinline__ float mul_pow2f(float v, int e) {
+  const int e1 = e / 2, e2 = e - e1;
+  return v * __int_as_float((127 + e1) << 23) * __int_as_float((127 + e2) << 23);
+}
+
+// byte offset of 16-byte chunk c of token row r in a raw int8 page: the
+// chunks of 8 consecutive rows land in distinct bank groups for ldmatrix
+template <int D>
+__device__ __forceinline__ uint32_t swz_raw(int r, int c) {
+  if (D == 128) return (uint32_t)(r * D + ((c ^ (r & 7)) << 4));
+  return (uint32_t)(r * D + ((c ^ ((r >> 1) & 3)) << 4));
 }
 
 // byte offset of 16-byte chunk c of token row r in a swizzled page tile
@@ -117,12 +162,12 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
 
 template <int D, bool INT8>
 struct Smem {
-  // per warp, per stage: bf16 tiles (converted for int8) and raw int8 pages
+  // per warp, per stage: bf16 tiles, or raw int8 pages and their scales
   static constexpr int TILE = PAGE * D * 2;                  // one bf16 page tile
   static constexpr int RAW = INT8 ? PAGE * D : 0;            // one int8 page
   static constexpr int SC = INT8 ? PAGE * 4 : 0;             // per-token scales
   static constexpr int STAGE = INT8 ? 2 * RAW + 2 * SC : 2 * TILE;
-  static constexpr int WARP = 2 * STAGE + (INT8 ? 2 * TILE : 0);
+  static constexpr int WARP = 2 * STAGE;
   static constexpr int TOTAL = WARPS * WARP;
 };
 
@@ -150,9 +195,45 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
   uint8_t *wsm = smem + (size_t)warp * SM::WARP;
   const uint32_t wsm_s = (uint32_t)__cvta_generic_to_shared(wsm);
 
-  // Q fragments (rows = the G query heads of this group, padded to 16)
+  // Q fragments (rows = the G query heads of this group, padded to 16);
+  // rs0 / rs1 multiply the scores of rows g / g+8
   uint32_t qa[D / 16][4];
-  {
+  float rs0 = a.scale_log2, rs1 = a.scale_log2;
+  if constexpr (INT8) {
+    // f16 * 2^-e per row (max |q| * 2^-e in [2^14, 2^15)), head dimension
+    // permuted like the K fragments: lane quad q4 of k16 step ks holds
+    // d = 16 ks + 4 q4 .. +3 (fragment columns 2q4, 2q4+1, 2q4+8, 2q4+9)
+    const uint2 *qrow0 = reinterpret_cast<const uint2 *>(a.q + ((size_t)i * a.Hq + (size_t)h * a.G + g) * D);
+    const uint2 *qrow1 = reinterpret_cast<const uint2 *>(a.q + ((size_t)i * a.Hq + (size_t)h * a.G + g + 8) * D);
+    const bool v0 = g < a.G, v1 = g + 8 < a.G;
+    uint2 r0[D / 16], r1[D / 16];
+    unsigned mx0 = 0, mx1 = 0;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ks++) {
+      r0[ks] = v0 ? __ldcg(qrow0 + ks * 4 + q4) : make_uint2(0u, 0u);
+      r1[ks] = v1 ? __ldcg(qrow1 + ks * 4 + q4) : make_uint2(0u, 0u);
+      mx0 = max(mx0, max(max(r0[ks].x & 0x7FFFu, (r0[ks].x >> 16) & 0x7FFFu), max(r0[ks].y & 0x7FFFu, (r0[ks].y >> 16) & 0x7FFFu)));
+      mx1 = max(mx1, max(max(r1[ks].x & 0x7FFFu, (r1[ks].x >> 16) & 0x7FFFu), max(r1[ks].y & 0x7FFFu, (r1[ks].y >> 16) & 0x7FFFu)));
+    }
+    mx0 = max(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = max(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = max(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = max(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const int e0 = (mx0 != 0 && mx0 < 0x7F80u) ? max((int)(mx0 >> 7), 1) - 127 - 14 : 0;
+    const int e1 = (mx1 != 0 && mx1 < 0x7F80u) ? max((int)(mx1 >> 7), 1) - 127 - 14 : 0;
+    auto cvt = [](uint32_t w, int e) {
+      return pack_f16x2(mul_pow2f(__uint_as_float(w << 16), -e), mul_pow2f(__uint_as_float(w & 0xFFFF0000u), -e));
+    };
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ks++) {
+      qa[ks][0] = cvt(r0[ks].x, e0);
+      qa[ks][1] = cvt(r1[ks].x, e1);
+      qa[ks][2] = cvt(r0[ks].y, e0);
+      qa[ks][3] = cvt(r1[ks].y, e1);
+    }
+    rs0 = mul_pow2f(a.scale_log2, e0);
+    rs1 = mul_pow2f(a.scale_log2, e1);
+  } else {
     const uint32_t *qrow0 = reinterpret_cast<const uint32_t *>(a.q + ((size_t)i * a.Hq + (size_t)h * a.G + g) * D);
     const uint32_t *qrow1 = reinterpret_cast<const uint32_t *>(a.q + ((size_t)i * a.Hq + (size_t)h * a.G + g + 8) * D);
     const bool v0 = g < a.G, v1 = g + 8 < a.G;
@@ -169,6 +250,7 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
 #pragma unroll
   for (int dt = 0; dt < D / 8; dt++) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  int kcur = INT_MAX;  // int8: O is in units of 2^-kcur (P scaled by 2^kcur); INT_MAX: not set yet
 
   const int pg0 = t0 / PAGE, pg1 = t1 > t0 ? (t1 + PAGE - 1) / PAGE : pg0;
   const int npages = pg1 - pg0;
@@ -200,8 +282,8 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
       for (int c = lane; c < PAGE * RCH; c += 32) {
         const int r = c / RCH, cc = c % RCH;
         const int bytes = tok0 + r < len ? 16 : 0;
-        cp_async16(st_s + r * D + cc * 16, kp + (size_t)r * D + cc * 16, bytes);
-        cp_async16(st_s + SM::RAW + r * D + cc * 16, vp + (size_t)r * D + cc * 16, bytes);
+        cp_async16(st_s + swz_raw<D>(r, cc), kp + (size_t)r * D + cc * 16, bytes);
+        cp_async16(st_s + SM::RAW + swz_raw<D>(r, cc), vp + (size_t)r * D + cc * 16, bytes);
       }
       {
         // per-token scales: lanes 0-15 the K scales, lanes 16-31 the V scales
@@ -231,6 +313,7 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
     const int tok0 = p * PAGE;
     uint32_t kt = wsm_s + stage * SM::STAGE, vt = kt + SM::TILE;
     float ksc[2][2], vsc[2][2];
+    float kfac = 1.f;  // O correction when this page lowers kcur
     if (INT8) {
       // scales of this lane's token columns (tok 2q, 2q+1 of each n-tile)
       const float *scs = reinterpret_cast<const float *>(wsm + stage * SM::STAGE + 2 * SM::RAW);
@@ -243,35 +326,46 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
           ksc[nt][e] = ok ? scs[r] : 0.f;
           vsc[nt][e] = ok ? scs[PAGE + r] : 0.f;
         }
-      // int8 -> bf16 (exact) into the swizzled tiles
-      const int8_t *rk = reinterpret_cast<const int8_t *>(wsm + stage * SM::STAGE);
-      uint8_t *tk = wsm + 2 * SM::STAGE;
-      for (int c = lane; c < 2 * PAGE * CHUNKS; c += 32) {
-        const bool isv = c >= PAGE * CHUNKS;
-        const int cc_ = isv ? c - PAGE * CHUNKS : c;
-        const int r = cc_ / CHUNKS, cc = cc_ % CHUNKS;
-        const int8_t *src = rk + (isv ? SM::RAW : 0) + r * D + cc * 8;
-        const uint2 raw = *reinterpret_cast<const uint2 *>(src);
-        uint4 outv;
-        i8x4_to_bf16(raw.x, outv.x, outv.y);
-        i8x4_to_bf16(raw.y, outv.z, outv.w);
-        *reinterpret_cast<uint4 *>(tk + (isv ? SM::TILE : 0) + swz<D>(r, cc)) = outv;
+      // this page's P scaling 2^kp from its largest V scale (P * scale < 2^15)
+      float vm = fmaxf(fmaxf(vsc[0][0], vsc[0][1]), fmaxf(vsc[1][0], vsc[1][1]));
+      const unsigned vmb = __reduce_max_sync(0xffffffffu, __float_as_uint(vm));
+      if (vmb != 0u) {
+        const int kp = min(120, max(-120, 14 - ((int)((vmb >> 23) & 0xFFu) - 127)));
+        if (kp < kcur) {
+          kfac = kcur == INT_MAX ? 1.f : (kp - kcur >= -126 ? __int_as_float((127 + kp - kcur) << 23) : 0.f);
+          kcur = kp;
+        }
       }
-      __syncwarp();
-      kt = wsm_s + 2 * SM::STAGE;
-      vt = kt + SM::TILE;
     }
-
     // S = Q K^T for the page's 16 tokens (two n-tiles of 8)
     float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    if constexpr (INT8) {
+      // ldmatrix on the raw page: matrix mi = tokens 8 (mi & 1) .. +7 of
+      // 16-byte chunk 2 ks2 + (mi >> 1); lane (g, q4) gets bytes 4 q4 .. +3
+      // of token g, the fragment columns {2q4, 2q4+1 | 2q4+8, 2q4+9}
+      const uint32_t kr = wsm_s + stage * SM::STAGE;
+      const int mi = lane >> 3;
+      const int tok = (mi & 1) * 8 + (lane & 7);
 #pragma unroll
-    for (int ks = 0; ks < D / 16; ks++) {
-      const int r = (lane >> 4) * 8 + (lane & 7);
-      const int c = ks * 2 + ((lane >> 3) & 1);
-      uint32_t b0, b1, b2, b3;
-      ldsm_x4(kt + swz<D>(r, c), b0, b1, b2, b3);
-      mma_bf16(s[0], qa[ks], b0, b1);
-      mma_bf16(s[1], qa[ks], b2, b3);
+      for (int ks2 = 0; ks2 < D / 32; ks2++) {
+        uint32_t w[4];
+        ldsm_x4(kr + swz_raw<D>(tok, 2 * ks2 + (mi >> 1)), w[0], w[1], w[2], w[3]);
+#pragma unroll
+        for (int m = 0; m < 4; m++) {
+          const uint32_t u = w[m] ^ 0x80808080u;
+          mma_f16(s[m & 1], qa[2 * ks2 + (m >> 1)], i8pair_f16(u, 0x4140), i8pair_f16(u, 0x4342));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ks++) {
+        const int r = (lane >> 4) * 8 + (lane & 7);
+        const int c = ks * 2 + ((lane >> 3) & 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kt + swz<D>(r, c), b0, b1, b2, b3);
+        mma_bf16(s[0], qa[ks], b0, b1);
+        mma_bf16(s[1], qa[ks], b2, b3);
+      }
     }
     // scale, mask, online softmax
 #pragma unroll
@@ -279,7 +373,7 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
 #pragma unroll
       for (int e = 0; e < 4; e++) {
         const int tok = tok0 + nt * 8 + q4 * 2 + (e & 1);
-        float v = s[nt][e] * a.scale_log2;
+        float v = s[nt][e] * (e < 2 ? rs0 : rs1);
         if (INT8) v *= ksc[nt][e & 1];
         s[nt][e] = tok < len ? v : -INFINITY;
       }
@@ -304,22 +398,53 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
     }
     l0 = l0 * c0 + (pp[0][0] + pp[0][1] + pp[1][0] + pp[1][1]);
     l1 = l1 * c1 + (pp[0][2] + pp[0][3] + pp[1][2] + pp[1][3]);
+    // O's correction (int8: times 2^(kp - k) when this page lowered k)
+    const float oc0 = c0 * kfac, oc1 = c1 * kfac;
 #pragma unroll
     for (int dt = 0; dt < D / 8; dt++) {
-      o[dt][0] *= c0;
-      o[dt][1] *= c0;
-      o[dt][2] *= c1;
-      o[dt][3] *= c1;
+      o[dt][0] *= oc0;
+      o[dt][1] *= oc0;
+      o[dt][2] *= oc1;
+      o[dt][3] *= oc1;
     }
-    if (INT8) {
+    uint32_t pa[4], pl[4];
+    if constexpr (INT8) {
+      // P * V scale * 2^k as f16 hi + lo (22 significant bits)
+      const float k2 = kcur == INT_MAX ? 1.f : mul_pow2f(1.f, kcur);
 #pragma unroll
       for (int nt = 0; nt < 2; nt++)
 #pragma unroll
-        for (int e = 0; e < 4; e++) pp[nt][e] *= vsc[nt][e & 1];
-    }
+        for (int e = 0; e < 4; e++) pp[nt][e] *= vsc[nt][e & 1] * k2;
+      split_f16x2(pp[0][0], pp[0][1], pa[0], pl[0]);
+      split_f16x2(pp[0][2], pp[0][3], pa[1], pl[1]);
+      split_f16x2(pp[1][0], pp[1][1], pa[2], pl[2]);
+      split_f16x2(pp[1][2], pp[1][3], pa[3], pl[3]);
+      // ldmatrix.trans on the raw V page: lane (g, q4) gets V[2q4][2g],
+      // V[2q4][2g+1], V[2q4+1][2g], V[2q4+1][2g+1] of its 8-token x 16-byte
+      // matrix; bytes (0, 2) are the B fragment of column 2g (the even
+      // n-tile of the chunk), bytes (1, 3) of column 2g + 1 (the odd one)
+      const uint32_t vr = wsm_s + stage * SM::STAGE + SM::RAW;
+      const int mi = lane >> 3;
+      const int tok = (mi & 1) * 8 + (lane & 7);
+#pragma unroll
+      for (int cc2 = 0; cc2 < D / 32; cc2++) {
+        uint32_t w[4];
+        ldsm_x4_t(vr + swz_raw<D>(tok, 2 * cc2 + (mi >> 1)), w[0], w[1], w[2], w[3]);
+#pragma unroll
+        for (int cp = 0; cp < 2; cp++) {
+          const uint32_t ua = w[2 * cp] ^ 0x80808080u, ub = w[2 * cp + 1] ^ 0x80808080u;
+          const int nt = 2 * (2 * cc2 + cp);
+          const uint32_t e0 = i8pair_f16(ua, 0x4240), e1 = i8pair_f16(ub, 0x4240);
+          const uint32_t d0 = i8pair_f16(ua, 0x4341), d1 = i8pair_f16(ub, 0x4341);
+          mma_f16(o[nt], pa, e0, e1);
+          mma_f16(o[nt], pl, e0, e1);
+          mma_f16(o[nt + 1], pa, d0, d1);
+          mma_f16(o[nt + 1], pl, d0, d1);
+        }
+      }
+    } else {
     // P = P_hi + P_lo, both bf16 (P_lo = the rounding residue of P_hi), so
     // the two PV products carry P to ~2^-17 relative.
-    uint32_t pa[4], pl[4];
     split_bf16x2(pp[0][0], pp[0][1], pa[0], pl[0]);
     split_bf16x2(pp[0][2], pp[0][3], pa[1], pl[1]);
     split_bf16x2(pp[1][0], pp[1][1], pa[2], pl[2]);
@@ -335,6 +460,7 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
       mma_bf16(o[2 * dt2], pl, b0, b1);
       mma_bf16(o[2 * dt2 + 1], pl, b2, b3);
     }
+    }
     __syncwarp();
   }
   // row sums across the quad
@@ -348,13 +474,17 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
   float *mo = reinterpret_cast<float *>(smem);   // [WARPS][16][D]
   float *mm = mo + WARPS * 16 * D;               // [WARPS][16]
   float *ml = mm + WARPS * 16;                   // [WARPS][16]
+  // int8: n-tile dt holds columns 16 (dt / 2) + 4 q4 + (dt % 2) and +2, in
+  // units of 2^-kcur
+  const int oe = (INT8 && kcur != INT_MAX) ? -kcur : 0;
 #pragma unroll
   for (int dt = 0; dt < D / 8; dt++) {
-    const int d = dt * 8 + q4 * 2;
-    mo[((size_t)warp * 16 + g) * D + d] = o[dt][0];
-    mo[((size_t)warp * 16 + g) * D + d + 1] = o[dt][1];
-    mo[((size_t)warp * 16 + g + 8) * D + d] = o[dt][2];
-    mo[((size_t)warp * 16 + g + 8) * D + d + 1] = o[dt][3];
+    const int d = INT8 ? 16 * (dt >> 1) + 4 * q4 + (dt & 1) : dt * 8 + q4 * 2;
+    const int dd = INT8 ? 2 : 1;
+    mo[((size_t)warp * 16 + g) * D + d] = mul_pow2f(o[dt][0], oe);
+    mo[((size_t)warp * 16 + g) * D + d + dd] = mul_pow2f(o[dt][1], oe);
+    mo[((size_t)warp * 16 + g + 8) * D + d] = mul_pow2f(o[dt][2], oe);
+    mo[((size_t)warp * 16 + g + 8) * D + d + dd] = mul_pow2f(o[dt][3], oe);
   }
   if (q4 == 0) {
     mm[warp * 16 + g] = m0;
