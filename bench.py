@@ -19,7 +19,10 @@ scaling). Besides the headline the line carries:
                8 KV heads, ctx 1k/8k/32k, bf16 and int8 KV), heads split over
                the N ranks, GB/s against the HBM peak;
   flash        the causal flash-attention prefill configuration (B=4, H=32,
-               S=4096, d=128), TFLOP/s against the bf16 peak (N = 1);
+               S=4096, d=128), TFLOP/s against the bf16 peak, algorithmic
+               and as executed on the tensor pipe (N = 1);
+  prefill_gemm the K2 GEMM on the decoder's projection shapes at 2048 rows
+               (N = 1);
   gemv         the dequant-GEMV sweep (N = 1).
 --impl reference times the CPU oracle port of the reference path (rank 0).
 """
@@ -471,15 +474,38 @@ def main():
     tp = tp_parity(comm, ws)
     attn = decode_attn_sweep(ws, hbm, peak_src)
 
-    flash = None  # single-GPU configuration
+    flash = None  # single-GPU configurations
+    prefill_gemm = None
     if rank == 0 and ws == 1 and not args.no_flash:
         from vortex_b200 import kernel_bench as KB
         tfl, tsrc = measured_tflops()
         r = KB.flash_case(4, 32, 4096, True)
+        # the tensor pipe runs whole 128x128 tiles up to the diagonal and P.V
+        # twice (P as bf16 hi + lo): S, P_hi.V, P_lo.V per tile
+        nt = (4096 + 127) // 128
+        tiles = nt * (nt + 1) // 2
+        executed = 4 * 32 * tiles * 3 * 2 * 128 * 128 * 128
         flash = {"config": "B=4 H=32 S=4096 d=128 causal, q/k/v bf16 N(0,1), scale 1/sqrt(128)", "unit": "TFLOP/s",
                  "us": r["us"], "achieved": r["TFLOPs"], "peak": tfl, "peak_source": tsrc + " bf16 burst",
                  "frac": r["TFLOPs"] / tfl, "flops": r["flops"],
-                 "flops_formula": "4*B*H*d*S(S+1)/2 (visible score pairs only)"}
+                 "flops_formula": "4*B*H*d*S(S+1)/2 (visible score pairs only)",
+                 "tensor_executed_tflops": executed / (r["us"] * 1e-6) / 1e12,
+                 "tensor_frac_executed": executed / (r["us"] * 1e-6) / 1e12 / tfl,
+                 "executed_formula": "B*H*T*3*2*128^3, T = 528 causal 128x128 tiles per head (S, P_hi.V, P_lo.V)"}
+        # K2 prefill GEMM on the decoder's projection shapes (2048 prompt
+        # rows, Q4_0): the weights enter as two exact bf16 terms, so the
+        # tensor pipe runs twice the algorithmic FLOPs; the time includes the
+        # per-call weight expansion
+        gemm_rows = []
+        for n_, k_ in ((12288, 4096), (4096, 4096), (22016, 4096), (4096, 11008)):
+            g_ = KB.gemm_case("Q4_0", 2048, n_, k_, reps=5)
+            gemm_rows.append({"M": 2048, "N": n_, "K": k_, "us": round(g_["us"], 1),
+                              "achieved": round(g_["TFLOPs"], 1), "frac": round(g_["TFLOPs"] / tfl, 3),
+                              "tensor_frac_executed": round(2 * g_["TFLOPs"] / tfl, 3)})
+        prefill_gemm = {"config": "Y[2048, N] = X deq(W)^T, Q4_0 W ~ N(0, 0.02), X bf16 N(0, 1), f32 out",
+                        "unit": "TFLOP/s", "peak": tfl, "peak_source": tsrc + " bf16 burst",
+                        "flops_formula": "2*M*N*K (executed on the tensor pipe: twice, hi and lo weight terms)",
+                        "cases": gemm_rows}
 
     # dequant-GEMV sweep (weights 4096x4096, 11008x4096, 4096x11008; Q4_0 and
     # Q8_0; batch 1, 4, 16), each over rotating weight copies > 2x L2; one GPU
@@ -533,6 +559,7 @@ def main():
             "tp_parity": tp,
             "decode_attn": attn,
             "flash": flash,
+            "prefill_gemm": prefill_gemm,
             "gemv": gemv,
             "clocks": clocks,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
