@@ -11,12 +11,14 @@
 // bits. Each weight is split once per call into bf16 terms, t0 = bf16(w),
 // t1 = bf16(w - t0) (and t2 = bf16(w - t0 - t1) for Q8_0), whose sum is w
 // exactly. The GEMM then runs sum_t X * t^T into one f32 accumulator:
-//  * CTA tile 128 rows of X x 256 rows of W, k in stages of 64 (a 2-deep ring:
-//    X 16 KB + 32 KB per term per stage), loaded by TMA with 128-byte swizzle
-//    (no multicast);
-//  * one thread issues tcgen05.mma (M=128, N=256, K=16; bf16 -> f32), one per
-//    term and k16 step, into one of two TMEM partials (256 columns each, 4
-//    stages = 256 k per partial), and releases each stage with tcgen05.commit;
+//  * CTA tile 128 rows of X x 256 rows of W, k in blocks of 64; a stage is
+//    one (k block, term) pair, X 16 KB + the term's 32 KB, in a 4-deep ring,
+//    loaded by TMA with 128-byte swizzle (no multicast; X is read once per
+//    term, from L2);
+//  * one thread issues tcgen05.mma (M=128, N=256, K=16; bf16 -> f32), four per
+//    stage, into one of two TMEM partials (256 columns each, 4 k blocks =
+//    256 k per partial, every term), and releases each stage with
+//    tcgen05.commit;
 //  * eight epilogue warps (one output row and 128 columns per thread) add each partial
 //    (tcgen05.ld) to the row's f32 sums in registers with round-to-nearest
 //    adds, so the long K reduction keeps f32 accuracy (the tensor core's own
@@ -53,8 +55,10 @@ constexpr uint32_t TMEM_COLS = 2 * BN;        // two stage partials
 
 template <int TERMS>
 struct GemmGeo {
-  static constexpr int STAGE_BYTES = A_BYTES + TERMS * B_BYTES;
-  // ring depth: as many stages as fit (Q4_0: 4 x 48 KB, Q8_0: 3 x 64 KB)
+  // a stage is one (k block, weight term) pair: the X tile and one term's
+  // W tile, so the ring holds four stages whatever the term count (with all
+  // terms of a k block in one stage, 128x256 tiles left room for two)
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (227 * 1024 - 1024) / STAGE_BYTES;
   static constexpr int SMEM_ALLOC = STAGES * STAGE_BYTES + 1024;
 };
@@ -105,14 +109,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0) {
     // ---------------- TMA producer
     if (lane == 0) {
-      for (int kb = 0; kb < nk; kb++) {
-        const int st = kb % STAGES;
-        if (kb >= STAGES) wait_or_flag(&empty[st], ((kb / STAGES) - 1) & 1, a.err);
+      for (int it = 0; it < nk * TERMS; it++) {
+        const int kb = it / TERMS, t = it % TERMS;
+        const int st = it % STAGES;
+        if (it >= STAGES) wait_or_flag(&empty[st], ((it / STAGES) - 1) & 1, a.err);
         uint8_t *base = sm + st * STAGE_BYTES;
         mbar_expect_tx(&full[st], STAGE_BYTES);
         tma_load_2d(base, &tx, kb * BK, m0, &full[st]);
         // the terms are stacked [TERMS * N, K]: term t of rows n0.. at row t * N + n0
-        for (int t = 0; t < TERMS; t++) tma_load_2d(base + A_BYTES + t * B_BYTES, &tw, kb * BK, t * a.N + n0, &full[st]);
+        tma_load_2d(base + A_BYTES, &tw, kb * BK, t * a.N + n0, &full[st]);
       }
     }
     __syncwarp();
@@ -120,22 +125,20 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------- MMA issue: stage kb accumulates into TMEM partial kb % 2
     if (lane == 0) {
       constexpr uint32_t ID = idesc_bf16(BM, BN, false);
-      for (int kb = 0; kb < nk; kb++) {
-        const int st = kb % STAGES, grp = kb / DRAIN, pb = grp & 1;
-        const bool first = kb % DRAIN == 0, last = kb % DRAIN == DRAIN - 1 || kb == nk - 1;
-        wait_or_flag(&full[st], (kb / STAGES) & 1, a.err);
+      for (int it = 0; it < nk * TERMS; it++) {
+        const int kb = it / TERMS, u = it % TERMS;
+        const int st = it % STAGES, grp = kb / DRAIN, pb = grp & 1;
+        const bool first = kb % DRAIN == 0 && u == 0;
+        const bool last = (kb % DRAIN == DRAIN - 1 || kb == nk - 1) && u == TERMS - 1;
+        wait_or_flag(&full[st], (it / STAGES) & 1, a.err);
         if (first && grp >= 2) wait_or_flag(&pfree[pb], ((grp >> 1) - 1) & 1, a.err);
         tc_fence_after();
         const uint32_t sa = smem_u32(sm + st * STAGE_BYTES);
         const uint32_t td = tmem + pb * BN;
 #pragma unroll
-        for (int t = 0; t < BK / 16; t++) {
-          const uint64_t ad = sw128_desc(sa + t * 32, 16, 1024);
-#pragma unroll
-          for (int u = 0; u < TERMS; u++)
-            umma_bf16(td, ad, sw128_desc(sa + A_BYTES + u * B_BYTES + t * 32, 16, 1024), ID,
-                      (!first || t > 0 || u > 0) ? 1u : 0u);
-        }
+        for (int t = 0; t < BK / 16; t++)
+          umma_bf16(td, sw128_desc(sa + t * 32, 16, 1024), sw128_desc(sa + A_BYTES + t * 32, 16, 1024), ID,
+                    (!first || t > 0) ? 1u : 0u);
         umma_commit(&empty[st]);
         if (last) umma_commit(&pfull[pb]);
       }
