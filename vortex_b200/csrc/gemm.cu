@@ -19,6 +19,9 @@
 //    stage, into one of two TMEM partials (256 columns each, 4 k blocks =
 //    256 k per partial, every term), and releases each stage with
 //    tcgen05.commit;
+//  * persistent CTAs, one per SM, walk the tiles (the m blocks of an n block
+//    consecutively); the TMA and MMA warps run on into the next tile while
+//    the epilogue warps write the previous one;
 //  * eight epilogue warps (one output row and 128 columns per thread) add each partial
 //    (tcgen05.ld) to the row's f32 sums in registers with round-to-nearest
 //    adds, so the long K reduction keeps f32 accuracy (the tensor core's own
@@ -27,6 +30,7 @@
 //    residual.
 // Every mbarrier wait is bounded; a timeout sets the context's device error
 // word and the kernel runs to completion.
+#include <algorithm>
 #include <atomic>
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -82,8 +86,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], pfull[2], pfree[2];
   __shared__ uint32_t tmem_base_s;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
   const int nk = (a.K + BK - 1) / BK;
+  // persistent: tiles blockIdx.x, + gridDim.x, ...; the m blocks of one n
+  // block are consecutive (concurrent CTAs share W tiles in L2)
+  const int mt = (a.M + BM - 1) / BM, ntile = mt * ((a.N + BN - 1) / BN);
+  const int ngrp = (nk + DRAIN - 1) / DRAIN;  // TMEM partial groups per tile
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
@@ -109,15 +116,19 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0) {
     // ---------------- TMA producer
     if (lane == 0) {
-      for (int it = 0; it < nk * TERMS; it++) {
-        const int kb = it / TERMS, t = it % TERMS;
-        const int st = it % STAGES;
-        if (it >= STAGES) wait_or_flag(&empty[st], ((it / STAGES) - 1) & 1, a.err);
-        uint8_t *base = sm + st * STAGE_BYTES;
-        mbar_expect_tx(&full[st], STAGE_BYTES);
-        tma_load_2d(base, &tx, kb * BK, m0, &full[st]);
-        // the terms are stacked [TERMS * N, K]: term t of rows n0.. at row t * N + n0
-        tma_load_2d(base + A_BYTES, &tw, kb * BK, t * a.N + n0, &full[st]);
+      int ig = 0;  // stage count over all tiles of this CTA
+      for (int tile = blockIdx.x; tile < ntile; tile += gridDim.x) {
+        const int m0 = (tile % mt) * BM, n0 = (tile / mt) * BN;
+        for (int it = 0; it < nk * TERMS; it++, ig++) {
+          const int kb = it / TERMS, t = it % TERMS;
+          const int st = ig % STAGES;
+          if (ig >= STAGES) wait_or_flag(&empty[st], ((ig / STAGES) - 1) & 1, a.err);
+          uint8_t *base = sm + st * STAGE_BYTES;
+          mbar_expect_tx(&full[st], STAGE_BYTES);
+          tma_load_2d(base, &tx, kb * BK, m0, &full[st]);
+          // the terms are stacked [TERMS * N, K]: term t of rows n0.. at row t * N + n0
+          tma_load_2d(base + A_BYTES, &tw, kb * BK, t * a.N + n0, &full[st]);
+        }
       }
     }
     __syncwarp();
@@ -125,12 +136,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------- MMA issue: stage kb accumulates into TMEM partial kb % 2
     if (lane == 0) {
       constexpr uint32_t ID = idesc_bf16(BM, BN, false);
-      for (int it = 0; it < nk * TERMS; it++) {
+      int ig = 0, g0 = 0;  // stage and partial-group counts over all tiles of this CTA
+      for (int tile = blockIdx.x; tile < ntile; tile += gridDim.x, g0 += ngrp)
+      for (int it = 0; it < nk * TERMS; it++, ig++) {
         const int kb = it / TERMS, u = it % TERMS;
-        const int st = it % STAGES, grp = kb / DRAIN, pb = grp & 1;
+        const int st = ig % STAGES, grp = g0 + kb / DRAIN, pb = grp & 1;
         const bool first = kb % DRAIN == 0 && u == 0;
         const bool last = (kb % DRAIN == DRAIN - 1 || kb == nk - 1) && u == TERMS - 1;
-        wait_or_flag(&full[st], (it / STAGES) & 1, a.err);
+        wait_or_flag(&full[st], (ig / STAGES) & 1, a.err);
         if (first && grp >= 2) wait_or_flag(&pfree[pb], ((grp >> 1) - 1) & 1, a.err);
         tc_fence_after();
         const uint32_t sa = smem_u32(sm + st * STAGE_BYTES);
@@ -149,13 +162,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     // and columns [128 * half, 128 * half + 128) of the tile; each partial is
     // added in f32 (round to nearest) to the row's sums
     const int q = warp & 3, half = (warp - 2) >> 2;
+    int g0 = 0;  // partial-group count over all tiles of this CTA
+    for (int tile = blockIdx.x; tile < ntile; tile += gridDim.x, g0 += ngrp) {
+    const int m0 = (tile % mt) * BM, n0 = (tile / mt) * BN;
     const int row = m0 + q * 32 + lane;
     float acc[128];
 #pragma unroll
     for (int i = 0; i < 128; i++) acc[i] = 0.f;
-    const int ngrp = (nk + DRAIN - 1) / DRAIN;
-    for (int grp = 0; grp < ngrp; grp++) {
-      const int pb = grp & 1;
+    for (int gi = 0; gi < ngrp; gi++) {
+      const int grp = g0 + gi, pb = grp & 1;
       wait_or_flag(&pfull[pb], (grp >> 1) & 1, a.err);
       tc_fence_after();
 #pragma unroll
@@ -208,6 +223,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
+    }  // tile
   }
   tc_fence_before();
   __syncthreads();
@@ -348,7 +364,10 @@ int gemm_q_launch(vxb_ctx *ctx, int fmt, const void *d_tiled, int N, int K, cons
   a.N = N;
   a.K = K;
   a.y_dtype = y_dtype;
-  dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
+  // persistent CTAs, one per SM (the kernel holds an SM's shared memory)
+  const long long ntile = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int sms = ctx->num_sms > 0 ? ctx->num_sms : 148;
+  dim3 grid((unsigned)std::min<long long>(ntile, sms));
   if (terms == 2)
     gemm_terms_kernel<2><<<grid, THREADS, GemmGeo<2>::SMEM_ALLOC, st>>>(mx, mw, a);
   else
