@@ -297,6 +297,21 @@ int vxb_rmsnorm(vxb_ctx *ctx, const float *d_x, const float *d_w, const float *d
 int vxb_swiglu(vxb_ctx *ctx, const float *d_gu, int rows, int ffn, uint16_t *d_act, void *stream);
 /* argmax, stdlib/ai/transformer.vx:1163-1177 (first index of the maximum). */
 int vxb_argmax(vxb_ctx *ctx, const float *d_logits, int rows, int vocab, int32_t *d_out, void *stream);
+/* rope_embed, stdlib/ai/transformer.vx:442-466, on each of `rows` rows of f32
+ * d_x [rows, n]: adjacent pairs (x[2i], x[2i+1]) rotated by
+ * theta = d_pos[row] / exp(i * ln(10000) / dim) (d_pos int64 [rows]), an odd
+ * last element copied. Rotation in f64, rounded once to f32 into d_out
+ * [rows, n] (d_out may be d_x). dim <= 0 is VXB_EINVAL. */
+int vxb_rope(vxb_ctx *ctx, const float *d_x, int rows, int n, const int64_t *d_pos, int dim, float *d_out,
+             void *stream);
+/* the `rope` builtin, src/interpreter.rs:2368-2373: as vxb_rope with the angle
+ * of pair i given as d_angles[i] (f64 [n_angles], the same for every row) and
+ * 0 for i >= n_angles, as the builtin pads a short frequency list. */
+int vxb_rope_angles(vxb_ctx *ctx, const float *d_x, int rows, int n, const double *d_angles, int n_angles,
+                    float *d_out, void *stream);
+/* residual add, _vec_add stdlib/ai/transformer.vx:353-366: d_out = d_a + d_b,
+ * f32 [n] (d_out may be d_a or d_b). */
+int vxb_add(vxb_ctx *ctx, const float *d_a, const float *d_b, size_t n, float *d_out, void *stream);
 
 /* sample_top_p, stdlib/ai/transformer.vx:1179-1260 (with the file's series
  * _exp, 36-80), for each of `rows` rows of f32 logits [rows, vocab]:

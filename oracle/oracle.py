@@ -73,6 +73,8 @@ def lib():
             "vxo_paged_attention": (None, [_P, _P, _P, _SZ, _SZ, _P]),
             "vxo_rmsnorm_bias": (None, [_P, _P, _P, _SZ, ctypes.c_double, _P]),
             "vxo_rope_embed": (None, [_P, _SZ, ctypes.c_int64, ctypes.c_int64, _P]),
+            "vxo_rope_builtin": (None, [_P, _SZ, _P, _SZ, _P]),
+            "vxo_vec_add": (None, [_P, _P, _SZ, _P]),
             "vxo_silu": (ctypes.c_double, [ctypes.c_double]),
             "vxo_vx_exp": (ctypes.c_double, [ctypes.c_double]),
             "vxo_argmax": (ctypes.c_int64, [_P, _SZ]),
@@ -353,6 +355,21 @@ def rope_embed(x, pos: int, dim: int) -> np.ndarray:
     x = _f64(x)
     out = np.zeros(x.size)
     lib().vxo_rope_embed(_p(x), x.size, int(pos), int(dim), _p(out))
+    return out
+
+
+def rope_builtin(x, freqs) -> np.ndarray:
+    x, freqs = _f64(x), _f64(freqs)
+    out = np.zeros(x.size)
+    lib().vxo_rope_builtin(_p(x), x.size, _p(freqs), freqs.size, _p(out))
+    return out
+
+
+def vec_add(a, b) -> np.ndarray:
+    a, b = _f64(a), _f64(b)
+    assert a.size == b.size
+    out = np.zeros(a.size)
+    lib().vxo_vec_add(_p(a), _p(b), a.size, _p(out))
     return out
 
 

@@ -654,6 +654,24 @@ void vxo_rope_embed(const double *x, size_t n, int64_t pos, int64_t dim, double 
     }
 }
 
+/* the `rope` builtin, src/interpreter.rs:2368-2373: pair i of x
+ * (x[2i], x[2i+1]) rotated by the angle freqs[i], or by 0 for
+ * i >= n_freqs; an odd tail passes through. */
+void vxo_rope_builtin(const double *x, size_t n, const double *freqs, size_t n_freqs, double *out) {
+    for (size_t i = 0; i < n; i++) out[i] = x[i];
+    for (size_t i = 0; i < n / 2; i++) {
+        double f = i < n_freqs ? freqs[i] : 0.0;
+        double s = sin(f), c = cos(f);
+        out[2 * i] = x[2 * i] * c - x[2 * i + 1] * s;
+        out[2 * i + 1] = x[2 * i] * s + x[2 * i + 1] * c;
+    }
+}
+
+/* _vec_add, stdlib/ai/transformer.vx:353-366 (the residual add). */
+void vxo_vec_add(const double *a, const double *b, size_t n, double *out) {
+    for (size_t i = 0; i < n; i++) out[i] = a[i] + b[i];
+}
+
 /* _silu, stdlib/ai/transformer.vx:176-182 */
 double vxo_silu(double x) { return x * (1.0 / (1.0 + exp(0.0 - x))); }
 

@@ -103,6 +103,8 @@ void vxo_paged_attention(const double *query, const double *keys, const double *
 void vxo_rmsnorm_bias(const double *x, const double *w, const double *b, size_t n, double eps,
                       double *out);
 void vxo_rope_embed(const double *x, size_t n, int64_t pos, int64_t dim, double *out);
+void vxo_rope_builtin(const double *x, size_t n, const double *freqs, size_t n_freqs, double *out);
+void vxo_vec_add(const double *a, const double *b, size_t n, double *out);
 double vxo_silu(double x);
 void vxo_matvec(const double *w, const double *v, size_t out_dim, size_t in_dim, double *out);
 

@@ -336,6 +336,19 @@ def test_tf_positional_encoding_kat():
     assert np.all(pe >= -1 - 1e-6) and np.all(pe <= 1 + 1e-6)
 
 
+def test_rope_and_add_kats():
+    # position 0 turns every pair by 0 (stdlib/ai/tensor_ops.vx:1007-1014)
+    x = np.array([1.0, 0.0, 1.0, 0.0, 3.0])
+    assert np.array_equal(O.rope_embed(x, 0, 4), x)
+    # pair 0 at position 1 turns by exactly 1 radian, pair 1 by 1/10000^(1/4) (dim 4)
+    y = O.rope_embed(np.array([1.0, 0.0, 1.0, 0.0]), 1, 4)
+    assert np.allclose(y, [np.cos(1.0), np.sin(1.0), np.cos(0.1), np.sin(0.1)], rtol=0, atol=1e-15)
+    # the builtin turns pair i by freqs[i] and leaves pairs past the list alone
+    z = O.rope_builtin(np.array([1.0, 0.0, 2.0, 5.0, 7.0]), np.array([np.pi / 2]))
+    assert np.allclose(z, [0.0, 1.0, 2.0, 5.0, 7.0], rtol=0, atol=1e-15)
+    assert np.array_equal(O.vec_add([1.0, -2.5], [0.5, 2.5]), [1.5, 0.0])
+
+
 def test_tf_layer_norm_kat():
     x = np.array([[1, 2, 3, 4], [5, 6, 7, 8]], np.float32)  # test_layer_norm
     y = O.tf_layernorm(x, np.ones(4, np.float32), np.zeros(4, np.float32))

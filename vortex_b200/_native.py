@@ -94,6 +94,9 @@ SIGNATURES = {
     "vxb_rmsnorm": (_I, [_P, _P, _P, _P, _I, _I, ctypes.c_float, _P, _P]),
     "vxb_swiglu": (_I, [_P, _P, _I, _I, _P, _P]),
     "vxb_argmax": (_I, [_P, _P, _I, _I, _P, _P]),
+    "vxb_rope": (_I, [_P, _P, _I, _I, _P, _I, _P, _P]),
+    "vxb_rope_angles": (_I, [_P, _P, _I, _I, _P, _I, _P, _P]),
+    "vxb_add": (_I, [_P, _P, _P, _SZ, _P, _P]),
     "vxb_sample_top_p": (_I, [_P, _P, _I, _I, ctypes.c_double, ctypes.c_double, _P, _P, _P]),
     "vxb_batcher_create": (_I, [_I, ctypes.POINTER(_P)]),
     "vxb_batcher_destroy": (_I, [_P]),

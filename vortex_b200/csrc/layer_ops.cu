@@ -17,6 +17,8 @@
 // before a later kernel rewrote them.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "layer_ops.h"
 
 using namespace vxb;
@@ -376,6 +378,51 @@ __global__ void unshard_kernel(const float *__restrict__ in, int tp, int rows, i
   out[i] = in[((size_t)t * rows + r) * shard + c];
 }
 
+// Standalone RoPE of f32 rows: one thread per adjacent pair (x[2i], x[2i+1])
+// of a row, an odd last element copied. The angle is
+// pos[row] / exp(i * ln(10000) / dim) (rope_embed,
+// stdlib/ai/transformer.vx:442-466) when by_angle is 0, else angles[i], and
+// 0 for i >= n_angles (the `rope` builtin, src/interpreter.rs:2368-2373). The
+// rotation is evaluated in f64 and rounded to f32 once. out may equal x: each
+// element is read and written by the same thread.
+__global__ void rope_rows_kernel(const float *x, const int64_t *__restrict__ pos, int dim, int by_angle,
+                                 const double *__restrict__ angles, int n_angles, int rows, int n, float *out) {
+  const size_t half = (size_t)(n + 1) / 2, total = (size_t)rows * half;
+  const double ln_base = log(10000.0);
+  for (size_t g = (size_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = g / half, i = g % half;
+    const float *xr = x + r * n;
+    float *orow = out + r * n;
+    if (2 * i + 1 == (size_t)n) {
+      orow[2 * i] = xr[2 * i];
+      continue;
+    }
+    const double theta = by_angle ? (i < (size_t)n_angles ? angles[i] : 0.0)
+                                : (double)pos[r] / exp((double)i * ln_base / (double)dim);
+    double s, c;
+    sincos(theta, &s, &c);
+    const double x0 = xr[2 * i], x1 = xr[2 * i + 1];
+    orow[2 * i] = (float)(x0 * c - x1 * s);
+    orow[2 * i + 1] = (float)(x0 * s + x1 * c);
+  }
+}
+
+// Residual add (_vec_add, stdlib/ai/transformer.vx:353-366): out = a + b in
+// f32, 16-byte accesses when all three pointers allow them. out may equal a
+// or b.
+__global__ void add_kernel(const float *a, const float *b, size_t n, float *out) {
+  const bool vec = ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                     reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  const size_t n4 = vec ? n / 4 : 0, stride = (size_t)gridDim.x * blockDim.x;
+  const size_t t0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (size_t i = t0; i < n4; i += stride) {
+    const float4 va = __ldcs(reinterpret_cast<const float4 *>(a) + i);
+    const float4 vb = __ldcs(reinterpret_cast<const float4 *>(b) + i);
+    __stcs(reinterpret_cast<float4 *>(out) + i, make_float4(va.x + vb.x, va.y + vb.y, va.z + vb.z, va.w + vb.w));
+  }
+  for (size_t i = 4 * n4 + t0; i < n; i += stride) out[i] = a[i] + b[i];
+}
+
 template <typename... Args>
 int launch_pdl(vxb_ctx *ctx, void (*kfn)(Args...), dim3 grid, dim3 block, cudaStream_t st, const char *what,
                Args... args) {
@@ -504,6 +551,39 @@ VXB_API int vxb_swiglu(vxb_ctx *ctx, const float *d_gu, int rows, int ffn, uint1
   if (!ctx || !d_gu || !d_act || rows <= 0 || ffn <= 0) return set_error(ctx, VXB_EINVAL, "vxb_swiglu: bad arguments");
   if (int rc = use_device(ctx)) return rc;
   return swiglu_launch(ctx, d_gu, rows, ffn, d_act, (cudaStream_t)stream);
+}
+
+static int rope_rows(vxb_ctx *ctx, const float *d_x, int rows, int n, const int64_t *d_pos, int dim, int by_angle,
+                     const double *d_angles, int n_angles, float *d_out, cudaStream_t st) {
+  if (int rc = use_device(ctx)) return rc;
+  const size_t total = (size_t)rows * ((size_t)(n + 1) / 2);
+  const size_t cap = (size_t)(ctx->num_sms > 0 ? ctx->num_sms : 148) * 8;
+  const unsigned grid = (unsigned)std::max<size_t>(1, std::min((total + 255) / 256, cap));
+  rope_rows_kernel<<<grid, 256, 0, st>>>(d_x, d_pos, dim, by_angle, d_angles, n_angles, rows, n, d_out);
+  return launch_check(ctx, "rope_rows_kernel");
+}
+
+VXB_API int vxb_rope(vxb_ctx *ctx, const float *d_x, int rows, int n, const int64_t *d_pos, int dim, float *d_out,
+                     void *stream) {
+  if (!ctx || !d_x || !d_pos || !d_out || rows <= 0 || n <= 0 || dim <= 0)
+    return set_error(ctx, VXB_EINVAL, "vxb_rope: bad arguments");
+  return rope_rows(ctx, d_x, rows, n, d_pos, dim, 0, nullptr, 0, d_out, (cudaStream_t)stream);
+}
+
+VXB_API int vxb_rope_angles(vxb_ctx *ctx, const float *d_x, int rows, int n, const double *d_angles, int n_angles,
+                            float *d_out, void *stream) {
+  if (!ctx || !d_x || !d_out || rows <= 0 || n <= 0 || n_angles < 0 || (n_angles > 0 && !d_angles))
+    return set_error(ctx, VXB_EINVAL, "vxb_rope_angles: bad arguments");
+  return rope_rows(ctx, d_x, rows, n, nullptr, 1, 1, d_angles, n_angles, d_out, (cudaStream_t)stream);
+}
+
+VXB_API int vxb_add(vxb_ctx *ctx, const float *d_a, const float *d_b, size_t n, float *d_out, void *stream) {
+  if (!ctx || !d_a || !d_b || !d_out || n == 0) return set_error(ctx, VXB_EINVAL, "vxb_add: bad arguments");
+  if (int rc = use_device(ctx)) return rc;
+  const size_t cap = (size_t)(ctx->num_sms > 0 ? ctx->num_sms : 148) * 8;
+  const unsigned grid = (unsigned)std::max<size_t>(1, std::min((n / 4 + 255) / 256, cap));
+  add_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(d_a, d_b, n, d_out);
+  return launch_check(ctx, "add_kernel");
 }
 
 VXB_API int vxb_argmax(vxb_ctx *ctx, const float *d_logits, int rows, int vocab, int32_t *d_out, void *stream) {
