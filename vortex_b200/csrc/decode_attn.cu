@@ -398,14 +398,18 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
     }
     l0 = l0 * c0 + (pp[0][0] + pp[0][1] + pp[1][0] + pp[1][1]);
     l1 = l1 * c1 + (pp[0][2] + pp[0][3] + pp[1][2] + pp[1][3]);
-    // O's correction (int8: times 2^(kp - k) when this page lowered k)
+    // O's correction (int8: times 2^(kp - k) when this page lowered k),
+    // skipped by the whole warp when no row's maximum moved (most pages after
+    // the first few: the factor is exactly 1)
     const float oc0 = c0 * kfac, oc1 = c1 * kfac;
+    if (__any_sync(0xffffffffu, oc0 != 1.f || oc1 != 1.f)) {
 #pragma unroll
-    for (int dt = 0; dt < D / 8; dt++) {
-      o[dt][0] *= oc0;
-      o[dt][1] *= oc0;
-      o[dt][2] *= oc1;
-      o[dt][3] *= oc1;
+      for (int dt = 0; dt < D / 8; dt++) {
+        o[dt][0] *= oc0;
+        o[dt][1] *= oc0;
+        o[dt][2] *= oc1;
+        o[dt][3] *= oc1;
+      }
     }
     uint32_t pa[4], pl[4];
     if constexpr (INT8) {
