@@ -140,6 +140,14 @@ __device__ __forceinline__ uint32_t i8pair_f16(uint32_t w_xor80, uint32_t sel) {
   return hsub2_u(__byte_perm(w_xor80, 0x64646464u, sel), 0x64806480u);
 }
 
+// 2^x, the special-function unit's approximation (flushes results below
+// 2^-126 to zero; -inf gives 0)
+__device__ __forceinline__ float ex2a(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // v * 2^e for |e| <= 252 (two exact power-of-two factors)
 __device__ __forceinline__ float mul_pow2f(float v, int e) {
   const int e1 = e / 2, e2 = e - e1;
@@ -267,12 +275,21 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
     if (!INT8) {
       const uint16_t *kp = reinterpret_cast<const uint16_t *>(a.pool_k) + base * D;
       const uint16_t *vp = reinterpret_cast<const uint16_t *>(a.pool_v) + base * D;
+      if (tok0 + PAGE <= len) {
 #pragma unroll
-      for (int c = lane; c < PAGE * CHUNKS; c += 32) {
-        const int r = c / CHUNKS, cc = c % CHUNKS;
-        const int bytes = tok0 + r < len ? 16 : 0;
-        cp_async16(st_s + swz<D>(r, cc), kp + (size_t)r * D + cc * 8, bytes);
-        cp_async16(st_s + SM::TILE + swz<D>(r, cc), vp + (size_t)r * D + cc * 8, bytes);
+        for (int c = lane; c < PAGE * CHUNKS; c += 32) {
+          const int r = c / CHUNKS, cc = c % CHUNKS;
+          cp_async16(st_s + swz<D>(r, cc), kp + (size_t)r * D + cc * 8, 16);
+          cp_async16(st_s + SM::TILE + swz<D>(r, cc), vp + (size_t)r * D + cc * 8, 16);
+        }
+      } else {
+#pragma unroll
+        for (int c = lane; c < PAGE * CHUNKS; c += 32) {
+          const int r = c / CHUNKS, cc = c % CHUNKS;
+          const int bytes = tok0 + r < len ? 16 : 0;
+          cp_async16(st_s + swz<D>(r, cc), kp + (size_t)r * D + cc * 8, bytes);
+          cp_async16(st_s + SM::TILE + swz<D>(r, cc), vp + (size_t)r * D + cc * 8, bytes);
+        }
       }
     } else {
       const int8_t *kp = reinterpret_cast<const int8_t *>(a.pool_k) + base * D;
@@ -367,16 +384,23 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
         mma_bf16(s[1], qa[ks], b2, b3);
       }
     }
-    // scale, mask, online softmax
+    // scale, mask (pages inside the sequence need none), online softmax
+    const bool full = tok0 + PAGE <= len;
 #pragma unroll
     for (int nt = 0; nt < 2; nt++)
 #pragma unroll
       for (int e = 0; e < 4; e++) {
-        const int tok = tok0 + nt * 8 + q4 * 2 + (e & 1);
         float v = s[nt][e] * (e < 2 ? rs0 : rs1);
         if (INT8) v *= ksc[nt][e & 1];
-        s[nt][e] = tok < len ? v : -INFINITY;
+        s[nt][e] = v;
       }
+    if (!full) {
+#pragma unroll
+      for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+          if (tok0 + nt * 8 + q4 * 2 + (e & 1) >= len) s[nt][e] = -INFINITY;
+    }
     float mx0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
     float mx1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
@@ -384,17 +408,17 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
     const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    const float c0 = mn0 == -INFINITY ? 1.f : exp2f(m0 - mn0);
-    const float c1 = mn1 == -INFINITY ? 1.f : exp2f(m1 - mn1);
+    const float c0 = mn0 == -INFINITY ? 1.f : ex2a(m0 - mn0);
+    const float c1 = mn1 == -INFINITY ? 1.f : ex2a(m1 - mn1);
     m0 = mn0;
     m1 = mn1;
     float pp[2][4];
 #pragma unroll
     for (int nt = 0; nt < 2; nt++) {
-      pp[nt][0] = mn0 == -INFINITY ? 0.f : exp2f(s[nt][0] - mn0);
-      pp[nt][1] = mn0 == -INFINITY ? 0.f : exp2f(s[nt][1] - mn0);
-      pp[nt][2] = mn1 == -INFINITY ? 0.f : exp2f(s[nt][2] - mn1);
-      pp[nt][3] = mn1 == -INFINITY ? 0.f : exp2f(s[nt][3] - mn1);
+      pp[nt][0] = mn0 == -INFINITY ? 0.f : ex2a(s[nt][0] - mn0);
+      pp[nt][1] = mn0 == -INFINITY ? 0.f : ex2a(s[nt][1] - mn0);
+      pp[nt][2] = mn1 == -INFINITY ? 0.f : ex2a(s[nt][2] - mn1);
+      pp[nt][3] = mn1 == -INFINITY ? 0.f : ex2a(s[nt][3] - mn1);
     }
     l0 = l0 * c0 + (pp[0][0] + pp[0][1] + pp[1][0] + pp[1][1]);
     l1 = l1 * c1 + (pp[0][2] + pp[0][3] + pp[1][2] + pp[1][3]);
