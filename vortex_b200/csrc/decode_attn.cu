@@ -65,6 +65,12 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, int by
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes));
 }
 
+// 16-byte copy at compile-time offsets from a shared and a global base
+template <int SOFF, int GOFF>
+__device__ __forceinline__ void cp_async16_at(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0+%2], [%1+%3], 16;" ::"r"(dst), "l"(src), "n"(SOFF), "n"(GOFF));
+}
+
 __device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, int bytes) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(bytes));
 }
@@ -264,6 +270,15 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
   const int npages = pg1 - pg0;
   const int my = npages > warp ? (npages - warp + WARPS - 1) / WARPS : 0;
 
+  // d = 128, whole pages: lane L copies, for i = 0..7, physical 16-byte chunk
+  // L % 16 of token row 2i + L / 16, i.e. the logical chunk that the swizzle
+  // puts there; the shared offsets step by 512 bytes, the global ones repeat
+  // every four rows, so each copy is a base register plus an immediate
+  const int cr0 = lane >> 4, cpc = lane & 15;
+  const uint32_t c_soff = (uint32_t)(cr0 * 256 + cpc * 16);
+  int c_goff[4];
+#pragma unroll
+  for (int k = 0; k < 4; k++) c_goff[k] = cr0 * 256 + ((cpc ^ ((2 * k + cr0) & 7)) << 4) + k * 512;
   auto prefetch = [&](int j, int stage) {
     const int p = pg0 + warp + j * WARPS;
     const int tok0 = p * PAGE;
@@ -275,7 +290,28 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
     if (!INT8) {
       const uint16_t *kp = reinterpret_cast<const uint16_t *>(a.pool_k) + base * D;
       const uint16_t *vp = reinterpret_cast<const uint16_t *>(a.pool_v) + base * D;
-      if (tok0 + PAGE <= len) {
+      if (D == 128 && tok0 + PAGE <= len) {
+        const char *kb = reinterpret_cast<const char *>(kp), *vb = reinterpret_cast<const char *>(vp);
+        const char *k0 = kb + c_goff[0], *k1 = kb + c_goff[1], *k2 = kb + c_goff[2], *k3 = kb + c_goff[3];
+        const char *v0 = vb + c_goff[0], *v1 = vb + c_goff[1], *v2 = vb + c_goff[2], *v3 = vb + c_goff[3];
+        const uint32_t ks = st_s + c_soff, vs = st_s + SM::TILE + c_soff;
+        cp_async16_at<0 * 512, 0>(ks, k0);
+        cp_async16_at<1 * 512, 0>(ks, k1);
+        cp_async16_at<2 * 512, 0>(ks, k2);
+        cp_async16_at<3 * 512, 0>(ks, k3);
+        cp_async16_at<4 * 512, 2048>(ks, k0);
+        cp_async16_at<5 * 512, 2048>(ks, k1);
+        cp_async16_at<6 * 512, 2048>(ks, k2);
+        cp_async16_at<7 * 512, 2048>(ks, k3);
+        cp_async16_at<0 * 512, 0>(vs, v0);
+        cp_async16_at<1 * 512, 0>(vs, v1);
+        cp_async16_at<2 * 512, 0>(vs, v2);
+        cp_async16_at<3 * 512, 0>(vs, v3);
+        cp_async16_at<4 * 512, 2048>(vs, v0);
+        cp_async16_at<5 * 512, 2048>(vs, v1);
+        cp_async16_at<6 * 512, 2048>(vs, v2);
+        cp_async16_at<7 * 512, 2048>(vs, v3);
+      } else if (tok0 + PAGE <= len) {
 #pragma unroll
         for (int c = lane; c < PAGE * CHUNKS; c += 32) {
           const int r = c / CHUNKS, cc = c % CHUNKS;
