@@ -420,16 +420,21 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
         mma_bf16(s[1], qa[ks], b2, b3);
       }
     }
-    // scale, mask (pages inside the sequence need none), online softmax
+    // scale, mask (pages inside the sequence need none), online softmax.
+    // bf16 with a positive scale: the scale enters the exponent's FMA (the
+    // row maximum of s * rs is rs times the maximum of s)
     const bool full = tok0 + PAGE <= len;
+    const bool fold = !INT8 && rs0 > 0.f && rs1 > 0.f;
+    if (!fold) {
 #pragma unroll
-    for (int nt = 0; nt < 2; nt++)
+      for (int nt = 0; nt < 2; nt++)
 #pragma unroll
-      for (int e = 0; e < 4; e++) {
-        float v = s[nt][e] * (e < 2 ? rs0 : rs1);
-        if (INT8) v *= ksc[nt][e & 1];
-        s[nt][e] = v;
-      }
+        for (int e = 0; e < 4; e++) {
+          float v = s[nt][e] * (e < 2 ? rs0 : rs1);
+          if (INT8) v *= ksc[nt][e & 1];
+          s[nt][e] = v;
+        }
+    }
     if (!full) {
 #pragma unroll
       for (int nt = 0; nt < 2; nt++)
@@ -443,18 +448,34 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    if (fold) {
+      mx0 *= rs0;
+      mx1 *= rs1;
+    }
     const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
     const float c0 = mn0 == -INFINITY ? 1.f : ex2a(m0 - mn0);
     const float c1 = mn1 == -INFINITY ? 1.f : ex2a(m1 - mn1);
     m0 = mn0;
     m1 = mn1;
     float pp[2][4];
+    const float f0 = fold ? rs0 : 1.f, f1 = fold ? rs1 : 1.f;
+    if (__all_sync(0xffffffffu, mn0 != -INFINITY && mn1 != -INFINITY)) {
 #pragma unroll
-    for (int nt = 0; nt < 2; nt++) {
-      pp[nt][0] = mn0 == -INFINITY ? 0.f : ex2a(s[nt][0] - mn0);
-      pp[nt][1] = mn0 == -INFINITY ? 0.f : ex2a(s[nt][1] - mn0);
-      pp[nt][2] = mn1 == -INFINITY ? 0.f : ex2a(s[nt][2] - mn1);
-      pp[nt][3] = mn1 == -INFINITY ? 0.f : ex2a(s[nt][3] - mn1);
+      for (int nt = 0; nt < 2; nt++) {
+        pp[nt][0] = ex2a(fmaf(s[nt][0], f0, -mn0));
+        pp[nt][1] = ex2a(fmaf(s[nt][1], f0, -mn0));
+        pp[nt][2] = ex2a(fmaf(s[nt][2], f1, -mn1));
+        pp[nt][3] = ex2a(fmaf(s[nt][3], f1, -mn1));
+      }
+    } else {
+      // rows with no visible token yet (max -inf) get P = 0
+#pragma unroll
+      for (int nt = 0; nt < 2; nt++) {
+        pp[nt][0] = mn0 == -INFINITY ? 0.f : ex2a(fmaf(s[nt][0], f0, -mn0));
+        pp[nt][1] = mn0 == -INFINITY ? 0.f : ex2a(fmaf(s[nt][1], f0, -mn0));
+        pp[nt][2] = mn1 == -INFINITY ? 0.f : ex2a(fmaf(s[nt][2], f1, -mn1));
+        pp[nt][3] = mn1 == -INFINITY ? 0.f : ex2a(fmaf(s[nt][3], f1, -mn1));
+      }
     }
     l0 = l0 * c0 + (pp[0][0] + pp[0][1] + pp[1][0] + pp[1][1]);
     l1 = l1 * c1 + (pp[0][2] + pp[0][3] + pp[1][2] + pp[1][3]);
