@@ -561,24 +561,36 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
   float *ml = mm + WARPS * 16;                   // [WARPS][16]
   // int8: n-tile dt holds columns 16 (dt / 2) + 4 q4 + (dt % 2) and +2, in
   // units of 2^-kcur
+  // only the G live rows (the query heads of the group) are merged
+  const int G = a.G;
   const int oe = (INT8 && kcur != INT_MAX) ? -kcur : 0;
+  if (g < G) {
 #pragma unroll
-  for (int dt = 0; dt < D / 8; dt++) {
-    const int d = INT8 ? 16 * (dt >> 1) + 4 * q4 + (dt & 1) : dt * 8 + q4 * 2;
-    const int dd = INT8 ? 2 : 1;
-    mo[((size_t)warp * 16 + g) * D + d] = mul_pow2f(o[dt][0], oe);
-    mo[((size_t)warp * 16 + g) * D + d + dd] = mul_pow2f(o[dt][1], oe);
-    mo[((size_t)warp * 16 + g + 8) * D + d] = mul_pow2f(o[dt][2], oe);
-    mo[((size_t)warp * 16 + g + 8) * D + d + dd] = mul_pow2f(o[dt][3], oe);
+    for (int dt = 0; dt < D / 8; dt++) {
+      const int d = INT8 ? 16 * (dt >> 1) + 4 * q4 + (dt & 1) : dt * 8 + q4 * 2;
+      const int dd = INT8 ? 2 : 1;
+      mo[((size_t)warp * 16 + g) * D + d] = INT8 ? mul_pow2f(o[dt][0], oe) : o[dt][0];
+      mo[((size_t)warp * 16 + g) * D + d + dd] = INT8 ? mul_pow2f(o[dt][1], oe) : o[dt][1];
+    }
+    if (q4 == 0) {
+      mm[warp * 16 + g] = m0;
+      ml[warp * 16 + g] = l0;
+    }
   }
-  if (q4 == 0) {
-    mm[warp * 16 + g] = m0;
-    mm[warp * 16 + g + 8] = m1;
-    ml[warp * 16 + g] = l0;
-    ml[warp * 16 + g + 8] = l1;
+  if (g + 8 < G) {
+#pragma unroll
+    for (int dt = 0; dt < D / 8; dt++) {
+      const int d = INT8 ? 16 * (dt >> 1) + 4 * q4 + (dt & 1) : dt * 8 + q4 * 2;
+      const int dd = INT8 ? 2 : 1;
+      mo[((size_t)warp * 16 + g + 8) * D + d] = INT8 ? mul_pow2f(o[dt][2], oe) : o[dt][2];
+      mo[((size_t)warp * 16 + g + 8) * D + d + dd] = INT8 ? mul_pow2f(o[dt][3], oe) : o[dt][3];
+    }
+    if (q4 == 0) {
+      mm[warp * 16 + g + 8] = m1;
+      ml[warp * 16 + g + 8] = l1;
+    }
   }
   __syncthreads();
-  const int G = a.G;
   const size_t grp = (size_t)i * a.Hkv + h;
   const float LN2 = 0.69314718055994530942f;
   for (int e = threadIdx.x; e < G * D; e += THREADS) {
