@@ -162,6 +162,15 @@ def test_decode_attention_ragged(KV, dtype_name, Hq, H, D):
 
 
 @pytest.mark.parametrize("dtype_name", ["BF16", "I8"])
+def test_decode_attention_block_size_32(KV, dtype_name):
+    """Cache blocks of 32 tokens: each block holds two 16-token pages."""
+    dtype = getattr(KV, dtype_name)
+    lens = [1, 31, 32, 33, 100, 0, 257]
+    c, keys, vals = _fill(KV, lens, 8, 128, dtype, bs=32, seed=5)
+    _check(KV, c, keys, vals, lens, 32, 8, 128)
+
+
+@pytest.mark.parametrize("dtype_name", ["BF16", "I8"])
 @pytest.mark.parametrize("ctx", [1024, 8192])
 def test_decode_attention_c4_shapes(KV, dtype_name, ctx):
     """Decode attention config: batch 32, 32 q heads / 8 kv heads, d 128."""

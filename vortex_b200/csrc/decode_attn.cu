@@ -282,8 +282,9 @@ __global__ void __launch_bounds__(THREADS) decode_attn_kernel(const DecodeArgs a
   auto prefetch = [&](int j, int stage) {
     const int p = pg0 + warp + j * WARPS;
     const int tok0 = p * PAGE;
-    const int block = __ldcg(table + tok0 / a.bs);
-    const int off = tok0 % a.bs;
+    // blocks of one page (the usual 16 tokens) need no division
+    const int block = __ldcg(table + (a.bs == PAGE ? p : tok0 / a.bs));
+    const int off = a.bs == PAGE ? 0 : tok0 % a.bs;
     const size_t base = ((size_t)block * a.Hkv + h) * a.bs + off;  // token row index in pool
     uint8_t *st = wsm + stage * SM::STAGE;
     const uint32_t st_s = wsm_s + stage * SM::STAGE;
