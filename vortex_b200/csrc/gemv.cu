@@ -535,9 +535,10 @@ __device__ __forceinline__ void stream_consume(const StreamArgs &a, const uint8_
   const uint16_t *xl = xs + (BAT ? (lane >> 2) * a.xs_stride : 0) + (lane & 3) * 4;
   constexpr int BLK = CS * G::BPC;  // blocks per stage
   constexpr int GB = 4;             // blocks per group of independent accumulators
+  int slot = 0;      // it % ring, kept without a division
+  uint32_t ph = 0u;  // (it / ring) & 1
   for (int it = 0; it < n_iter; it++) {
-    const int slot = it % a.ring;
-    if (!mbar_wait(&full[slot], (it / a.ring) & 1)) atomicExch(a.err, 1);
+    if (!mbar_wait(&full[slot], ph)) atomicExch(a.err, 1);
     const uint8_t *st = ring + slot * STB;
     uint4 wv[CS];
     uint32_t sv[CS][G::BPC];
@@ -559,6 +560,10 @@ __device__ __forceinline__ void stream_consume(const StreamArgs &a, const uint8_
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_expect_tx(&full[slot], STB);
       bulk_g2s(ring + slot * STB, src + (size_t)(it + a.ring) * STB, STB, &full[slot]);
+    }
+    if (++slot == a.ring) {
+      slot = 0;
+      ph ^= 1u;
     }
     const uint16_t *xk = xl + it * CS * G::CH;
 #pragma unroll
