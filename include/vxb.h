@@ -301,7 +301,8 @@ int vxb_argmax(vxb_ctx *ctx, const float *d_logits, int rows, int vocab, int32_t
  * d_x [rows, n]: adjacent pairs (x[2i], x[2i+1]) rotated by
  * theta = d_pos[row] / exp(i * ln(10000) / dim) (d_pos int64 [rows]), an odd
  * last element copied. Rotation in f64, rounded once to f32 into d_out
- * [rows, n] (d_out may be d_x). dim <= 0 is VXB_EINVAL. */
+ * [rows, n] (d_out may be d_x). dim <= 0 is VXB_EINVAL; rows or n of 0 is
+ * an empty result (VXB_OK, nothing read or written). */
 int vxb_rope(vxb_ctx *ctx, const float *d_x, int rows, int n, const int64_t *d_pos, int dim, float *d_out,
              void *stream);
 /* the `rope` builtin, src/interpreter.rs:2368-2373: as vxb_rope with the angle
@@ -310,7 +311,7 @@ int vxb_rope(vxb_ctx *ctx, const float *d_x, int rows, int n, const int64_t *d_p
 int vxb_rope_angles(vxb_ctx *ctx, const float *d_x, int rows, int n, const double *d_angles, int n_angles,
                     float *d_out, void *stream);
 /* residual add, _vec_add stdlib/ai/transformer.vx:353-366: d_out = d_a + d_b,
- * f32 [n] (d_out may be d_a or d_b). */
+ * f32 [n] (d_out may be d_a or d_b); n = 0 is an empty result (VXB_OK). */
 int vxb_add(vxb_ctx *ctx, const float *d_a, const float *d_b, size_t n, float *d_out, void *stream);
 
 /* sample_top_p, stdlib/ai/transformer.vx:1179-1260 (with the file's series

@@ -115,6 +115,16 @@ def test_swiglu_matches_oracle(B, rows, ffn):
         assert rel_err(y[r], ref[r]) <= 1e-2
 
 
+def test_empty_inputs_give_empty_outputs(B):
+    """rope_embed / _vec_add of empty vectors are empty in the reference."""
+    e = torch.zeros(0, 8, device="cuda")
+    assert B.rope_embed(e, 3, 8).shape == (0, 8)
+    assert B.rope(e, [0.5]).shape == (0, 8)
+    z = torch.zeros(0, device="cuda")
+    assert B.vec_add(z, z).numel() == 0
+    assert O.rope_embed(np.zeros(0), 3, 8).size == 0 and O.vec_add([], []).size == 0
+
+
 def test_bad_arguments_are_errors(B):
     from vortex_b200 import _native as N
     from vortex_b200.quant import _dptr, _stream_ptr, context

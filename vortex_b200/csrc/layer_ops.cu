@@ -565,20 +565,25 @@ static int rope_rows(vxb_ctx *ctx, const float *d_x, int rows, int n, const int6
 
 VXB_API int vxb_rope(vxb_ctx *ctx, const float *d_x, int rows, int n, const int64_t *d_pos, int dim, float *d_out,
                      void *stream) {
-  if (!ctx || !d_x || !d_pos || !d_out || rows <= 0 || n <= 0 || dim <= 0)
-    return set_error(ctx, VXB_EINVAL, "vxb_rope: bad arguments");
+  if (!ctx || rows < 0 || n < 0 || dim <= 0) return set_error(ctx, VXB_EINVAL, "vxb_rope: bad arguments");
+  if (rows == 0 || n == 0) return VXB_OK;  // an empty input rotates to an empty output
+  if (!d_x || !d_pos || !d_out) return set_error(ctx, VXB_EINVAL, "vxb_rope: null pointer");
   return rope_rows(ctx, d_x, rows, n, d_pos, dim, 0, nullptr, 0, d_out, (cudaStream_t)stream);
 }
 
 VXB_API int vxb_rope_angles(vxb_ctx *ctx, const float *d_x, int rows, int n, const double *d_angles, int n_angles,
                             float *d_out, void *stream) {
-  if (!ctx || !d_x || !d_out || rows <= 0 || n <= 0 || n_angles < 0 || (n_angles > 0 && !d_angles))
+  if (!ctx || rows < 0 || n < 0 || n_angles < 0 || (n_angles > 0 && !d_angles))
     return set_error(ctx, VXB_EINVAL, "vxb_rope_angles: bad arguments");
+  if (rows == 0 || n == 0) return VXB_OK;
+  if (!d_x || !d_out) return set_error(ctx, VXB_EINVAL, "vxb_rope_angles: null pointer");
   return rope_rows(ctx, d_x, rows, n, nullptr, 1, 1, d_angles, n_angles, d_out, (cudaStream_t)stream);
 }
 
 VXB_API int vxb_add(vxb_ctx *ctx, const float *d_a, const float *d_b, size_t n, float *d_out, void *stream) {
-  if (!ctx || !d_a || !d_b || !d_out || n == 0) return set_error(ctx, VXB_EINVAL, "vxb_add: bad arguments");
+  if (!ctx) return set_error(ctx, VXB_EINVAL, "vxb_add: bad arguments");
+  if (n == 0) return VXB_OK;  // _vec_add of two empty vectors is empty
+  if (!d_a || !d_b || !d_out) return set_error(ctx, VXB_EINVAL, "vxb_add: null pointer");
   if (int rc = use_device(ctx)) return rc;
   const size_t cap = (size_t)(ctx->num_sms > 0 ? ctx->num_sms : 148) * 8;
   const unsigned grid = (unsigned)std::max<size_t>(1, std::min((n / 4 + 255) / 256, cap));
